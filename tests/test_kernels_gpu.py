@@ -1,0 +1,285 @@
+"""Parity of the sm_100a dequant-matmul kernels against the oracle (GPU).
+
+Every case computes the same packed weights two ways: the CUDA kernel through
+the drop-in ops / C ABI, and the numpy oracle (dequantize, fp32 matmul, fp16).
+Tolerances:
+  * bit-exact for dequantized weights (lw_dequant_*) and one-hot probes;
+  * outputs: max-abs error <= 1e-2 * ||ref[m, :]||_2 / sqrt(N) per row (the
+    row-scaled bound), and also the reference's own allclose (atol 1e-2 /
+    rtol 1e-3 for fp16 and INT8, 0.05 / 1e-2 for INT4; tests/test_kernels.py).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    from liteweight_b200 import build
+    build.build()
+
+
+def kern():
+    from liteweight_b200 import kernels
+    return kernels
+
+
+def check_rows(got: torch.Tensor, ref: np.ndarray, what: str):
+    g = got.float().cpu().numpy()
+    r = ref.astype(np.float32)
+    assert g.shape == r.shape, (g.shape, r.shape)
+    assert np.isfinite(g).all(), what
+    tol = oq.row_tolerance(r)
+    err = np.abs(g - r)
+    ratio = (err / np.maximum(tol, 1e-12)).max()
+    assert np.all(err <= tol), f"{what}: max err {err.max():.4g}, worst err/tol {ratio:.3f}"
+    return ratio
+
+
+def quantized(N, K, G, bits, seed, scale=0.02):
+    g = torch.Generator().manual_seed(seed)
+    W = (torch.randn(N, K, generator=g) * scale).half()
+    if bits == 8:
+        return oq.quantize_int8(W.numpy(), G)
+    return oq.quantize_int4(W.numpy(), G)
+
+
+def run_quant(act_np, q, s, G, bits):
+    k = kern()
+    act = torch.from_numpy(act_np).to(DEV)
+    qt, st = torch.from_numpy(q).to(DEV), torch.from_numpy(s).to(DEV)
+    return (k.matmul_int8 if bits == 8 else k.matmul_int4)(act, qt, st, group_size=G)
+
+
+# ------------------------------------------------ the reference's kernel tests
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 8192), (4, 2048, 8192), (16, 2048, 2048), (128, 512, 512)])
+def test_fp16_close_to_torch(M, K, N):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, dtype=torch.float16, device=DEV)
+    b = torch.randn(K, N, dtype=torch.float16, device=DEV)
+    got = kern().matmul_fp16(a, b)
+    ref = (a.float().cpu().numpy() @ b.float().cpu().numpy()).astype(np.float16)
+    assert got.shape == (M, N) and got.dtype == torch.float16
+    assert torch.allclose(got.cpu(), torch.from_numpy(ref), atol=1e-2, rtol=1e-3)
+    check_rows(got, ref, "fp16 kn")
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 8192), (4, 2048, 8192), (16, 2048, 2048), (3, 70, 130)])
+def test_fp16_transposed_weight(M, K, N):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, dtype=torch.float16, device=DEV)
+    w = torch.randn(N, K, dtype=torch.float16, device=DEV)
+    got = kern().matmul_fp16(a, w.T)
+    ref = (a.float().cpu().numpy() @ w.float().cpu().numpy().T).astype(np.float16)
+    assert torch.allclose(got.cpu(), torch.from_numpy(ref), atol=1e-2, rtol=1e-3)
+
+
+def test_fp16_non_tile_multiple_shape():
+    a = torch.randn(3, 70, dtype=torch.float16, device=DEV)
+    b = torch.randn(70, 130, dtype=torch.float16, device=DEV)
+    got = kern().matmul_fp16(a, b)
+    ref = torch.from_numpy((a.float().cpu().numpy() @ b.float().cpu().numpy()).astype(np.float16))
+    assert torch.allclose(got.cpu(), ref, atol=1e-2)
+
+
+@pytest.mark.parametrize("M,K,N,G", [(1, 2048, 8192, 128), (4, 2048, 8192, 128), (16, 2048, 2048, 128),
+                                     (1, 2048, 8192, 2048)])
+def test_int8_matches_oracle(M, K, N, G):
+    torch.manual_seed(1)
+    act = torch.randn(M, K, dtype=torch.float16)
+    W = torch.randn(N, K, dtype=torch.float16)
+    q, s = oq.quantize_int8(W.numpy(), G)
+    got = run_quant(act.numpy(), q, s, G, 8)
+    oracle = oq.fakequant_matmul(act.numpy(), W.numpy(), G)
+    assert got.shape == (M, N) and got.dtype == torch.float16
+    assert torch.allclose(got.cpu(), torch.from_numpy(oracle), atol=1e-2, rtol=1e-3)
+    check_rows(got, oracle, f"int8 {M}x{K}x{N} G{G}")
+
+
+def test_int8_no_nan():
+    act = torch.randn(1, 256, dtype=torch.float16)
+    W = torch.randn(64, 256, dtype=torch.float16)
+    q, s = oq.quantize_int8(W.numpy(), 128)
+    out = run_quant(act.numpy(), q, s, 128, 8)
+    assert not out.isnan().any() and not out.isinf().any()
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 8192), (4, 2048, 8192), (16, 2048, 2048)])
+def test_int4_matches_oracle(M, K, N):
+    torch.manual_seed(2)
+    act = torch.randn(M, K, dtype=torch.float16)
+    W = torch.randn(N, K, dtype=torch.float16)
+    q, s = oq.quantize_int4(W.numpy(), 128)
+    got = run_quant(act.numpy(), q, s, 128, 4)
+    oracle = oq.fakequant_matmul_int4(act.numpy(), W.numpy(), 128)
+    assert torch.allclose(got.cpu(), torch.from_numpy(oracle), atol=0.05, rtol=1e-2)
+    check_rows(got, oracle, f"int4 {M}x{K}x{N}")
+
+
+# ------------------------------------------------ golden vectors from the reference
+
+def test_golden_fakequant_outputs(golden_dir):
+    qg = dict(np.load(golden_dir / "quant_golden.npz"))
+    names = sorted({k.split("/")[0] for k in qg if k.endswith("/act")})
+    assert names
+    for name in names:
+        act, G = qg[f"{name}/act"], int(qg[f"{name}/G"])
+        for bits in (8, 4):
+            got = run_quant(act, qg[f"{name}/q{bits}"], qg[f"{name}/s{bits}"], G, bits)
+            ref = qg[f"{name}/out{bits}"]
+            atol, rtol = (1e-2, 1e-3) if bits == 8 else (0.05, 1e-2)
+            assert torch.allclose(got.cpu(), torch.from_numpy(ref), atol=atol, rtol=rtol), name
+            check_rows(got, ref, f"{name} int{bits}")
+
+
+def test_dequant_kernels_bit_exact(golden_dir):
+    from liteweight_b200.quantize import dequantize_int4, dequantize_int8
+    qg = dict(np.load(golden_dir / "quant_golden.npz"))
+    d4 = dequantize_int4(torch.from_numpy(qg["codes4/q"]).to(DEV), torch.from_numpy(qg["codes4/s"]).to(DEV), 128)
+    assert np.array_equal(d4.cpu().numpy().view(np.uint16), qg["codes4/dq"].view(np.uint16))
+    d8 = dequantize_int8(torch.from_numpy(qg["codes8/q"]).to(DEV), torch.from_numpy(qg["codes8/s"]).to(DEV), 128)
+    assert np.array_equal(d8.cpu().numpy().view(np.uint16), qg["codes8/dq"].view(np.uint16))
+    for name in ("tq_64x256", "tq_32x512", "ties_i8", "group_axis"):
+        G = int(qg[f"{name}/G"])
+        d8 = dequantize_int8(torch.from_numpy(qg[f"{name}/q8"]).to(DEV), torch.from_numpy(qg[f"{name}/s8"]).to(DEV), G)
+        assert np.array_equal(d8.cpu().numpy().view(np.uint16), qg[f"{name}/dq8"].view(np.uint16)), name
+        d4 = dequantize_int4(torch.from_numpy(qg[f"{name}/q4"]).to(DEV), torch.from_numpy(qg[f"{name}/s4"]).to(DEV), G)
+        assert np.array_equal(d4.cpu().numpy().view(np.uint16), qg[f"{name}/dq4"].view(np.uint16)), name
+
+
+def test_every_code_through_the_gemv():
+    """All 16 nibble codes (incl. -8) and all 256 int8 codes (incl. -128) through the
+    fast path: one-hot activation rows select single weight columns, so the output
+    must equal the dequantized weight bit for bit."""
+    g = np.random.default_rng(5)
+    N, K = 32, 256
+    q4 = g.integers(0, 256, (N, K // 2), dtype=np.uint8)
+    q8 = g.integers(-128, 128, (N, K), dtype=np.int8)
+    s = (g.random((N, K // 128)) * 0.05 + 1e-3).astype(np.float16)
+    for bits, q in ((4, q4), (8, q8)):
+        w = oq.dequantize_int4(q, s, 128) if bits == 4 else oq.dequantize_int8(q, s, 128)
+        for k0 in range(0, K, 32):
+            act = np.eye(K, dtype=np.float16)[k0:k0 + 32]
+            got = run_quant(act, q, s, 128, bits).cpu().numpy()
+            assert np.array_equal(got.view(np.uint16), w[:, k0:k0 + 32].T.copy().view(np.uint16)), (bits, k0)
+
+
+# ------------------------------------------------ config-2 sweep (Llama-3.2-1B shapes)
+
+SWEEP_KN = [(2048, 2048), (2048, 512), (2048, 8192), (8192, 2048)]
+SWEEP_M = [1, 2, 4, 8, 16, 32, 64, 128, 256]
+_cache = {}
+
+
+def sweep_weights(K, N, bits):
+    key = (K, N, bits)
+    if key not in _cache:
+        q, s = quantized(N, K, 128, bits, seed=K * 7 + N + bits)
+        w = (oq.dequantize_int4 if bits == 4 else oq.dequantize_int8)(q, s, 128).astype(np.float32)
+        _cache[key] = (w, torch.from_numpy(q).to(DEV), torch.from_numpy(s).to(DEV))
+    return _cache[key]
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("K,N", SWEEP_KN)
+def test_sweep_parity(bits, K, N):
+    w, qt, st = sweep_weights(K, N, bits)
+    k = kern()
+    fn = k.matmul_int4 if bits == 4 else k.matmul_int8
+    rng = np.random.default_rng(K + N)
+    for M in SWEEP_M:
+        act = rng.standard_normal((M, K)).astype(np.float16)
+        ref = (act.astype(np.float32) @ w.T).astype(np.float16)
+        got = fn(torch.from_numpy(act).to(DEV), qt, st, group_size=128)
+        check_rows(got, ref, f"int{bits} M={M} K={K} N={N}")
+
+
+# ------------------------------------------------ edge cases
+
+@pytest.mark.parametrize("bits,M,K,N,G", [
+    (4, 1, 192, 40, 64),      # K tail inside a chunk, N not a multiple of 16
+    (4, 3, 2048, 17, 128),    # ragged N
+    (8, 5, 48, 24, 16),       # tiny K, G = 16
+    (8, 2, 320, 33, 8),       # G below the 16-element piece -> generic path
+    (4, 2, 70, 10, 35),       # odd group -> generic path
+    (8, 40, 1024, 96, 128),   # M above one launch block (M blocking)
+    (4, 33, 4096, 64, 4096),  # per-output-channel INT4, M = 33
+    (8, 9, 8192, 48, 128),    # two n8 batch tiles
+])
+def test_edge_shapes(bits, M, K, N, G):
+    q, s = quantized(N, K, G, bits, seed=M * 1000 + N)
+    act = np.random.default_rng(M + K).standard_normal((M, K)).astype(np.float16)
+    got = run_quant(act, q, s, G, bits)
+    ref = oq.packed_matmul(act, q, s, G, bits)
+    check_rows(got, ref, f"int{bits} {M}x{K}x{N} G{G}")
+
+
+def test_empty_m():
+    q, s = quantized(16, 256, 128, 8, seed=1)
+    out = run_quant(np.zeros((0, 256), np.float16), q, s, 128, 8)
+    assert out.shape == (0, 16)
+
+
+def test_non_contiguous_activation():
+    q, s = quantized(64, 512, 128, 4, seed=3)
+    big = torch.randn(4, 1024, dtype=torch.float16, device=DEV)
+    act = big[:, ::2]
+    got = kern().matmul_int4(act, torch.from_numpy(q).to(DEV), torch.from_numpy(s).to(DEV), group_size=128)
+    ref = oq.packed_matmul(act.cpu().numpy(), q, s, 128, 4)
+    check_rows(got, ref, "strided act")
+
+
+def test_assertions_like_reference():
+    k = kern()
+    q, s = quantized(16, 256, 128, 8, seed=1)
+    act = torch.zeros(1, 256, dtype=torch.float32, device=DEV)
+    with pytest.raises(AssertionError):
+        k.matmul_int8(act, torch.from_numpy(q).to(DEV), torch.from_numpy(s).to(DEV))
+    with pytest.raises(AssertionError):
+        k.matmul_int4(act.half(), torch.from_numpy(q).to(DEV), torch.from_numpy(s).to(DEV))
+
+
+def test_quantlinear_bias_and_shape():
+    from liteweight_b200.quantlinear import QuantLinear
+    torch.manual_seed(4)
+    lin = torch.nn.Linear(256, 96, bias=True).half()
+    for bits in (8, 4):
+        ql = QuantLinear.from_linear(lin, group_size=128, bits=bits).to(DEV)
+        x = torch.randn(2, 3, 256, dtype=torch.float16, device=DEV)
+        y = ql(x)
+        assert y.shape == (2, 3, 96)
+        q, s = ql.qweight.cpu().numpy(), ql.scales.cpu().numpy()
+        ref = oq.packed_matmul(x.reshape(-1, 256).cpu().numpy(), q, s, 128, bits)
+        ref = (ref.astype(np.float32) + ql.bias.cpu().numpy().astype(np.float32)).astype(np.float16)
+        check_rows(y.reshape(-1, 96), ref, f"QuantLinear bits={bits}")
+
+
+def test_deterministic_and_graph_capturable():
+    q, s = quantized(2048, 2048, 128, 4, seed=9)
+    qt, st = torch.from_numpy(q).to(DEV), torch.from_numpy(s).to(DEV)
+    act = torch.randn(4, 2048, dtype=torch.float16, device=DEV)
+    k = kern()
+    a = k.matmul_int4(act, qt, st)
+    b = k.matmul_int4(act, qt, st)
+    assert torch.equal(a, b)
+    out = [None]
+    g = torch.cuda.CUDAGraph()
+    s_ = torch.cuda.Stream()
+    with torch.cuda.stream(s_):
+        k.matmul_int4(act, qt, st)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s_):
+            out[0] = k.matmul_int4(act, qt, st)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out[0], a)
