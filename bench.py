@@ -167,6 +167,35 @@ def gemv_bytes(M: int, K: int, N: int, bits: int) -> int:
     return quant_matmul_workload(M, K, N, bits, GROUP).bytes_moved
 
 
+def capture_graph(fn):
+    """CUDA graph of fn() captured on a side stream (after one eager warm-up there)."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(g, reps: int) -> float:
+    """Average ms of one replay, CUDA events on the launching stream."""
+    import torch
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
 class GemvWorkload:
     name = "gemv"
     metric = "dequant-GEMV HBM GB/s (M=1, Llama-3.2-1B linear shapes, INT4+INT8 G128)"
@@ -178,12 +207,9 @@ class GemvWorkload:
         self.torch, self.nat, self.dev = torch, nat, device
         self.M = 1
         gen = torch.Generator(device=device).manual_seed(seed)
-        # weight copies: enough that one rotation exceeds 2x L2
-        self.items = []     # (bits, K, N)
-        for bits in (4, 8):
-            for K, N in GEMV_SHAPES:
-                self.items.append((bits, K, N))
+        self.items = [(bits, K, N) for bits in (4, 8) for K, N in GEMV_SHAPES]   # (bits, K, N)
         step_w = sum(N * K * b // 8 for b, K, N in self.items)
+        # weight copies: one rotation is more than twice the L2
         self.R = max(3, -(-2 * L2_BYTES // step_w))
         self.weights = []   # [copy][item] -> (q, s)
         for _ in range(self.R):
@@ -196,42 +222,47 @@ class GemvWorkload:
                 s = (torch.rand(N, K // GROUP, device=device, generator=gen) * 2e-3 + 1e-4).half()
                 per.append((q, s))
             self.weights.append(per)
-        self.acts = {K: torch.randn(self.M, K, dtype=torch.float16, device=device, generator=gen)
+        self.acts = {K: torch.randn(256, K, dtype=torch.float16, device=device, generator=gen)
                      for K in {K for _, K, _ in self.items}}
-        self.outs = [torch.empty(self.M, N, dtype=torch.float16, device=device) for _, _, N in self.items]
+        self.outs = {N: torch.empty(256, N, dtype=torch.float16, device=device)
+                     for N in {N for _, _, N in self.items}}
         self.bytes_per_step = sum(gemv_bytes(self.M, K, N, b) for b, K, N in self.items)
-        self.launch_events = None
+        n0 = nat.launch_count()
+        self.step_graphs = [capture_graph(lambda r=r: self._step(r)) for r in range(self.R)]
+        # capture_graph runs fn twice (eager warm-up + capture): launches of one step
+        self.launches_per_step = (nat.launch_count() - n0) // (2 * self.R)
 
-    def _call(self, i: int, copy: int, act, out):
+    def _call(self, i: int, copy: int, M: int):
         bits, K, N = self.items[i]
         q, s = self.weights[copy][i]
+        act, out = self.acts[K], self.outs[N]
+        stream = self.torch.cuda.current_stream().cuda_stream
+        ws, ws_bytes = self.nat.matmul_workspace(bits, M, N, K, self.dev, stream)
         fn = "lw_gemm_w4a16" if bits == 4 else "lw_gemm_w8a16"
-        self.nat.call(fn, act.data_ptr(), q.data_ptr(), s.data_ptr(), None, out.data_ptr(), act.shape[0], N, K,
-                      GROUP, self.torch.cuda.current_stream().cuda_stream)
+        self.nat.call(fn, act.data_ptr(), q.data_ptr(), s.data_ptr(), None, out.data_ptr(), M, N, K, GROUP,
+                      ws, ws_bytes, stream)
 
-    def step(self, it: int, record: bool = False):
-        copy = it % self.R
-        for i, (bits, K, N) in enumerate(self.items):
-            if record:
-                e0 = self.torch.cuda.Event(enable_timing=True)
-                e1 = self.torch.cuda.Event(enable_timing=True)
-                e0.record()
-                self._call(i, copy, self.acts[K], self.outs[i])
-                e1.record()
-                self.launch_events.append((i, e0, e1))
-            else:
-                self._call(i, copy, self.acts[K], self.outs[i])
+    def _step(self, copy: int):
+        for i in range(len(self.items)):
+            self._call(i, copy, self.M)
 
-    def kernel_stats(self, steps: int):
-        """Per kernel family (bits): algorithmic bytes and summed launch time."""
+    def step(self, it: int):
+        self.step_graphs[it % self.R].replay()
+
+    def kernel_stats(self) -> dict:
+        """Per kernel family: algorithmic bytes and device time of its launches in
+        one step, each launch timed in a graph of R back-to-back launches over the
+        rotating weight copies (CUDA events around the replays)."""
         fam = {}
-        for i, e0, e1 in self.launch_events:
-            bits, K, N = self.items[i]
-            key = f"gemv_w{bits}a16"
-            d = fam.setdefault(key, {"bytes": 0, "ms": 0.0, "launches": 0})
+        for i, (bits, K, N) in enumerate(self.items):
+            g = capture_graph(lambda i=i: [self._call(i, r, self.M) for r in range(self.R)])
+            ms = time_graph(g, 20) / self.R
+            d = fam.setdefault(f"gemv_w{bits}a16", {"bytes": 0, "ms": 0.0, "launches": 0, "shapes": {}})
             d["bytes"] += gemv_bytes(self.M, K, N, bits)
-            d["ms"] += e0.elapsed_time(e1)
+            d["ms"] += ms
             d["launches"] += 1
+            d["shapes"][f"{K}x{N}"] = {"us": round(ms * 1e3, 3),
+                                       "GB/s": round(gemv_bytes(self.M, K, N, bits) / (ms * 1e-3) / 1e9, 1)}
         return fam
 
     def e2e(self, steps: int) -> dict:
@@ -239,8 +270,8 @@ class GemvWorkload:
         activation copied in and the result copied out every call."""
         torch = self.torch
         from liteweight_b200 import kernels
-        host_act = {K: a.cpu().pin_memory() for K, a in self.acts.items()}
-        host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in self.outs]
+        host_act = {K: a[:self.M].cpu().pin_memory() for K, a in self.acts.items()}
+        host_out = [torch.empty(self.M, N, dtype=torch.float16).pin_memory() for _, _, N in self.items]
         h2d = sum(self.M * K * 2 for _, K, _ in self.items)
         d2h = sum(self.M * N * 2 for _, _, N in self.items)
 
@@ -263,31 +294,19 @@ class GemvWorkload:
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / steps
         return {"value": round(self.bytes_per_step / (ms * 1e-3) / 1e9, 2), "unit": self.unit,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4)}
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
+                "path": "liteweight_b200.kernels.matmul_int4/int8 per call (ctypes), pinned host in/out"}
 
     def sweep(self) -> dict:
-        """GB/s of one launch vs M for both bit widths (the 'vs M' curve)."""
-        torch = self.torch
+        """Algorithmic GB/s vs M for both bit widths over the four shapes (graph-timed)."""
         out = {}
         for bits in (4, 8):
             for M in (1, 2, 4, 8, 16, 32, 64, 128, 256):
-                tot_b, tot_ms = 0, 0.0
-                for K, N in GEMV_SHAPES:
-                    i = self.items.index((bits, K, N))
-                    act = torch.randn(M, K, dtype=torch.float16, device=self.dev)
-                    o = torch.empty(M, N, dtype=torch.float16, device=self.dev)
-                    reps = 2 * self.R
-                    for r in range(self.R):
-                        self._call(i, r, act, o)
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    for r in range(reps):
-                        self._call(i, r % self.R, act, o)
-                    e1.record()
-                    torch.cuda.synchronize()
-                    tot_ms += e0.elapsed_time(e1) / reps
-                    tot_b += gemv_bytes(M, K, N, bits)
-                out[f"w{bits}_M{M}"] = round(tot_b / (tot_ms * 1e-3) / 1e9, 1)
+                idx = [self.items.index((bits, K, N)) for K, N in GEMV_SHAPES]
+                g = capture_graph(lambda: [self._call(i, r, M) for r in range(self.R) for i in idx])
+                ms = time_graph(g, 5) / self.R
+                tot_b = sum(gemv_bytes(M, K, N, bits) for K, N in GEMV_SHAPES)
+                out[f"w{bits}_M{M}"] = round(tot_b / (ms * 1e-3) / 1e9, 1)
         return out
 
 
@@ -398,22 +417,20 @@ def run_ours(args, dist: Dist):
     torch.cuda.synchronize()
     dist.barrier(dev)
     torch.cuda.synchronize()
-    wl.launch_events = []
-    n0 = nat.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(smi_gpu_id(dist.local_rank)) as clk:
         e0.record()
         for it in range(args.steps):
-            wl.step(args.warmup + it, record=True)
+            wl.step(args.warmup + it)
         e1.record()
         torch.cuda.synchronize()
-    launches = nat.launch_count() - n0
+    launches = args.steps * wl.launches_per_step   # kernels inside the replayed step graphs
     dist.barrier(dev)
     ms = e0.elapsed_time(e1)
     ms_max = dist.max(ms, dev)
     total_bytes = dist.sum(wl.bytes_per_step * args.steps, dev)
     value = total_bytes / (ms_max * 1e-3) / 1e9
-    fam = wl.kernel_stats(args.steps)
+    fam = wl.kernel_stats()
     e2e = wl.e2e(max(10, args.steps))
     sweep = wl.sweep() if (dist.world == 1 and not args.no_sweep) else None
     peak, peak_src = b200_measured(ROOT / "MEASURED_PEAKS.json")
@@ -441,7 +458,8 @@ def run_ours(args, dist: Dist):
                        "l2": f"rotating {wl.R} weight copies ({wl.R * sum(N * K * b // 8 for b, K, N in wl.items) >> 20}"
                              " MiB) > L2"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
-            "kernels": {k: {"launches": v["launches"], "GB/s": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1)}
+            "kernels": {k: {"launches_per_step": v["launches"],
+                            "GB/s": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1), "shapes": v["shapes"]}
                         for k, v in fam.items()},
             "clocks": clocks}
     if sweep is not None:

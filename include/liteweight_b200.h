@@ -63,17 +63,33 @@ unsigned long long lw_launch_count(void);
  *   bias fp16 [N] or NULL, out fp16 [M,N].
  * lw_gemm_w4a16 replaces kernels/matmul_int4.py:122-165:
  *   qweight uint8 [N,K/2] (even k in the low nibble), K even.
+ *
+ * workspace (optional; may be NULL with workspace_bytes = 0): device scratch
+ * of at least lw_gemm_workspace_size() bytes, 256-byte aligned, ZEROED before
+ * its first use; every completed call leaves it zeroed again. With it, a
+ * weight tile may be split between warps (better balance for small N); the
+ * partial sums are combined in a fixed order, so results are deterministic
+ * for a given shape and device. Calls that run concurrently (different
+ * streams) must not share a workspace.
  */
 int lw_gemm_w8a16(const void* act, const void* qweight, const void* scales, const void* bias,
-                  void* out, int M, int N, int K, int group_size, lw_stream_t stream);
+                  void* out, int M, int N, int K, int group_size, void* workspace,
+                  size_t workspace_bytes, lw_stream_t stream);
 int lw_gemm_w4a16(const void* act, const void* qweight, const void* scales, const void* bias,
-                  void* out, int M, int N, int K, int group_size, lw_stream_t stream);
+                  void* out, int M, int N, int K, int group_size, void* workspace,
+                  size_t workspace_bytes, lw_stream_t stream);
+
+/* Workspace bytes the matmul entry points can use for these sizes (bits = 4,
+ * 8 or 16); 0 when no tile is split. Needs a current CUDA device. No
+ * counterpart in the reference (its Triton kernels need no scratch). */
+size_t lw_gemm_workspace_size(int bits, int M, int N, int K);
 
 /* fp16 matmul with the weight in nn.Linear layout: out[M,N] = a[M,K] @ w[N,K]^T.
  * Replaces kernels/matmul_fp16.py:67-85 when `b` is the transpose of a
  * contiguous [N,K] tensor (how bench/benchmark.py:133 calls it: `W.T`), and
  * is the engine's un-quantized lm_head. */
-int lw_gemm_f16(const void* a, const void* w, void* out, int M, int N, int K, lw_stream_t stream);
+int lw_gemm_f16(const void* a, const void* w, void* out, int M, int N, int K, void* workspace,
+                size_t workspace_bytes, lw_stream_t stream);
 
 /* fp16 matmul with a row-major b[K,N]: replaces kernels/matmul_fp16.py:67-85
  * for a contiguous b. */

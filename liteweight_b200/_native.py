@@ -25,14 +25,16 @@ _SIGNATURES: dict[str, list] = {
     "lw_status_string": [c_int],
     "lw_abi_version": [],
     "lw_launch_count": [],
-    "lw_gemm_w8a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p],
-    "lw_gemm_w4a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p],
-    "lw_gemm_f16": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
+    "lw_gemm_workspace_size": [c_int] * 4,
+    "lw_gemm_w8a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p, ctypes.c_size_t, c_void_p],
+    "lw_gemm_w4a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p, ctypes.c_size_t, c_void_p],
+    "lw_gemm_f16": [c_void_p] * 3 + [c_int] * 3 + [c_void_p, ctypes.c_size_t, c_void_p],
     "lw_gemm_f16_kn": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
     "lw_dequant_w8": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
     "lw_dequant_w4": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
 }
-_RESTYPE = {"lw_status_string": ctypes.c_char_p, "lw_launch_count": ctypes.c_ulonglong}
+_RESTYPE = {"lw_status_string": ctypes.c_char_p, "lw_launch_count": ctypes.c_ulonglong,
+            "lw_gemm_workspace_size": ctypes.c_size_t}
 
 
 class LiteweightError(RuntimeError):
@@ -96,6 +98,30 @@ def call(fn: str, *args) -> None:
 def launch_count() -> int:
     """Kernels the library has enqueued so far (its own counter)."""
     return int(lib().lw_launch_count())
+
+
+_workspaces: dict = {}
+
+
+def workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """Zero-initialised scratch for the matmul entry points, one per (device,
+    stream) so concurrent streams never share it; grown on demand. The kernels
+    leave it zeroed after every call."""
+    key = (device.index, stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def matmul_workspace(bits: int, M: int, N: int, K: int, device: torch.device, stream: int) -> tuple[int, int]:
+    """(pointer, bytes) of a workspace large enough for this matmul."""
+    need = int(lib().lw_gemm_workspace_size(bits, M, N, K))
+    if need == 0:
+        return 0, 0
+    ws = workspace(device, stream, need)
+    return ws.data_ptr(), ws.numel()
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

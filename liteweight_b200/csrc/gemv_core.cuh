@@ -1,0 +1,458 @@
+// Persistent stream-K dequant GEMV core for B200 (sm_100a), shared by the
+// plain matmul entry points and the fused decode-step kernels.
+//
+// out[m, n] = sum_k act[m, k] * W[n, k], W in liteweight's INT8 / packed INT4
+// format (or fp16), each weight dequantized exactly as
+// liteweight/quantize.py:30-43 / :102-128 do, fp32 accumulation, one fp16
+// rounding (liteweight/quantize.py:60).
+//
+// Work decomposition. The weight matrix is cut into 16-row tiles; each tile's
+// K extent is cut into chunks of 4 lanes x 16 bytes per row. The flattened
+// (tile, chunk) sequence is divided into equal contiguous runs, one per warp
+// of a persistent grid, so every warp streams the same number of bytes. A
+// warp streams its run with a two-deep register double buffer (the loads of
+// the next batch are in flight while the current one is dequantized and fed
+// to the tensor core), so each SM keeps tens of KB of weight loads
+// outstanding all the time. A tile that lies inside one warp's run is
+// finished by that warp directly; a tile shared by several warps is combined
+// deterministically: each contributor writes its fp32 fragment to its own
+// slot of a scratch area and bumps the tile's counter; the last arriver sums
+// the slots in slot order, applies the epilogue and resets the counter.
+//
+// Inner loop (per warp, per 16-byte piece and row pair): the codes are
+// unpacked to exact fp16 integers with integer tricks, scaled with one fp16
+// multiply (bit-identical to the reference's fp32 product rounded to fp16),
+// and used directly from registers as the A operand of mma.sync.m16n8k16;
+// the activation, staged once per CTA in shared memory in the element order
+// the unpack produces, is the B operand; batch rows are the n8 columns.
+//
+// Prologues (activation staging): plain copy; RMSNorm of the residual stream
+// (modeling_llama.py:63-68 rounding points); residual update + RMSNorm for
+// tensor parallelism. Epilogues (per lane, rows g and g+8 of a tile are in
+// the same lane): plain (+bias, +residual), RoPE + KV-cache append for the
+// fused QKV projection, SwiGLU for the fused gate/up projection, raw fp32
+// partial sums (tensor-parallel row split), logits + argmax.
+#pragma once
+
+#include "lw_common.cuh"
+
+namespace lw {
+
+template <int BITS>
+struct WT;
+template <>
+struct WT<4> {
+  static constexpr int E = 32;  // elements per 16-byte piece
+};
+template <>
+struct WT<8> {
+  static constexpr int E = 16;
+};
+template <>
+struct WT<16> {
+  static constexpr int E = 8;
+};
+
+enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_RESID_NORM = 2 };
+enum { EPI_PLAIN = 0, EPI_ROPE_KV = 1, EPI_SWIGLU = 2, EPI_F32 = 3, EPI_ARGMAX = 4 };
+
+constexpr int kStreamThreads = 256;
+constexpr int kMaxM = 32;
+
+struct StreamParams {
+  // matmul
+  const __half* act;       // [M][lda]; the residual stream x for the norm prologues
+  const uint8_t* w;        // [N][K * BITS / 8]
+  const __half* scales;    // [N][K / G]
+  const __half* bias;      // [N] or null (EPI_PLAIN)
+  const __half* residual;  // [M][ldo] or null (EPI_PLAIN): out = residual + y
+  __half* out;             // [M][ldo]
+  int lda, ldo;
+  int M, N, K, G;
+  int kchunks;  // chunks per tile row
+  int tiles;    // ceil(N / 16)
+  int per;      // chunks per warp
+  int cp;       // staged activation row stride, halves
+  // prologue
+  const __half* gamma;     // [K] RMSNorm weight
+  float eps;
+  const float* psum;       // PRO_RESID_NORM: fp32 [M][K] to add to the residual
+  __half* x_out;           // PRO_RESID_NORM: updated residual, written by CTA 0
+  // epilogue
+  const __half* rope_cos;  // [max_seq][head_dim] fp16
+  const __half* rope_sin;
+  const int* pos;          // device: position written this step
+  int head_dim, n_q_heads, n_kv_heads, max_seq;
+  __half* q_out;           // [M][n_q_heads * head_dim]
+  __half* k_cache;         // [M][n_kv_heads][max_seq][head_dim] (this layer)
+  __half* v_cache;
+  float* out_f32;          // EPI_F32: [M][ldo]
+  unsigned long long* argmax_keys;  // EPI_ARGMAX: [M], zero before the launch
+  // split-tile combination (scratch)
+  float* slots;            // [tiles][max_slots][32 lanes][4 * MT]
+  int* counters;           // [tiles], zero before the first launch, left zero
+  int max_slots;
+};
+
+LW_DEV uint32_t bcast_h(const __half* p) {
+  const unsigned short s = __ldg(reinterpret_cast<const unsigned short*>(p));
+  return (uint32_t)s | ((uint32_t)s << 16);
+}
+
+template <int BITS, int MT>
+LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, uint32_t sa, uint32_t sb,
+                       const __half* arow, int cp, int g, int M) {
+  const uint32_t* a32 = reinterpret_cast<const uint32_t*>(&qa);
+  const uint32_t* b32 = reinterpret_cast<const uint32_t*>(&qb);
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  if constexpr (BITS == 4) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      uint32_t A[4], B[4];
+      dequant_int4_word(a32[w], A);
+      dequant_int4_word(b32[w], B);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        A[i] = hmul2_u32(A[i], sa);
+        B[i] = hmul2_u32(B[i], sb);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint4 av = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + w * 32) : z;
+        mma16816(acc[mt], A[0], B[0], A[1], B[1], av.x, av.y);
+        mma16816(acc[mt], A[2], B[2], A[3], B[3], av.z, av.w);
+      }
+    }
+  } else if constexpr (BITS == 8) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint4 av[MT];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) av[mt] = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + j * 32) : z;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t A[2], B[2];
+        dequant_int8_word(a32[2 * j + h], A);
+        dequant_int8_word(b32[2 * j + h], B);
+        A[0] = hmul2_u32(A[0], sa);
+        A[1] = hmul2_u32(A[1], sa);
+        B[0] = hmul2_u32(B[0], sb);
+        B[1] = hmul2_u32(B[1], sb);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          mma16816(acc[mt], A[0], B[0], A[1], B[1], h ? av[mt].z : av[mt].x, h ? av[mt].w : av[mt].y);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const uint4 av = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp) : z;
+      mma16816(acc[mt], qa.x, qb.x, qa.y, qb.y, av.x, av.y);
+      mma16816(acc[mt], qa.z, qb.z, qa.w, qb.w, av.z, av.w);
+    }
+  }
+}
+
+// Total order on fp16 values as unsigned keys (larger value -> larger key).
+LW_DEV uint32_t f16_order_key(__half h) {
+  const uint32_t u = __half_as_ushort(h);
+  return (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
+}
+
+LW_DEV float silu_f32(float x) { return x / (1.0f + expf(-x)); }
+
+// Epilogue for one tile: v[mt][i] holds D(row, col) with rows n_lo = 16*tile +
+// g (i = 0, 1) and n_hi = n_lo + 8 (i = 2, 3), cols m = 8*mt + 2t (+1 for odd i).
+template <int MT, int EPI>
+LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const int n_lo = tile * 16 + g, n_hi = n_lo + 8;
+  if constexpr (EPI == EPI_PLAIN || EPI == EPI_F32) {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int m = mt * 8 + 2 * t + (i & 1);
+        const int n = (i < 2) ? n_lo : n_hi;
+        if (m < p.M && n < p.N) {
+          if constexpr (EPI == EPI_F32) {
+            p.out_f32[(size_t)m * p.ldo + n] = v[mt][i];
+          } else {
+            float y = r16(v[mt][i]);
+            if (p.bias) y = r16(y + __half2float(p.bias[n]));
+            if (p.residual) y = r16(__half2float(p.residual[(size_t)m * p.ldo + n]) + y);
+            p.out[(size_t)m * p.ldo + n] = __float2half_rn(y);
+          }
+        }
+      }
+  } else if constexpr (EPI == EPI_ROPE_KV) {
+    // Rows of the fused q|k|v projection are stored so that tile rows g and
+    // g+8 are head dims d and d + hd/2 (the rotate_half partners).
+    const int hd = p.head_dim;
+    const int head = (tile * 16) / hd;
+    const int jt = tile % (hd / 16);
+    const int d_lo = 8 * jt + g, d_hi = d_lo + hd / 2;
+    const int pos = *p.pos;
+    const float c_lo = __half2float(p.rope_cos[(size_t)pos * hd + d_lo]);
+    const float c_hi = __half2float(p.rope_cos[(size_t)pos * hd + d_hi]);
+    const float s_lo = __half2float(p.rope_sin[(size_t)pos * hd + d_lo]);
+    const float s_hi = __half2float(p.rope_sin[(size_t)pos * hd + d_hi]);
+    const int nq = p.n_q_heads, nkv = p.n_kv_heads;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int m = mt * 8 + 2 * t + c;
+        if (m >= p.M || n_lo >= p.N) continue;
+        const float y_lo = r16(v[mt][c]), y_hi = r16(v[mt][2 + c]);
+        float o_lo = y_lo, o_hi = y_hi;
+        if (head < nq + nkv) {
+          // modeling_llama.py:161-162: q*cos + rotate_half(q)*sin, fp16 after each op
+          o_lo = r16(r16(y_lo * c_lo) + r16(-y_hi * s_lo));
+          o_hi = r16(r16(y_hi * c_hi) + r16(y_lo * s_hi));
+        }
+        __half* dst;
+        if (head < nq) {
+          dst = p.q_out + (size_t)m * nq * hd + (size_t)head * hd;
+        } else if (head < nq + nkv) {
+          dst = p.k_cache + (((size_t)m * nkv + (head - nq)) * p.max_seq + pos) * hd;
+        } else {
+          dst = p.v_cache + (((size_t)m * nkv + (head - nq - nkv)) * p.max_seq + pos) * hd;
+        }
+        dst[d_lo] = __float2half_rn(o_lo);
+        dst[d_hi] = __float2half_rn(o_hi);
+      }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // Tile rows g = gate row 8*tile + g, g+8 = the matching up row.
+    const int i_out = tile * 8 + g;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int m = mt * 8 + 2 * t + c;
+        if (m >= p.M || n_lo >= p.N) continue;
+        // modeling_llama.py:183: act_fn(gate) * up, fp16 after each op
+        const float gt = r16(v[mt][c]), up = r16(v[mt][2 + c]);
+        const float a = r16(silu_f32(gt));
+        p.out[(size_t)m * p.ldo + i_out] = __float2half_rn(a * up);
+      }
+  } else if constexpr (EPI == EPI_ARGMAX) {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int m = mt * 8 + 2 * t + c;
+        unsigned long long best = 0ull;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n = h ? n_hi : n_lo;
+          if (m < p.M && n < p.N) {
+            const __half y = __float2half_rn(v[mt][2 * h + c]);
+            p.out[(size_t)m * p.ldo + n] = y;
+            const unsigned long long key =
+                ((unsigned long long)f16_order_key(y) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+            best = key > best ? key : best;
+          }
+        }
+        // lanes with the same t share the column: reduce over g
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+          best = other > best ? other : best;
+        }
+        if (g == 0 && m < p.M && best) atomicMax(p.argmax_keys + m, best);
+      }
+  }
+}
+
+template <int BITS, int MT, int U, int PRO, int EPI>
+__global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const StreamParams p) {
+  constexpr int E = WT<BITS>::E;
+  constexpr int KC = 4 * E;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __half* act_s = reinterpret_cast<__half*>(smem);
+  __shared__ float ssq[kMaxM];
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int wid = blockIdx.x * (kStreamThreads / 32) + (tid >> 5);
+  const int C = p.kchunks;
+  const int total = p.tiles * C;
+  const int g0 = min(total, wid * p.per), g1 = min(total, g0 + p.per);
+  const size_t rowbytes = (size_t)p.K * BITS / 8;
+  const int npieces = (int)(rowbytes / 16);
+  const int ngroups = (BITS < 16) ? p.K / p.G : 1;
+
+  uint4 qa0[U], qb0[U], qa1[U], qb1[U];
+  uint32_t sa0[U], sb0[U], sa1[U], sb1[U];
+
+  auto load = [&](int gp, int n, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
+    const int tt = gp / C, c0 = gp - tt * C;
+    const int r0 = tt * 16 + g, r1 = r0 + 8;
+    const bool v0 = r0 < p.N, v1 = r1 < p.N;
+    const uint8_t* w0 = p.w + (size_t)(v0 ? r0 : 0) * rowbytes;
+    const uint8_t* w1 = p.w + (size_t)(v1 ? r1 : 0) * rowbytes;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int pc = (c0 + u) * 4 + t;
+      const bool ok = (u < n) && (pc < npieces);
+      qa[u] = (ok && v0) ? ldg_stream(w0 + (size_t)pc * 16) : make_uint4(0, 0, 0, 0);
+      qb[u] = (ok && v1) ? ldg_stream(w1 + (size_t)pc * 16) : make_uint4(0, 0, 0, 0);
+      if constexpr (BITS < 16) {
+        const int grp = ((c0 + u) * KC + t * E) / p.G;
+        sa[u] = (ok && v0) ? bcast_h(p.scales + (size_t)r0 * ngroups + grp) : 0u;
+        sb[u] = (ok && v1) ? bcast_h(p.scales + (size_t)r1 * ngroups + grp) : 0u;
+      } else {
+        sa[u] = sb[u] = 0u;
+      }
+    }
+  };
+  auto batch_len = [&](int gp) -> int {
+    if (gp >= g1) return 0;
+    const int c = gp % C;
+    return min(U, min(C - c, g1 - gp));
+  };
+
+  // Weights do not depend on the previous kernel: start both buffers first.
+  int gA = g0, nA = batch_len(gA);
+  if (nA) load(gA, nA, qa0, qb0, sa0, sb0);
+  int gB = gA + nA, nB = batch_len(gB);
+  if (nB) load(gB, nB, qa1, qb1, sa1, sb1);
+  int gnext = gB + nB;
+
+  pdl_wait();
+
+  // ---- stage the activation (M rows, K padded to the chunk) in lane order
+  {
+    const int groups8 = C * KC / 8;
+    if constexpr (PRO != PRO_PLAIN) {
+      if (tid < kMaxM) ssq[tid] = 0.f;
+      __syncthreads();
+    }
+    for (int i = tid; i < p.M * groups8; i += kStreamThreads) {
+      const int m = i / groups8, k = (i - m * groups8) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (k < p.K) {
+        v = ldg_nc(p.act + (size_t)m * p.lda + k);
+        if constexpr (PRO == PRO_RESID_NORM) {
+          // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
+          const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
+          const float ps[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+          __half* hv = reinterpret_cast<__half*>(&v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
+          if (blockIdx.x == 0) *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v;
+        }
+        if constexpr (PRO != PRO_PLAIN) {
+          const __half* hv = reinterpret_cast<const __half*>(&v);
+          float s = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float f = __half2float(hv[e]);
+            s = fmaf(f, f, s);
+          }
+          atomicAdd(&ssq[m], s);
+        }
+      }
+      if constexpr (BITS == 4) v = perm_int4_pairs(v);
+      const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
+      sts128(act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8, v);
+    }
+    if constexpr (PRO != PRO_PLAIN) {
+      __syncthreads();
+      // modeling_llama.py:65-68: h = weight * fp16(x * rsqrt(mean(x^2) + eps))
+      for (int i = tid; i < p.M * groups8; i += kStreamThreads) {
+        const int m = i / groups8, k = (i - m * groups8) * 8;
+        if (k >= p.K) continue;
+        const float rstd = 1.0f / sqrtf(ssq[m] / (float)p.K + p.eps);
+        const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
+        __half* dst = act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8;
+        uint4 v = lds128(dst);
+        uint4 gm = ldg_nc(p.gamma + k);
+        if constexpr (BITS == 4) gm = perm_int4_pairs(gm);
+        __half* hv = reinterpret_cast<__half*>(&v);
+        const __half* hg = reinterpret_cast<const __half*>(&gm);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          hv[e] = __float2half_rn(__half2float(hg[e]) * r16(__half2float(hv[e]) * rstd));
+        sts128(dst, v);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- stream the warp's run of (tile, chunk) work
+  float acc[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+  int seg = g0;  // start of the current tile segment
+  const __half* abase = act_s + (size_t)g * p.cp + t * 8;
+
+  auto flush = [&](int tile, int end) {
+    const bool whole = (seg == tile * C) && (end == (tile + 1) * C);
+    if (whole) {
+      finish_tile<MT, EPI>(p, tile, acc, lane);
+    } else {
+      const int first = (tile * C) / p.per;
+      const int last = ((tile + 1) * C - 1) / p.per;
+      const int slot = wid - first, nslot = last - first + 1;
+      float* base = p.slots + (size_t)tile * p.max_slots * 32 * 4 * MT;
+      float4* mine = reinterpret_cast<float4*>(base + ((size_t)slot * 32 + lane) * 4 * MT);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) mine[mt] = make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
+      __threadfence();
+      int old = 0;
+      if (lane == 0) old = atomicAdd(p.counters + tile, 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == nslot - 1) {
+        __threadfence();
+        float sum[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) sum[mt][0] = sum[mt][1] = sum[mt][2] = sum[mt][3] = 0.f;
+        for (int s = 0; s < nslot; ++s) {
+          const float4* src = reinterpret_cast<const float4*>(base + ((size_t)s * 32 + lane) * 4 * MT);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const float4 f = __ldcg(src + mt);
+            sum[mt][0] += f.x;
+            sum[mt][1] += f.y;
+            sum[mt][2] += f.z;
+            sum[mt][3] += f.w;
+          }
+        }
+        finish_tile<MT, EPI>(p, tile, sum, lane);
+        if (lane == 0) p.counters[tile] = 0;
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+    seg = end;
+  };
+
+  auto compute = [&](int gp, int n, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
+    const int tt = gp / C, c0 = gp - tt * C;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (u < n) gemv_piece<BITS, MT>(acc, qa[u], qb[u], sa[u], sb[u], abase + (c0 + u) * KC, p.cp, g, p.M);
+    const int end = gp + n;
+    if (end == (tt + 1) * C || end == g1) flush(tt, end);
+  };
+
+  while (nA) {
+    compute(gA, nA, qa0, qb0, sa0, sb0);
+    gA = gnext;
+    nA = batch_len(gA);
+    if (nA) load(gA, nA, qa0, qb0, sa0, sb0);
+    gnext = gA + nA;
+    if (!nB) break;
+    compute(gB, nB, qa1, qb1, sa1, sb1);
+    gB = gnext;
+    nB = batch_len(gB);
+    if (nB) load(gB, nB, qa1, qb1, sa1, sb1);
+    gnext = gB + nB;
+  }
+  pdl_launch_dependents();
+}
+
+}  // namespace lw

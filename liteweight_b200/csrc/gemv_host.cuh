@@ -1,0 +1,127 @@
+// Host-side planning and launch of the persistent stream-K GEMV kernel.
+#pragma once
+
+#include <algorithm>
+
+#include "gemv_core.cuh"
+
+namespace lw {
+
+constexpr int kStageBudget = 220 * 1024;   // dynamic shared memory for the staged activation
+constexpr int kBatch = 2;                  // 16-byte chunks per row per register buffer
+
+inline int device_sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct StreamPlan {
+  int tiles, kchunks, cp, per, grid, max_slots, mt;
+  size_t smem, ws_bytes;  // ws_bytes = 0 when no tile is split
+};
+
+inline int mt_for(int M) { return M <= 8 ? 1 : (M <= 16 ? 2 : 4); }
+
+// Largest activation row block one launch can stage.
+template <int BITS>
+int stage_rows(int K) {
+  constexpr int KC = 4 * WT<BITS>::E;
+  const int kpad = ((K + KC - 1) / KC) * KC;
+  return std::max(1, std::min(kMaxM, kStageBudget / (kpad * 2)));
+}
+
+template <int BITS, int MT, int PRO, int EPI>
+cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
+  constexpr int KC = 4 * WT<BITS>::E;
+  pl->mt = MT;
+  pl->tiles = (N + 15) / 16;
+  pl->kchunks = (K + KC - 1) / KC;
+  const int kpad = pl->kchunks * KC;
+  pl->cp = ((size_t)M * (kpad + 32) * 2 <= (size_t)kStageBudget) ? kpad + 32 : kpad;
+  pl->smem = (size_t)M * pl->cp * 2;
+  auto kern = gemv_stream_kernel<BITS, MT, kBatch, PRO, EPI>;
+  cudaError_t e = cudaSuccess;
+  if (pl->smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl->smem);
+  if (e != cudaSuccess) return e;
+  int occ = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kStreamThreads, pl->smem);
+  if (e != cudaSuccess) return e;
+  occ = std::max(1, occ);
+  const long long warps_max = (long long)device_sm_count() * occ * (kStreamThreads / 32);
+  const long long total = (long long)pl->tiles * pl->kchunks;
+  long long per = std::max<long long>(kBatch, (total + warps_max - 1) / warps_max);
+  if (!allow_split) per = (per + pl->kchunks - 1) / pl->kchunks * pl->kchunks;
+  pl->per = (int)per;
+  const long long warps = (total + per - 1) / per;
+  pl->grid = (int)((warps + kStreamThreads / 32 - 1) / (kStreamThreads / 32));
+  const bool split = (per % pl->kchunks) != 0;
+  pl->max_slots = split ? (pl->kchunks - 1) / pl->per + 2 : 0;
+  pl->ws_bytes = split ? align_up((size_t)pl->tiles * 4, 256) + (size_t)pl->tiles * pl->max_slots * 32 * 4 * MT * 4 : 0;
+  return cudaSuccess;
+}
+
+// Launch one row block (M <= 32). The workspace (counters first, zeroed before
+// first use, then slots) is used only when the plan splits tiles; without a
+// large enough workspace the plan keeps tiles whole.
+template <int BITS, int PRO, int EPI>
+cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl) {
+  StreamPlan pl;
+  cudaError_t e;
+  const int mt = mt_for(p.M);
+#define LW_PLAN(MT_)                                                                    \
+  e = plan_for<BITS, MT_, PRO, EPI>(p.M, p.N, p.K, true, &pl);                          \
+  if (e == cudaSuccess && pl.ws_bytes > ws_bytes)                                       \
+    e = plan_for<BITS, MT_, PRO, EPI>(p.M, p.N, p.K, false, &pl);
+  if (mt == 1) {
+    LW_PLAN(1)
+  } else if (mt == 2) {
+    LW_PLAN(2)
+  } else {
+    LW_PLAN(4)
+  }
+#undef LW_PLAN
+  if (e != cudaSuccess) return e;
+  p.tiles = pl.tiles;
+  p.kchunks = pl.kchunks;
+  p.cp = pl.cp;
+  p.per = pl.per;
+  p.max_slots = pl.max_slots;
+  if (pl.ws_bytes) {
+    p.counters = static_cast<int*>(ws);
+    p.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + align_up((size_t)pl.tiles * 4, 256));
+  } else {
+    p.counters = nullptr;
+    p.slots = nullptr;
+  }
+  dim3 grid(pl.grid), block(kStreamThreads);
+  if (mt == 1) return lw_launch(gemv_stream_kernel<BITS, 1, kBatch, PRO, EPI>, grid, block, pl.smem, s, pdl, p);
+  if (mt == 2) return lw_launch(gemv_stream_kernel<BITS, 2, kBatch, PRO, EPI>, grid, block, pl.smem, s, pdl, p);
+  return lw_launch(gemv_stream_kernel<BITS, 4, kBatch, PRO, EPI>, grid, block, pl.smem, s, pdl, p);
+}
+
+// Workspace bytes a launch of these sizes can use to split tiles.
+template <int BITS, int PRO, int EPI>
+size_t stream_workspace(int M, int N, int K) {
+  size_t need = 0;
+  const int rows = stage_rows<BITS>(K);
+  for (int m0 = 0; m0 < M; m0 += rows) {
+    const int mb = std::min(rows, M - m0);
+    StreamPlan pl;
+    cudaError_t e;
+    const int mt = mt_for(mb);
+    if (mt == 1)
+      e = plan_for<BITS, 1, PRO, EPI>(mb, N, K, true, &pl);
+    else if (mt == 2)
+      e = plan_for<BITS, 2, PRO, EPI>(mb, N, K, true, &pl);
+    else
+      e = plan_for<BITS, 4, PRO, EPI>(mb, N, K, true, &pl);
+    if (e == cudaSuccess) need = std::max(need, pl.ws_bytes);
+  }
+  return need;
+}
+
+}  // namespace lw

@@ -24,7 +24,8 @@ def matmul_fp16(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     s = nat.stream_of(a)
     if b.t().is_contiguous():
         # b = w.T with w [N, K] contiguous
-        nat.call("lw_gemm_f16", a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, s)
+        ws, ws_bytes = nat.matmul_workspace(16, M, N, K, a.device, s)
+        nat.call("lw_gemm_f16", a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, ws, ws_bytes, s)
     else:
         b = b.contiguous()
         nat.call("lw_gemm_f16_kn", a.data_ptr(), b.data_ptr(), c.data_ptr(), M, N, K, s)

@@ -36,6 +36,8 @@ def matmul_int4(act: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     out = torch.empty((M, N), device=act.device, dtype=torch.float16)
     if M == 0 or N == 0:
         return out
+    stream = nat.stream_of(act)
+    ws, ws_bytes = nat.matmul_workspace(4, M, N, K, act.device, stream)
     nat.call("lw_gemm_w4a16", act.data_ptr(), qweight.data_ptr(), scales.data_ptr(), None, out.data_ptr(),
-             M, N, K, group_size, nat.stream_of(act))
+             M, N, K, group_size, ws, ws_bytes, stream)
     return out

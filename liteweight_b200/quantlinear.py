@@ -51,8 +51,10 @@ class QuantLinear(nn.Module):
         out = torch.empty((m, self.out_features), dtype=torch.float16, device=x.device)
         if m:
             fn = "lw_gemm_w8a16" if self.bits == 8 else "lw_gemm_w4a16"
+            stream = nat.stream_of(x)
+            ws, ws_bytes = nat.matmul_workspace(self.bits, m, self.out_features, self.in_features, x.device, stream)
             nat.call(fn, x.data_ptr(), self.qweight.data_ptr(), self.scales.data_ptr(), nat.ptr(self.bias),
-                     out.data_ptr(), m, self.out_features, self.in_features, self.group_size, nat.stream_of(x))
+                     out.data_ptr(), m, self.out_features, self.in_features, self.group_size, ws, ws_bytes, stream)
         return out.reshape(*orig_shape[:-1], self.out_features)
 
     @classmethod

@@ -57,19 +57,21 @@ def test_version_and_status_strings(lib):
 def test_quant_gemm_argument_validation(lib, fn):
     f = getattr(lib, fn)
     fake = 0x1000   # never dereferenced: validation fails first
-    assert f(None, fake, fake, None, fake, 1, 64, 256, 128, None) == 1          # null act
-    assert f(fake, fake, fake, None, fake, 0, 64, 256, 128, None) == 2          # M = 0
-    assert f(fake, fake, fake, None, fake, 1, 64, 256, 100, None) == 3          # K % G
-    assert f(fake, fake, fake, None, fake, 1, 64, 256, 0, None) == 3            # G = 0
-    assert f(fake, fake, None, None, fake, 1, 64, 256, 128, None) == 1          # null scales
-    assert f(fake + 1, fake, fake, None, fake, 1, 64, 256, 128, None) == 4      # odd fp16 pointer
+    assert f(None, fake, fake, None, fake, 1, 64, 256, 128, None, 0, None) == 1          # null act
+    assert f(fake, fake, fake, None, fake, 0, 64, 256, 128, None, 0, None) == 2          # M = 0
+    assert f(fake, fake, fake, None, fake, 1, 64, 256, 100, None, 0, None) == 3          # K % G
+    assert f(fake, fake, fake, None, fake, 1, 64, 256, 0, None, 0, None) == 3            # G = 0
+    assert f(fake, fake, None, None, fake, 1, 64, 256, 128, None, 0, None) == 1          # null scales
+    assert f(fake + 1, fake, fake, None, fake, 1, 64, 256, 128, None, 0, None) == 4      # odd fp16 pointer
+    assert f(fake, fake, fake, None, fake, 1, 64, 256, 128, None, 4096, None) == 7       # bytes without pointer
+    assert f(fake, fake, fake, None, fake, 1, 64, 256, 128, fake + 16, 4096, None) == 4  # unaligned workspace
 
 
 def test_int4_odd_k_rejected(lib):
     fake = 0x1000
-    assert lib.lw_gemm_w4a16(fake, fake, fake, None, fake, 1, 8, 255, 255, None) == 2
+    assert lib.lw_gemm_w4a16(fake, fake, fake, None, fake, 1, 8, 255, 255, None, 0, None) == 2
 
 
 def test_error_becomes_exception(lib):
     with pytest.raises(nat.LiteweightError, match="bad group size"):
-        nat.call("lw_gemm_w8a16", 0x1000, 0x1000, 0x1000, None, 0x1000, 1, 64, 256, 100, None)
+        nat.call("lw_gemm_w8a16", 0x1000, 0x1000, 0x1000, None, 0x1000, 1, 64, 256, 100, None, 0, None)

@@ -283,3 +283,42 @@ def test_deterministic_and_graph_capturable():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out[0], a)
+
+
+@pytest.mark.parametrize("bits,M,K,N", [(4, 1, 8192, 512), (8, 3, 14336, 256), (16, 2, 4096, 1024),
+                                        (4, 9, 4096, 64), (8, 1, 2048, 2048)])
+def test_split_tiles_with_workspace(bits, M, K, N):
+    """Tiles shared between warps (workspace given) and whole tiles (no
+    workspace) both match the oracle; the workspace is left zeroed and repeated
+    calls are bit-identical."""
+    from liteweight_b200 import _native as nat
+    rng = np.random.default_rng(bits * 100 + M)
+    act = rng.standard_normal((M, K)).astype(np.float16)
+    if bits == 16:
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
+        ref = oq.matmul_dequant(act, w)
+        q, s = w, None
+    else:
+        q, s = quantized(N, K, 128, bits, seed=N + K)
+        ref = oq.packed_matmul(act, q, s, 128, bits)
+    a = torch.from_numpy(act).to(DEV)
+    qt = torch.from_numpy(q).to(DEV)
+    st = torch.from_numpy(s).to(DEV) if s is not None else None
+    need = int(nat.lib().lw_gemm_workspace_size(bits, M, N, K))
+    assert need > 0, "shape chosen to split tiles"
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    outs = []
+    stream = torch.cuda.current_stream().cuda_stream
+    for wsp, wsb in ((ws.data_ptr(), need), (ws.data_ptr(), need), (None, 0)):
+        o = torch.empty(M, N, dtype=torch.float16, device=DEV)
+        if bits == 16:
+            nat.call("lw_gemm_f16", a.data_ptr(), qt.data_ptr(), o.data_ptr(), M, N, K, wsp, wsb, stream)
+        else:
+            fn = "lw_gemm_w4a16" if bits == 4 else "lw_gemm_w8a16"
+            nat.call(fn, a.data_ptr(), qt.data_ptr(), st.data_ptr(), None, o.data_ptr(), M, N, K, 128, wsp, wsb,
+                     stream)
+        torch.cuda.synchronize()
+        outs.append(o)
+        check_rows(o, ref, f"bits={bits} ws={wsb}")
+    assert torch.equal(outs[0], outs[1])
+    assert int(ws.count_nonzero()) == 0 or bool((ws.view(torch.int32)[: (N + 15) // 16] == 0).all())
