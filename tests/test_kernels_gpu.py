@@ -321,4 +321,5 @@ def test_split_tiles_with_workspace(bits, M, K, N):
         outs.append(o)
         check_rows(o, ref, f"bits={bits} ws={wsb}")
     assert torch.equal(outs[0], outs[1])
-    assert int(ws.count_nonzero()) == 0 or bool((ws.view(torch.int32)[: (N + 15) // 16] == 0).all())
+    # the per-tile counters at the head of the workspace are back to zero
+    assert int(ws[: 4 * ((N + 15) // 16)].count_nonzero()) == 0
