@@ -65,8 +65,9 @@ unsigned long long lw_launch_count(void);
  *   qweight uint8 [N,K/2] (even k in the low nibble), K even.
  *
  * workspace (optional; may be NULL with workspace_bytes = 0): device scratch
- * of at least lw_gemm_workspace_size() bytes, 256-byte aligned, ZEROED before
- * its first use; every completed call leaves it zeroed again. With it, a
+ * of at least lw_gemm_workspace_size() bytes, 256-byte aligned, whose first
+ * 64 KiB (per-tile counters) are ZEROED before its first use; every completed
+ * call leaves them zeroed again, the rest is scratch. With it, a
  * weight tile may be split between warps (better balance for small N); the
  * partial sums are combined in a fixed order, so results are deterministic
  * for a given shape and device. Calls that run concurrently (different
@@ -101,6 +102,100 @@ int lw_dequant_w8(const void* qweight, const void* scales, void* out, int N, int
                   lw_stream_t stream);
 int lw_dequant_w4(const void* qweight, const void* scales, void* out, int N, int K, int group_size,
                   lw_stream_t stream);
+
+/* ---- decode step (one new token per sequence) -----------------------------
+ * The kernels of one decode step of the HF LlamaForCausalLM that liteweight's
+ * generate() drives (liteweight/generate.py:106-124; transformers
+ * modeling_llama.py:290-335, which the reference calls through
+ * QuantLinear.forward, liteweight/quantlinear.py:54-66). No single
+ * counterpart in the reference: there each op is a separate torch/HF call.
+ * Every kernel reads the current position from device memory, so a captured
+ * CUDA graph of one step replays every step. */
+
+/* How the fused GEMV stages its activation. */
+enum {
+  LW_PRO_PLAIN = 0,      /* act as given */
+  LW_PRO_NORM = 1,       /* RMSNorm(act) * gamma (modeling_llama.py:63-68) */
+  LW_PRO_RESID_NORM = 2  /* x_out = act + fp16(psum) (CTA 0 writes it), then RMSNorm */
+};
+
+/* What the fused GEMV does with each output. */
+enum {
+  LW_EPI_PLAIN = 0,    /* out = fp16(y) (+bias) (+residual); residual may alias out */
+  LW_EPI_ROPE_KV = 1,  /* q|k|v rows (rope-pair order): RoPE q,k; q -> q_out, k,v -> cache at *pos */
+  LW_EPI_SWIGLU = 2,   /* gate|up rows interleaved by 8: out[i] = silu(gate_i) * up_i */
+  LW_EPI_F32 = 3,      /* out_f32 = y unrounded (tensor-parallel partial sum) */
+  LW_EPI_ARGMAX = 4    /* out = fp16 logits; argmax_keys[m] = max(key) (first max wins) */
+};
+
+typedef struct {
+  int bits;          /* 4, 8 (liteweight formats) or 16 (fp16 weight) */
+  int prologue;      /* LW_PRO_* */
+  int epilogue;      /* LW_EPI_* */
+  int pdl;           /* 1: programmatic dependent launch (overlaps the previous kernel) */
+  int M, N, K, group_size;  /* M <= 32 rows */
+  int lda, ldo;
+  const void* act;      /* fp16 [M][lda] (the residual stream for the norm prologues) */
+  const void* weight;   /* [N][K*bits/8] */
+  const void* scales;   /* fp16 [N][K/group_size] (bits 4, 8) */
+  const void* bias;     /* fp16 [N] or NULL (LW_EPI_PLAIN) */
+  const void* residual; /* fp16 [M][ldo] or NULL (LW_EPI_PLAIN) */
+  void* out;            /* fp16 [M][ldo] */
+  const void* gamma;    /* fp16 [K] RMSNorm weight */
+  const float* psum;    /* fp32 [M][K] (LW_PRO_RESID_NORM) */
+  void* x_out;          /* fp16 [M][lda] (LW_PRO_RESID_NORM); must not alias act */
+  float eps;
+  int head_dim, n_q_heads, n_kv_heads, max_seq;
+  int argmax_offset;    /* vocabulary index of weight row 0 (vocab-sharded lm_head) */
+  const void* rope_cos; /* fp16 [max_seq][head_dim] */
+  const void* rope_sin;
+  const int* pos;       /* device position of this step */
+  void* q_out;          /* fp16 [M][n_q_heads*head_dim] */
+  void* k_cache;        /* fp16 [M][n_kv_heads][max_seq][head_dim] */
+  void* v_cache;
+  float* out_f32;       /* fp32 [M][ldo] (LW_EPI_F32) */
+  unsigned long long* argmax_keys; /* [M], zero before the launch (LW_EPI_ARGMAX) */
+  void* workspace;      /* as for lw_gemm_w8a16 */
+  size_t workspace_bytes;
+} lw_fused_gemv_args;
+
+int lw_fused_gemv(const lw_fused_gemv_args* args, lw_stream_t stream);
+size_t lw_fused_gemv_workspace_size(const lw_fused_gemv_args* args);
+
+/* Split-KV GQA attention of one query per sequence over cache positions
+ * 0..*pos (modeling_llama.py:197-222 with repeat_kv): scores scaled by
+ * head_dim^-0.5, fp32 softmax, fp16 output [batch][n_q_heads*head_dim].
+ * n_split > 1 needs part_o (fp32 [batch][n_q_heads][n_split][head_dim]),
+ * part_ml (fp32 [batch][n_q_heads][n_split][2]) and counters (int
+ * [batch][n_kv_heads], zero before first use, kept zero). */
+typedef struct {
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  void* out;
+  float* part_o;
+  float* part_ml;
+  int* counters;
+  const int* pos;
+  int batch, n_q_heads, n_kv_heads, head_dim, max_seq, n_split, pdl;
+} lw_attention_args;
+
+int lw_attention_decode(const lw_attention_args* args, lw_stream_t stream);
+
+/* sizeof(lw_fused_gemv_args) for which = 0, sizeof(lw_attention_args) for
+ * which = 1, else 0: lets a binding check its struct layout at load time. */
+size_t lw_struct_size(int which);
+
+/* x[b] = embed[tokens[*pos][b]] (tokens int32 [max_seq+1][batch]). */
+int lw_embed_tokens(const int* tokens, const void* embed, void* x, const int* pos, int batch, int hidden,
+                    int pdl, lw_stream_t stream);
+
+/* Next token per sequence: tokens[*pos+1][b] if it is >= 0 (a prompt token),
+ * else the argmax decoded from keys[b], which is then stored there; writes
+ * its embedding to x, clears keys and advances *pos by one (done: an int
+ * kept zero between calls). generate.py:49-52 (greedy pick). */
+int lw_sample_tokens(int* tokens, unsigned long long* keys, const void* embed, void* x, int* pos, int* done,
+                     int batch, int hidden, int pdl, lw_stream_t stream);
 
 #ifdef __cplusplus
 }

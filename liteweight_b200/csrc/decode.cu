@@ -1,0 +1,438 @@
+// Decode-step kernels for a Llama-family model on B200 (sm_100a).
+//
+// One decode step (one new token per sequence) of the HF LlamaForCausalLM that
+// liteweight's generate() drives (liteweight/generate.py:106-124 ->
+// transformers modeling_llama.py:290-335) runs as 5 kernels per layer:
+//
+//   1. fused GEMV: RMSNorm prologue + q|k|v projection + RoPE + KV append
+//   2. split-KV GQA attention over the cache (last CTA per head group combines)
+//   3. fused GEMV: o_proj + residual add
+//   4. fused GEMV: RMSNorm prologue + gate|up projection + SwiGLU
+//   5. fused GEMV: down_proj + residual add
+//
+// then the final RMSNorm + lm_head + argmax GEMV and a sampling kernel that
+// picks the next token (or takes the forced prompt token), writes its
+// embedding as the next step's residual stream and advances the position.
+// Every kernel reads the position from device memory, so one captured CUDA
+// graph replays any step. With tensor parallelism the o/down projections
+// write fp32 partial sums instead (all-reduced by the caller) and the next
+// norm prologue adds them to the residual.
+#include "gemv_host.cuh"
+
+namespace lw {
+
+// ------------------------------------------------------------- attention
+
+struct AttnParams {
+  const __half* q;     // [B][nq * hd]
+  const __half* k;     // [B][nkv][S][hd] (this layer)
+  const __half* v;
+  __half* out;         // [B][nq * hd]
+  float* part_o;       // [B][nq][nsplit][hd]
+  float* part_ml;      // [B][nq][nsplit][2] (running max in log2 units, sum)
+  int* counters;       // [B][nkv], zero before the first launch, left zero
+  const int* pos;      // attend over positions 0..*pos
+  int B, nq, nkv, S, nsplit;
+  float scale_log2;    // head_dim^-0.5 * log2(e)
+};
+
+constexpr int kAttnWarps = 4;
+
+// One CTA = one (sequence, kv head, position split). Lanes split the head
+// dimension; each warp walks its positions with an online softmax per query
+// head of the GQA group; warps, then splits, are merged by max-rescaling.
+template <int HD, int GQ>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnParams p) {
+  constexpr int D = HD / 32;
+  __shared__ float sm_m[kAttnWarps][GQ], sm_l[kAttnWarps][GQ];
+  __shared__ float sm_acc[kAttnWarps][GQ][HD];
+  __shared__ int sm_last;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  const int len = *p.pos + 1;
+  const int chunk = (len + p.nsplit - 1) / p.nsplit;
+  const int s0 = split * chunk, s1 = min(len, s0 + chunk);
+
+  float qf[GQ][D];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    const __half* qp = p.q + (size_t)b * p.nq * HD + (size_t)(kvh * GQ + h) * HD + lane * D;
+#pragma unroll
+    for (int d = 0; d < D; ++d) qf[h][d] = __half2float(qp[d]) * p.scale_log2;
+  }
+  float m[GQ], l[GQ], acc[GQ][D];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int d = 0; d < D; ++d) acc[h][d] = 0.f;
+  }
+  const size_t head_base = ((size_t)b * p.nkv + kvh) * p.S;
+  for (int s = s0 + warp; s < s1; s += kAttnWarps) {
+    const __half* kp = p.k + (head_base + s) * HD + lane * D;
+    const __half* vp = p.v + (head_base + s) * HD + lane * D;
+    float kf[D], vf[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      kf[d] = __half2float(kp[d]);
+      vf[d] = __half2float(vp[d]);
+    }
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+      float dot = 0.f;
+#pragma unroll
+      for (int d = 0; d < D; ++d) dot = fmaf(qf[h][d], kf[d], dot);
+      dot = warp_sum(dot);
+      const float mn = fmaxf(m[h], dot);
+      const float corr = exp2f(m[h] - mn);
+      const float e = exp2f(dot - mn);
+      l[h] = l[h] * corr + e;
+#pragma unroll
+      for (int d = 0; d < D; ++d) acc[h][d] = fmaf(acc[h][d], corr, e * vf[d]);
+      m[h] = mn;
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    if (lane == 0) {
+      sm_m[warp][h] = m[h];
+      sm_l[warp][h] = l[h];
+    }
+#pragma unroll
+    for (int d = 0; d < D; ++d) sm_acc[warp][h][lane * D + d] = acc[h][d];
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  // merge the warps: thread -> (h, dim) pairs
+  for (int i = threadIdx.x; i < GQ * HD; i += kAttnWarps * 32) {
+    const int h = i / HD, d = i - h * HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][h]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float c = exp2f(sm_m[w][h] - M);
+        L = fmaf(sm_l[w][h], c, L);
+        A = fmaf(sm_acc[w][h][d], c, A);
+      }
+    }
+    const int head = kvh * GQ + h;
+    if (p.nsplit == 1) {
+      p.out[(size_t)b * p.nq * HD + (size_t)head * HD + d] = __float2half_rn(A / L);
+    } else {
+      const size_t slot = ((size_t)b * p.nq + head) * p.nsplit + split;
+      p.part_o[slot * HD + d] = A;
+      if (d == 0) {
+        p.part_ml[slot * 2] = M;
+        p.part_ml[slot * 2 + 1] = L;
+      }
+    }
+  }
+  if (p.nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(p.counters + b * p.nkv + kvh, 1);
+    sm_last = (old == p.nsplit - 1);
+  }
+  __syncthreads();
+  if (!sm_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < GQ * HD; i += kAttnWarps * 32) {
+    const int h = i / HD, d = i - h * HD;
+    const int head = kvh * GQ + h;
+    const size_t base = ((size_t)b * p.nq + head) * p.nsplit;
+    float M = -INFINITY;
+    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, __ldcg(p.part_ml + (base + s) * 2));
+    float L = 0.f, A = 0.f;
+    for (int s = 0; s < p.nsplit; ++s) {
+      const float ms = __ldcg(p.part_ml + (base + s) * 2);
+      if (ms == -INFINITY) continue;
+      const float c = exp2f(ms - M);
+      L = fmaf(__ldcg(p.part_ml + (base + s) * 2 + 1), c, L);
+      A = fmaf(__ldcg(p.part_o + (base + s) * HD + d), c, A);
+    }
+    p.out[(size_t)b * p.nq * HD + (size_t)head * HD + d] = __float2half_rn(A / L);
+  }
+  if (threadIdx.x == 0) p.counters[b * p.nkv + kvh] = 0;
+}
+
+// ------------------------------------------------------------- tokens
+
+// x[b] = embed[tokens[*pos][b]]
+__global__ void embed_kernel(const int* __restrict__ tokens, const __half* __restrict__ embed,
+                             __half* __restrict__ x, const int* pos, int B, int H) {
+  pdl_wait();
+  const int b = blockIdx.x;
+  const int tok = tokens[(size_t)(*pos) * B + b];
+  const uint4* src = reinterpret_cast<const uint4*>(embed + (size_t)tok * H);
+  uint4* dst = reinterpret_cast<uint4*>(x + (size_t)b * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// Next token per sequence: the forced token at position *pos + 1 when the
+// table holds one (>= 0, a prompt token), else the argmax of the logits
+// (first index of the maximum, torch.argmax semantics; generate.py:51-52).
+// Writes it to the table, loads its embedding as the next residual stream,
+// clears the argmax key and, in the last block to finish, advances *pos.
+__global__ void sample_kernel(int* __restrict__ tokens, unsigned long long* __restrict__ keys,
+                              const __half* __restrict__ embed, __half* __restrict__ x, int* pos,
+                              int* done, int B, int H) {
+  pdl_wait();
+  __shared__ int s_tok;
+  const int b = blockIdx.x;
+  const int p_next = *pos + 1;
+  if (threadIdx.x == 0) {
+    int tok = tokens[(size_t)p_next * B + b];
+    if (tok < 0) {
+      tok = (int)(0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull));
+      tokens[(size_t)p_next * B + b] = tok;
+    }
+    keys[b] = 0ull;
+    s_tok = tok;
+  }
+  __syncthreads();
+  const uint4* src = reinterpret_cast<const uint4*>(embed + (size_t)s_tok * H);
+  uint4* dst = reinterpret_cast<uint4*>(x + (size_t)b * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int old = atomicAdd(done, 1);
+    if (old == B - 1) {
+      *pos = p_next;
+      *done = 0;
+    }
+  }
+}
+
+}  // namespace lw
+
+// ======================================================================= host
+
+namespace {
+
+inline bool al(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+lw::StreamParams to_stream(const lw_fused_gemv_args* a) {
+  lw::StreamParams p = {};
+  p.act = static_cast<const __half*>(a->act);
+  p.w = static_cast<const uint8_t*>(a->weight);
+  p.scales = static_cast<const __half*>(a->scales);
+  p.bias = static_cast<const __half*>(a->bias);
+  p.residual = static_cast<const __half*>(a->residual);
+  p.out = static_cast<__half*>(a->out);
+  p.lda = a->lda;
+  p.ldo = a->ldo;
+  p.M = a->M;
+  p.N = a->N;
+  p.K = a->K;
+  p.G = a->bits == 16 ? a->K : a->group_size;
+  p.gamma = static_cast<const __half*>(a->gamma);
+  p.eps = a->eps;
+  p.psum = a->psum;
+  p.x_out = static_cast<__half*>(a->x_out);
+  p.rope_cos = static_cast<const __half*>(a->rope_cos);
+  p.rope_sin = static_cast<const __half*>(a->rope_sin);
+  p.pos = a->pos;
+  p.head_dim = a->head_dim;
+  p.n_q_heads = a->n_q_heads;
+  p.n_kv_heads = a->n_kv_heads;
+  p.max_seq = a->max_seq;
+  p.q_out = static_cast<__half*>(a->q_out);
+  p.k_cache = static_cast<__half*>(a->k_cache);
+  p.v_cache = static_cast<__half*>(a->v_cache);
+  p.out_f32 = a->out_f32;
+  p.argmax_keys = a->argmax_keys;
+  p.argmax_offset = a->argmax_offset;
+  return p;
+}
+
+template <int BITS, int PRO, int EPI>
+cudaError_t fused_launch(const lw_fused_gemv_args* a, cudaStream_t s) {
+  return lw::launch_stream_block<BITS, PRO, EPI>(to_stream(a), a->workspace, a->workspace_bytes, s, a->pdl != 0);
+}
+
+template <int BITS, int PRO, int EPI>
+size_t fused_ws(const lw_fused_gemv_args* a) {
+  return lw::stream_workspace<BITS, PRO, EPI>(a->M, a->N, a->K);
+}
+
+// The (bits, prologue, epilogue) combinations the decode step uses.
+#define LW_FUSED_TABLE(X)                                   \
+  X(4, lw::PRO_NORM, lw::EPI_ROPE_KV)                       \
+  X(8, lw::PRO_NORM, lw::EPI_ROPE_KV)                       \
+  X(4, lw::PRO_RESID_NORM, lw::EPI_ROPE_KV)                 \
+  X(8, lw::PRO_RESID_NORM, lw::EPI_ROPE_KV)                 \
+  X(4, lw::PRO_NORM, lw::EPI_SWIGLU)                        \
+  X(8, lw::PRO_NORM, lw::EPI_SWIGLU)                        \
+  X(4, lw::PRO_RESID_NORM, lw::EPI_SWIGLU)                  \
+  X(8, lw::PRO_RESID_NORM, lw::EPI_SWIGLU)                  \
+  X(4, lw::PRO_PLAIN, lw::EPI_PLAIN)                        \
+  X(8, lw::PRO_PLAIN, lw::EPI_PLAIN)                        \
+  X(4, lw::PRO_PLAIN, lw::EPI_F32)                          \
+  X(8, lw::PRO_PLAIN, lw::EPI_F32)                          \
+  X(16, lw::PRO_NORM, lw::EPI_ARGMAX)                       \
+  X(16, lw::PRO_RESID_NORM, lw::EPI_ARGMAX)
+
+int validate(const lw_fused_gemv_args* a) {
+  if (!a) return LW_ERR_NULL_POINTER;
+  if (!a->act || !a->weight) return LW_ERR_NULL_POINTER;
+  if (a->bits != 4 && a->bits != 8 && a->bits != 16) return LW_ERR_UNSUPPORTED;
+  if (a->M <= 0 || a->M > 32 || a->N <= 0 || a->K <= 0) return LW_ERR_BAD_SHAPE;
+  if (a->bits != 16 && (!a->scales || a->group_size <= 0 || a->K % a->group_size)) return LW_ERR_BAD_GROUP;
+  const int E = a->bits == 4 ? 32 : (a->bits == 8 ? 16 : 8);
+  if ((size_t)a->K * a->bits / 8 % 16 || a->K % 8 || (a->bits != 16 && a->group_size % E)) return LW_ERR_UNSUPPORTED;
+  if (!al(a->act, 16) || !al(a->weight, 16) || a->lda % 8) return LW_ERR_ALIGNMENT;
+  const int KC = 4 * E;
+  if ((size_t)a->M * ((a->K + KC - 1) / KC) * KC * 2 > (size_t)lw::kStageBudget) return LW_ERR_UNSUPPORTED;
+  if (a->prologue != LW_PRO_PLAIN) {
+    if (!a->gamma || !al(a->gamma, 16)) return LW_ERR_NULL_POINTER;
+    if (a->prologue == LW_PRO_RESID_NORM && (!a->psum || !a->x_out || !al(a->psum, 16) || !al(a->x_out, 16)))
+      return LW_ERR_NULL_POINTER;
+  }
+  switch (a->epilogue) {
+    case LW_EPI_PLAIN:
+      if (!a->out) return LW_ERR_NULL_POINTER;
+      break;
+    case LW_EPI_F32:
+      if (!a->out_f32) return LW_ERR_NULL_POINTER;
+      break;
+    case LW_EPI_ROPE_KV:
+      if (!a->q_out || !a->k_cache || !a->v_cache || !a->rope_cos || !a->rope_sin || !a->pos)
+        return LW_ERR_NULL_POINTER;
+      if (a->head_dim % 16 || a->N != (a->n_q_heads + 2 * a->n_kv_heads) * a->head_dim) return LW_ERR_BAD_SHAPE;
+      break;
+    case LW_EPI_SWIGLU:
+      if (!a->out) return LW_ERR_NULL_POINTER;
+      if (a->N % 16) return LW_ERR_BAD_SHAPE;
+      break;
+    case LW_EPI_ARGMAX:
+      if (!a->out || !a->argmax_keys) return LW_ERR_NULL_POINTER;
+      break;
+    default:
+      return LW_ERR_UNSUPPORTED;
+  }
+  if (a->workspace_bytes && !a->workspace) return LW_ERR_WORKSPACE;
+  if (a->workspace && !al(a->workspace, 256)) return LW_ERR_ALIGNMENT;
+  return LW_OK;
+}
+
+template <int HD, int GQ>
+cudaError_t attn_launch(const lw::AttnParams& p, cudaStream_t s, bool pdl) {
+  dim3 grid(p.nsplit, p.nkv, p.B), block(lw::kAttnWarps * 32);
+  return lw_launch(lw::attn_decode_kernel<HD, GQ>, grid, block, 0, s, pdl, p);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lw_fused_gemv(const lw_fused_gemv_args* a, lw_stream_t stream) {
+  int st = validate(a);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaGetLastError();
+  cudaError_t e = cudaErrorInvalidValue;
+  bool found = false;
+#define X(B_, P_, E_)                                                         \
+  if (!found && a->bits == B_ && a->prologue == P_ && a->epilogue == E_) {  \
+    found = true;                                                           \
+    e = fused_launch<B_, P_, E_>(a, s);                                     \
+  }
+  LW_FUSED_TABLE(X)
+#undef X
+  if (!found) return LW_ERR_UNSUPPORTED;
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+
+size_t lw_fused_gemv_workspace_size(const lw_fused_gemv_args* a) {
+  if (validate(a) != LW_OK) return 0;
+  size_t r = 0;
+  bool found = false;
+#define X(B_, P_, E_)                                                         \
+  if (!found && a->bits == B_ && a->prologue == P_ && a->epilogue == E_) {  \
+    found = true;                                                           \
+    r = fused_ws<B_, P_, E_>(a);                                            \
+  }
+  LW_FUSED_TABLE(X)
+#undef X
+  return r;
+}
+
+int lw_attention_decode(const lw_attention_args* a, lw_stream_t stream) {
+  if (!a || !a->q || !a->k_cache || !a->v_cache || !a->out || !a->pos) return LW_ERR_NULL_POINTER;
+  if (a->batch <= 0 || a->n_kv_heads <= 0 || a->n_q_heads % a->n_kv_heads || a->max_seq <= 0 || a->n_split <= 0)
+    return LW_ERR_BAD_SHAPE;
+  if (a->n_split > 1 && (!a->part_o || !a->part_ml || !a->counters)) return LW_ERR_WORKSPACE;
+  lw::AttnParams p = {};
+  p.q = static_cast<const __half*>(a->q);
+  p.k = static_cast<const __half*>(a->k_cache);
+  p.v = static_cast<const __half*>(a->v_cache);
+  p.out = static_cast<__half*>(a->out);
+  p.part_o = a->part_o;
+  p.part_ml = a->part_ml;
+  p.counters = a->counters;
+  p.pos = a->pos;
+  p.B = a->batch;
+  p.nq = a->n_q_heads;
+  p.nkv = a->n_kv_heads;
+  p.S = a->max_seq;
+  p.nsplit = a->n_split;
+  p.scale_log2 = (1.0f / sqrtf((float)a->head_dim)) * 1.4426950408889634f;
+  const int gq = a->n_q_heads / a->n_kv_heads;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool pdl = a->pdl != 0;
+  cudaGetLastError();
+  cudaError_t e;
+  if (a->head_dim == 128 && gq == 4) e = attn_launch<128, 4>(p, s, pdl);
+  else if (a->head_dim == 128 && gq == 8) e = attn_launch<128, 8>(p, s, pdl);
+  else if (a->head_dim == 128 && gq == 2) e = attn_launch<128, 2>(p, s, pdl);
+  else if (a->head_dim == 128 && gq == 1) e = attn_launch<128, 1>(p, s, pdl);
+  else if (a->head_dim == 64 && gq == 4) e = attn_launch<64, 4>(p, s, pdl);
+  else if (a->head_dim == 64 && gq == 2) e = attn_launch<64, 2>(p, s, pdl);
+  else if (a->head_dim == 64 && gq == 8) e = attn_launch<64, 8>(p, s, pdl);
+  else if (a->head_dim == 64 && gq == 1) e = attn_launch<64, 1>(p, s, pdl);
+  else return LW_ERR_UNSUPPORTED;
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+
+size_t lw_struct_size(int which) {
+  if (which == 0) return sizeof(lw_fused_gemv_args);
+  if (which == 1) return sizeof(lw_attention_args);
+  return 0;
+}
+
+int lw_embed_tokens(const int* tokens, const void* embed, void* x, const int* pos, int batch, int hidden, int pdl,
+                    lw_stream_t stream) {
+  if (!tokens || !embed || !x || !pos) return LW_ERR_NULL_POINTER;
+  if (batch <= 0 || hidden <= 0 || hidden % 8) return LW_ERR_BAD_SHAPE;
+  if (!al(embed, 16) || !al(x, 16)) return LW_ERR_ALIGNMENT;
+  cudaGetLastError();
+  cudaError_t e = lw_launch(lw::embed_kernel, dim3(batch), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                            pdl != 0, tokens, static_cast<const __half*>(embed), static_cast<__half*>(x), pos, batch,
+                            hidden);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+
+int lw_sample_tokens(int* tokens, unsigned long long* keys, const void* embed, void* x, int* pos, int* done,
+                     int batch, int hidden, int pdl, lw_stream_t stream) {
+  if (!tokens || !keys || !embed || !x || !pos || !done) return LW_ERR_NULL_POINTER;
+  if (batch <= 0 || hidden <= 0 || hidden % 8) return LW_ERR_BAD_SHAPE;
+  if (!al(embed, 16) || !al(x, 16)) return LW_ERR_ALIGNMENT;
+  cudaGetLastError();
+  cudaError_t e = lw_launch(lw::sample_kernel, dim3(batch), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                            pdl != 0, tokens, keys, static_cast<const __half*>(embed), static_cast<__half*>(x), pos,
+                            done, batch, hidden);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -88,6 +88,7 @@ struct StreamParams {
   __half* v_cache;
   float* out_f32;          // EPI_F32: [M][ldo]
   unsigned long long* argmax_keys;  // EPI_ARGMAX: [M], zero before the launch
+  int argmax_offset;       // EPI_ARGMAX: index of row 0 in the full vocabulary (vocab shards)
   // split-tile combination (scratch)
   float* slots;            // [tiles][max_slots][32 lanes][4 * MT]
   int* counters;           // [tiles], zero before the first launch, left zero
@@ -250,7 +251,8 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
             const __half y = __float2half_rn(v[mt][2 * h + c]);
             p.out[(size_t)m * p.ldo + n] = y;
             const unsigned long long key =
-                ((unsigned long long)f16_order_key(y) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+                ((unsigned long long)f16_order_key(y) << 32) |
+                (unsigned long long)(0xFFFFFFFFu - (uint32_t)(n + p.argmax_offset));
             best = key > best ? key : best;
           }
         }

@@ -9,6 +9,11 @@ namespace lw {
 
 constexpr int kStageBudget = 220 * 1024;   // dynamic shared memory for the staged activation
 constexpr int kBatch = 2;                  // 16-byte chunks per row per register buffer
+// Workspace layout: a fixed region of per-tile counters (kept zero between
+// calls, so any later call of any shape finds its counters zero), then the
+// fp32 slots, which are fully rewritten before they are read.
+constexpr size_t kCounterBytes = 64 * 1024;
+constexpr int kMaxSplitTiles = (int)(kCounterBytes / 4);
 
 inline int device_sm_count() {
   int dev = 0, n = 0;
@@ -54,13 +59,13 @@ cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   const long long warps_max = (long long)device_sm_count() * occ * (kStreamThreads / 32);
   const long long total = (long long)pl->tiles * pl->kchunks;
   long long per = std::max<long long>(kBatch, (total + warps_max - 1) / warps_max);
-  if (!allow_split) per = (per + pl->kchunks - 1) / pl->kchunks * pl->kchunks;
+  if (!allow_split || pl->tiles > kMaxSplitTiles) per = (per + pl->kchunks - 1) / pl->kchunks * pl->kchunks;
   pl->per = (int)per;
   const long long warps = (total + per - 1) / per;
   pl->grid = (int)((warps + kStreamThreads / 32 - 1) / (kStreamThreads / 32));
   const bool split = (per % pl->kchunks) != 0;
   pl->max_slots = split ? (pl->kchunks - 1) / pl->per + 2 : 0;
-  pl->ws_bytes = split ? align_up((size_t)pl->tiles * 4, 256) + (size_t)pl->tiles * pl->max_slots * 32 * 4 * MT * 4 : 0;
+  pl->ws_bytes = split ? kCounterBytes + (size_t)pl->tiles * pl->max_slots * 32 * 4 * MT * 4 : 0;
   return cudaSuccess;
 }
 
@@ -92,7 +97,7 @@ cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaS
   p.max_slots = pl.max_slots;
   if (pl.ws_bytes) {
     p.counters = static_cast<int*>(ws);
-    p.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + align_up((size_t)pl.tiles * 4, 256));
+    p.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
   } else {
     p.counters = nullptr;
     p.slots = nullptr;

@@ -1,5 +1,556 @@
-"""Native decode engine (the fused decode kernels are not built yet)."""
+"""Native decode engine for Llama-family models on B200.
 
+Replaces the per-token loop of liteweight/generate.py:97-124 (HF forward with
+DynamicCache, ~10 eager ops + 7 QuantLinear calls per layer, a host sync per
+token) with one CUDA graph per decode step built from the library's fused
+kernels (include/liteweight_b200.h, decode step section):
+
+  per layer: [RMSNorm + q|k|v GEMV + RoPE + KV append] -> [split-KV GQA
+  attention] -> [o GEMV + residual] -> [RMSNorm + gate|up GEMV + SwiGLU] ->
+  [down GEMV + residual];  then [RMSNorm + lm_head GEMV + argmax] -> [pick /
+  embed next token, advance position].
+
+The position lives on the device, so the same graph replays every step; the
+prompt is consumed by the same step (its tokens are "forced" in the token
+table), so prefill and decode share one code path. KV cache: preallocated
+fp16 [B, n_kv, max_seq, head_dim] per layer (the layout of the reference's
+KVCache, generate.py:22-25).
+
+Tensor parallelism (``tp_size > 1``, one process per GPU): q/k/v and gate/up
+are split by output rows (heads / intermediate), o and down by input
+columns; o/down write fp32 partial sums that an NCCL all-reduce sums, and the
+next norm prologue adds them to the residual. The lm_head is split by
+vocabulary rows; the per-rank argmax keys are max-reduced.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from liteweight_b200 import _native as nat
+
+c_int, c_void_p, c_float, c_size_t = ctypes.c_int, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
+
+PRO_PLAIN, PRO_NORM, PRO_RESID_NORM = 0, 1, 2
+EPI_PLAIN, EPI_ROPE_KV, EPI_SWIGLU, EPI_F32, EPI_ARGMAX = 0, 1, 2, 3, 4
+
+
+class FusedGemvArgs(ctypes.Structure):
+    """Mirror of lw_fused_gemv_args (include/liteweight_b200.h)."""
+    _fields_ = [
+        ("bits", c_int), ("prologue", c_int), ("epilogue", c_int), ("pdl", c_int),
+        ("M", c_int), ("N", c_int), ("K", c_int), ("group_size", c_int), ("lda", c_int), ("ldo", c_int),
+        ("act", c_void_p), ("weight", c_void_p), ("scales", c_void_p), ("bias", c_void_p), ("residual", c_void_p),
+        ("out", c_void_p), ("gamma", c_void_p), ("psum", c_void_p), ("x_out", c_void_p),
+        ("eps", c_float), ("head_dim", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("max_seq", c_int),
+        ("argmax_offset", c_int),
+        ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("pos", c_void_p),
+        ("q_out", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
+        ("out_f32", c_void_p), ("argmax_keys", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+    ]
+
+
+class AttentionArgs(ctypes.Structure):
+    """Mirror of lw_attention_args (include/liteweight_b200.h)."""
+    _fields_ = [
+        ("q", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p), ("out", c_void_p),
+        ("part_o", c_void_p), ("part_ml", c_void_p), ("counters", c_void_p), ("pos", c_void_p),
+        ("batch", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("max_seq", c_int),
+        ("n_split", c_int), ("pdl", c_int),
+    ]
+
+
+nat.register("lw_fused_gemv", [ctypes.POINTER(FusedGemvArgs), c_void_p])
+nat.register("lw_fused_gemv_workspace_size", [ctypes.POINTER(FusedGemvArgs)], c_size_t)
+nat.register("lw_attention_decode", [ctypes.POINTER(AttentionArgs), c_void_p])
+nat.register("lw_embed_tokens", [c_void_p] * 4 + [c_int] * 3 + [c_void_p])
+nat.register("lw_sample_tokens", [c_void_p] * 6 + [c_int] * 3 + [c_void_p])
+nat.register("lw_struct_size", [c_int], c_size_t)
+
+
+def check_abi() -> None:
+    """The ctypes mirrors must have the library's struct sizes."""
+    lib = nat.lib()
+    for which, cls in ((0, FusedGemvArgs), (1, AttentionArgs)):
+        got = int(lib.lw_struct_size(which))
+        if got != ctypes.sizeof(cls):
+            raise RuntimeError(f"{cls.__name__}: ctypes size {ctypes.sizeof(cls)} != library size {got}")
+
+
+# ------------------------------------------------------------------ model spec / weights
+
+@dataclass
+class LlamaSpec:
+    hidden: int
+    inter: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    bits: int = 4
+    group_size: int = 128
+    eps: float = 1e-5
+    rope_theta: float = 500000.0
+
+    def linear_shapes(self):
+        """(name, out_features, in_features) of the quantized linears of one layer."""
+        h, i, hd = self.hidden, self.inter, self.head_dim
+        return [("q", self.n_heads * hd, h), ("k", self.n_kv_heads * hd, h), ("v", self.n_kv_heads * hd, h),
+                ("o", h, self.n_heads * hd), ("gate", i, h), ("up", i, h), ("down", h, i)]
+
+    def weight_bytes_per_token(self, include_lm_head: bool = True) -> int:
+        """Bytes one decode step must read: packed weights + fp16 scales (+ lm_head, norms)."""
+        per_layer = sum(n * k * self.bits // 8 + 2 * n * (k // self.group_size) for _, n, k in self.linear_shapes())
+        total = self.n_layers * (per_layer + 4 * self.hidden)
+        if include_lm_head:
+            total += self.vocab * self.hidden * 2 + 2 * self.hidden
+        return total
+
+    def kv_bytes_per_position(self) -> int:
+        return self.n_layers * 2 * self.n_kv_heads * self.head_dim * 2
+
+
+LLAMA_3_2_1B = dict(hidden=2048, inter=8192, n_layers=16, n_heads=32, n_kv_heads=8, head_dim=64, vocab=128256)
+LLAMA_3_8B = dict(hidden=4096, inter=14336, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, vocab=128256)
+LLAMA_3_70B = dict(hidden=8192, inter=28672, n_layers=80, n_heads=64, n_kv_heads=8, head_dim=128, vocab=128256)
+
+
+@dataclass
+class LayerWeights:
+    """One layer's quantized linears in liteweight's format, unsharded, natural row order."""
+    q: tuple
+    k: tuple
+    v: tuple
+    o: tuple
+    gate: tuple
+    up: tuple
+    down: tuple
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+
+
+def rope_pair_order(n_heads: int, head_dim: int, device) -> torch.Tensor:
+    """Row permutation that puts head dims d and d + hd/2 in rows g and g+8 of
+    each 16-row tile: tile j of a head holds dims 8j..8j+7 and hd/2+8j..+7."""
+    hd, half = head_dim, head_dim // 2
+    per_head = []
+    for j in range(hd // 16):
+        per_head += list(range(8 * j, 8 * j + 8)) + list(range(half + 8 * j, half + 8 * j + 8))
+    idx = torch.tensor(per_head, dtype=torch.long)
+    return torch.cat([idx + h * hd for h in range(n_heads)]).to(device)
+
+
+def interleave8(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Rows a[8t:8t+8], b[8t:8t+8] alternately (gate/up pairs in one 16-row tile)."""
+    n = a.shape[0]
+    return torch.stack([a.reshape(n // 8, 8, -1), b.reshape(n // 8, 8, -1)], dim=1).reshape(2 * n, -1).contiguous()
+
+
+def shard_rows(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    n = t.shape[0] // size
+    return t[rank * n:(rank + 1) * n]
+
+
+def shard_cols(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    n = t.shape[1] // size
+    return t[:, rank * n:(rank + 1) * n]
+
+
+class PackedLayer:
+    """Device buffers of one layer in the engine's layout (this rank's shard)."""
+
+    def __init__(self, lw: LayerWeights, spec: LlamaSpec, rank: int, size: int, device):
+        hd = spec.head_dim
+        nq, nkv = spec.n_heads // size, spec.n_kv_heads // size
+
+        def rows(pair):
+            q, s = pair
+            return shard_rows(q, rank, size), shard_rows(s, rank, size)
+
+        qw, qs = rows(lw.q)
+        kw, ks = rows(lw.k)
+        vw, vs = rows(lw.v)
+        perm_q = rope_pair_order(nq, hd, qw.device)
+        perm_kv = rope_pair_order(nkv, hd, qw.device)
+        self.qkv_w = torch.cat([qw[perm_q], kw[perm_kv], vw[perm_kv]]).contiguous().to(device)
+        self.qkv_s = torch.cat([qs[perm_q], ks[perm_kv], vs[perm_kv]]).contiguous().to(device)
+        gw, gs = rows(lw.gate)
+        uw, us = rows(lw.up)
+        self.gu_w = interleave8(gw, uw).to(device)
+        self.gu_s = interleave8(gs, us).to(device)
+        # o / down: split the input columns (K); packed INT4 columns are K/2 bytes
+        ow, os_ = lw.o
+        dw, ds = lw.down
+        self.o_w = shard_cols(ow, rank, size).contiguous().to(device)
+        self.o_s = shard_cols(os_, rank, size).contiguous().to(device)
+        self.d_w = shard_cols(dw, rank, size).contiguous().to(device)
+        self.d_s = shard_cols(ds, rank, size).contiguous().to(device)
+        self.in_norm = lw.in_norm.to(device=device, dtype=torch.float16).contiguous()
+        self.post_norm = lw.post_norm.to(device=device, dtype=torch.float16).contiguous()
+
+
+def rope_tables(inv_freq: torch.Tensor, max_seq: int, scaling: float, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [max_seq, head_dim] fp16, computed like modeling_llama.py:124-136."""
+    inv = inv_freq.to(device=device, dtype=torch.float32)
+    pos = torch.arange(max_seq, device=device, dtype=torch.float32)
+    freqs = (inv[None, :, None] @ pos[None, None, :]).transpose(1, 2)[0]
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return (emb.cos() * scaling).half().contiguous(), (emb.sin() * scaling).half().contiguous()
+
+
+def default_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
+    """modeling_llama.py:119-121 (default RoPE)."""
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(dtype=torch.float) / head_dim))
+
+
+# ------------------------------------------------------------------ engine
+
+class DecodeEngine:
+    """Batched greedy decode of a Llama model on one GPU (or one tensor-parallel rank)."""
+
+    def __init__(self, spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
+                 lm_head: torch.Tensor | None, rope_cos: torch.Tensor, rope_sin: torch.Tensor, batch: int,
+                 max_seq: int, device=None, tp_rank: int = 0, tp_size: int = 1, tp_group=None, pdl: bool = True):
+        self.spec, self.B, self.S = spec, batch, max_seq
+        self.device = torch.device(device) if device is not None else embed.device
+        self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
+        assert spec.n_heads % tp_size == 0 and spec.n_kv_heads % tp_size == 0, "heads must split evenly"
+        assert spec.inter % (8 * tp_size) == 0 and spec.vocab % tp_size == 0
+        assert batch <= 32, "one launch stages at most 32 activation rows"
+        self.nq, self.nkv = spec.n_heads // tp_size, spec.n_kv_heads // tp_size
+        self.inter = spec.inter // tp_size
+        self.vshard = spec.vocab // tp_size
+        self.pdl = int(pdl)
+        check_abi()
+        dev, H, hd = self.device, spec.hidden, spec.head_dim
+        self.layers = layers
+        self.embed = embed.to(device=dev, dtype=torch.float16).contiguous()
+        head = self.embed if lm_head is None else lm_head.to(device=dev, dtype=torch.float16).contiguous()
+        self.lm_head = shard_rows(head, tp_rank, tp_size)
+        self.final_norm = final_norm.to(device=dev, dtype=torch.float16).contiguous()
+        self.rope_cos = rope_cos.to(dev).contiguous()
+        self.rope_sin = rope_sin.to(dev).contiguous()
+        assert self.rope_cos.shape[0] >= max_seq
+        f16 = dict(dtype=torch.float16, device=dev)
+        self.k_cache = [torch.zeros(batch, self.nkv, max_seq, hd, **f16) for _ in layers]
+        self.v_cache = [torch.zeros(batch, self.nkv, max_seq, hd, **f16) for _ in layers]
+        self.x = torch.zeros(batch, H, **f16)
+        self.x2 = torch.zeros(batch, H, **f16)
+        self.q = torch.zeros(batch, self.nq * hd, **f16)
+        self.attn = torch.zeros(batch, self.nq * hd, **f16)
+        self.act = torch.zeros(batch, self.inter, **f16)
+        self.logits = torch.zeros(batch, self.vshard, **f16)
+        self.psum = torch.zeros(batch, H, dtype=torch.float32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.keys = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.tokens = torch.full((max_seq + 1, batch), -1, dtype=torch.int32, device=dev)
+        # attention split: about two waves of CTAs at full length, >= 32 positions per split
+        self.n_split = max(1, min(-(-2 * 148 // (batch * self.nkv)), -(-max_seq // 32)))
+        self.part_o = torch.zeros(batch, self.nq, self.n_split, hd, dtype=torch.float32, device=dev)
+        self.part_ml = torch.zeros(batch, self.nq, self.n_split, 2, dtype=torch.float32, device=dev)
+        self.attn_counters = torch.zeros(batch * self.nkv, dtype=torch.int32, device=dev)
+        self._build_calls()
+        self.graph = None
+        self.host_pos = 0
+
+    # -------------------------------------------------------------- call table
+    def _gemv(self, **kw) -> FusedGemvArgs:
+        a = FusedGemvArgs()
+        a.pdl, a.M, a.eps = self.pdl, self.B, self.spec.eps
+        for k, v in kw.items():
+            setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
+        return a
+
+    def _build_calls(self):
+        sp, B, H, hd = self.spec, self.B, self.spec.hidden, self.spec.head_dim
+        tp = self.tp_size > 1
+        calls = []
+        xs = [self.x, self.x2]
+        cur = 0           # index of the buffer holding the residual stream
+        pending = False   # an all-reduced partial waits to be added to the residual
+        gemv_args = []
+
+        def norm_pro():
+            nonlocal cur, pending
+            if pending:
+                d = dict(prologue=PRO_RESID_NORM, act=xs[cur], psum=self.psum, x_out=xs[1 - cur], lda=H)
+                cur = 1 - cur
+                pending = False
+            else:
+                d = dict(prologue=PRO_NORM, act=xs[cur], lda=H)
+            return d
+
+        for li, L in enumerate(self.layers):
+            pro = norm_pro()
+            a = self._gemv(bits=sp.bits, epilogue=EPI_ROPE_KV, N=(self.nq + 2 * self.nkv) * hd, K=H,
+                           group_size=sp.group_size, weight=L.qkv_w, scales=L.qkv_s, gamma=L.in_norm,
+                           head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv, max_seq=self.S,
+                           rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, q_out=self.q,
+                           k_cache=self.k_cache[li], v_cache=self.v_cache[li], **pro)
+            calls.append(("gemv", a))
+            gemv_args.append(a)
+            at = AttentionArgs(q=self.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
+                               v_cache=self.v_cache[li].data_ptr(), out=self.attn.data_ptr(),
+                               part_o=self.part_o.data_ptr(), part_ml=self.part_ml.data_ptr(),
+                               counters=self.attn_counters.data_ptr(), pos=self.pos.data_ptr(), batch=B,
+                               n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
+                               n_split=self.n_split, pdl=self.pdl)
+            calls.append(("attn", at))
+            epi = dict(epilogue=EPI_F32, out_f32=self.psum) if tp else \
+                dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
+            a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.nq * hd, group_size=sp.group_size,
+                           weight=L.o_w, scales=L.o_s, act=self.attn, lda=self.nq * hd, ldo=H, **epi)
+            calls.append(("gemv", a))
+            gemv_args.append(a)
+            if tp:
+                calls.append(("allreduce", self.psum))
+                pending = True
+            pro = norm_pro()
+            a = self._gemv(bits=sp.bits, epilogue=EPI_SWIGLU, N=2 * self.inter, K=H, group_size=sp.group_size,
+                           weight=L.gu_w, scales=L.gu_s, gamma=L.post_norm, out=self.act, ldo=self.inter, **pro)
+            calls.append(("gemv", a))
+            gemv_args.append(a)
+            epi = dict(epilogue=EPI_F32, out_f32=self.psum) if tp else \
+                dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
+            a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
+                           weight=L.d_w, scales=L.d_s, act=self.act, lda=self.inter, ldo=H, **epi)
+            calls.append(("gemv", a))
+            gemv_args.append(a)
+            if tp:
+                calls.append(("allreduce", self.psum))
+                pending = True
+        pro = norm_pro()
+        a = self._gemv(bits=16, epilogue=EPI_ARGMAX, N=self.vshard, K=H, group_size=H, weight=self.lm_head,
+                       gamma=self.final_norm, out=self.logits, ldo=self.vshard, argmax_keys=self.keys,
+                       argmax_offset=self.tp_rank * self.vshard, **pro)
+        calls.append(("gemv", a))
+        gemv_args.append(a)
+        if tp:
+            calls.append(("allreduce_max", self.keys))
+        calls.append(("sample", None))
+        # one workspace shared by the sequential GEMVs of a step
+        need = max(int(nat.lib().lw_fused_gemv_workspace_size(ctypes.byref(a))) for a in gemv_args)
+        self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        for a in gemv_args:
+            a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        self.calls = calls
+        self.x_in = self.x   # layer 0 reads the residual stream from self.x; sample writes it there
+
+    # -------------------------------------------------------------- execution
+    def _enqueue_step(self, sample: bool = True):
+        lib = nat.lib()
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        for kind, a in self.calls:
+            if kind == "sample" and not sample:
+                continue
+            if kind == "gemv":
+                nat.check("lw_fused_gemv", lib.lw_fused_gemv(ctypes.byref(a), s))
+            elif kind == "attn":
+                nat.check("lw_attention_decode", lib.lw_attention_decode(ctypes.byref(a), s))
+            elif kind == "allreduce":
+                torch.distributed.all_reduce(a, group=self.tp_group)
+            elif kind == "allreduce_max":
+                torch.distributed.all_reduce(a, op=torch.distributed.ReduceOp.MAX, group=self.tp_group)
+            elif kind == "sample":
+                nat.check("lw_sample_tokens", lib.lw_sample_tokens(
+                    self.tokens.data_ptr(), self.keys.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
+                    self.pos.data_ptr(), self.done.data_ptr(), self.B, self.spec.hidden, self.pdl, s))
+
+    def kernels_per_step(self) -> int:
+        return sum(1 for k, _ in self.calls if k in ("gemv", "attn", "sample"))
+
+    def start(self, prompt: torch.Tensor, forced: torch.Tensor | None = None):
+        """Load a prompt (int [B, P]) and optional further forced tokens; position 0."""
+        B, P = prompt.shape
+        assert B == self.B
+        self.tokens.fill_(-1)
+        self.tokens[:P] = prompt.T.to(device=self.device, dtype=torch.int32)
+        if forced is not None:
+            self.tokens[P:P + forced.shape[1]] = forced.T.to(device=self.device, dtype=torch.int32)
+        self.pos.zero_()
+        self.keys.zero_()
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        nat.call("lw_embed_tokens", self.tokens.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
+                 self.pos.data_ptr(), self.B, self.spec.hidden, 0, s)
+        self.host_pos = 0
+        self.prompt_len = P
+
+    def capture(self):
+        """Capture one decode step as a CUDA graph (after one eager step to warm up)."""
+        if self.graph is not None:
+            return
+        saved = (self.tokens.clone(), self.pos.clone(), self.x_in.clone(), self.keys.clone())
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._enqueue_step()
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            self._enqueue_step()
+        torch.cuda.synchronize(self.device)
+        self.tokens.copy_(saved[0])
+        self.pos.copy_(saved[1])
+        self.x_in.copy_(saved[2])
+        self.keys.copy_(saved[3])
+        self.graph = g
+
+    def step(self, n: int = 1, graph: bool = True):
+        for _ in range(n):
+            if graph and self.graph is not None:
+                self.graph.replay()
+            else:
+                self._enqueue_step()
+            self.host_pos += 1
+
+    def step_logits(self):
+        """Eager step up to the logits (no token pick); pick_next() finishes it."""
+        self._enqueue_step(sample=False)
+
+    def pick_next(self):
+        """Pick the next token (forced table entry or argmax), embed it, advance."""
+        for kind, a in self.calls:
+            if kind == "sample":
+                s = torch.cuda.current_stream(self.device).cuda_stream
+                nat.check("lw_sample_tokens", nat.lib().lw_sample_tokens(
+                    self.tokens.data_ptr(), self.keys.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
+                    self.pos.data_ptr(), self.done.data_ptr(), self.B, self.spec.hidden, self.pdl, s))
+        self.host_pos += 1
+
+    def generated(self, new_tokens: int) -> torch.Tensor:
+        P = self.prompt_len
+        return self.tokens[P:P + new_tokens].T
+
+
+# ------------------------------------------------------------------ HF model glue
 
 def supports(model) -> bool:
-    return False
+    """True for LlamaForCausalLM-style models whose linears are liteweight QuantLinear."""
+    from liteweight_b200.quantlinear import QuantLinear
+    try:
+        inner = model.model
+        layer = inner.layers[0]
+        qls = [layer.self_attn.q_proj, layer.self_attn.k_proj, layer.self_attn.v_proj, layer.self_attn.o_proj,
+               layer.mlp.gate_proj, layer.mlp.up_proj, layer.mlp.down_proj]
+    except (AttributeError, IndexError, TypeError):
+        return False
+    if not all(isinstance(m, QuantLinear) and m.bias is None for m in qls):
+        return False
+    cfg = getattr(model, "config", None)
+    return cfg is not None and getattr(cfg, "hidden_act", "silu") == "silu" and torch.cuda.is_available() \
+        and next(model.parameters()).is_cuda
+
+
+def spec_from_hf(model) -> LlamaSpec:
+    cfg = model.config
+    layer = model.model.layers[0]
+    q = layer.self_attn.q_proj
+    hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+    return LlamaSpec(hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_layers=cfg.num_hidden_layers,
+                     n_heads=cfg.num_attention_heads, n_kv_heads=cfg.num_key_value_heads, head_dim=hd,
+                     vocab=cfg.vocab_size, bits=q.bits, group_size=q.group_size, eps=cfg.rms_norm_eps)
+
+
+def layers_from_hf(model) -> list:
+    out = []
+    for layer in model.model.layers:
+        a, m = layer.self_attn, layer.mlp
+        out.append(LayerWeights(
+            q=(a.q_proj.qweight, a.q_proj.scales), k=(a.k_proj.qweight, a.k_proj.scales),
+            v=(a.v_proj.qweight, a.v_proj.scales), o=(a.o_proj.qweight, a.o_proj.scales),
+            gate=(m.gate_proj.qweight, m.gate_proj.scales), up=(m.up_proj.qweight, m.up_proj.scales),
+            down=(m.down_proj.qweight, m.down_proj.scales),
+            in_norm=layer.input_layernorm.weight.data, post_norm=layer.post_attention_layernorm.weight.data))
+    return out
+
+
+def engine_from_hf(model, batch: int, max_seq: int, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
+                   pdl: bool = True) -> DecodeEngine:
+    spec = spec_from_hf(model)
+    dev = next(model.parameters()).device
+    packed = [PackedLayer(lw, spec, tp_rank, tp_size, dev) for lw in layers_from_hf(model)]
+    # the model's own rotary embedding: exact HF cos/sin (default or llama3 scaled)
+    rot = model.model.rotary_emb
+    x = torch.zeros(1, 1, spec.hidden, dtype=torch.float16, device=dev)
+    with torch.no_grad():
+        cos, sin = rot(x, torch.arange(max_seq, device=dev)[None])
+    lm_w = model.lm_head.weight.data
+    tied = lm_w.data_ptr() == model.model.embed_tokens.weight.data_ptr()
+    return DecodeEngine(spec, packed, model.model.embed_tokens.weight.data, model.model.norm.weight.data,
+                        None if tied else lm_w, cos[0], sin[0], batch, max_seq, dev, tp_rank, tp_size, tp_group, pdl)
+
+
+def build_engine(spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
+                 lm_head: torch.Tensor | None, inv_freq: torch.Tensor, batch: int, max_seq: int, device,
+                 attention_scaling: float = 1.0, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
+                 pdl: bool = True) -> DecodeEngine:
+    """Engine from unsharded LayerWeights (liteweight-format tensors, any device)."""
+    packed = [PackedLayer(lw, spec, tp_rank, tp_size, device) for lw in layers]
+    cos, sin = rope_tables(inv_freq, max_seq, attention_scaling, device)
+    return DecodeEngine(spec, packed, embed, final_norm, lm_head, cos, sin, batch, max_seq, device, tp_rank,
+                        tp_size, tp_group, pdl)
+
+
+def synthetic_layers(spec: LlamaSpec, device, seed: int = 0, std: float = 0.02) -> list:
+    """Random-init layers (W ~ N(0, std) quantized with liteweight's RTN on the
+    device, one linear at a time), norms 1 + N(0, 0.1): stands in for a
+    checkpoint of the given architecture."""
+    from liteweight_b200.quantize import quantize_int4, quantize_int8
+    quant = quantize_int4 if spec.bits == 4 else quantize_int8
+    g = torch.Generator(device=device).manual_seed(seed)
+    layers = []
+    for _ in range(spec.n_layers):
+        lin = {}
+        for name, n, k in spec.linear_shapes():
+            w = torch.randn(n, k, device=device, generator=g, dtype=torch.float32).mul_(std).half()
+            lin[name] = quant(w, spec.group_size)
+            del w
+        norms = [(1.0 + 0.1 * torch.randn(spec.hidden, device=device, generator=g)).half() for _ in range(2)]
+        layers.append(LayerWeights(in_norm=norms[0], post_norm=norms[1], **lin))
+    return layers
+
+
+_ENGINES: dict = {}
+
+
+def generate_ids(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: float = 0.0,
+                 top_k: int | None = None, eos_ids: set | None = None) -> list:
+    """Greedy (or sampled) continuation of input_ids [B, P]; returns a list of
+    token lists (each cut before its first EOS), as liteweight/generate.py:106-124."""
+    from liteweight_b200.generate import _sample
+    B, P = input_ids.shape
+    need = P + max_new_tokens
+    key = (id(model), B)
+    eng = _ENGINES.get(key)
+    if eng is None or eng.S < need:
+        eng = engine_from_hf(model, batch=B, max_seq=max(need, 256))
+        _ENGINES[key] = eng
+    eng.start(input_ids)
+    if temperature == 0.0:
+        eng.capture()
+        eng.step(P + max_new_tokens - 1)
+        out = eng.generated(max_new_tokens).cpu()
+    else:
+        # sampling (generate.py:54-59): same kernels; each new token is drawn by
+        # torch on the device from the logits and forced into the token table
+        for p in range(P + max_new_tokens - 1):
+            eng.step_logits()
+            if p >= P - 1:
+                eng.tokens[p + 1] = _sample(eng.logits.float(), temperature, top_k).to(torch.int32)
+            eng.pick_next()
+        out = eng.generated(max_new_tokens).cpu()
+    res = []
+    for row in out.tolist():
+        seq = []
+        for t in row:
+            if eos_ids and t in eos_ids:
+                break
+            seq.append(t)
+        res.append(seq)
+    return res

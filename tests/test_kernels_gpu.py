@@ -322,4 +322,17 @@ def test_split_tiles_with_workspace(bits, M, K, N):
         check_rows(o, ref, f"bits={bits} ws={wsb}")
     assert torch.equal(outs[0], outs[1])
     # the per-tile counters at the head of the workspace are back to zero
-    assert int(ws[: 4 * ((N + 15) // 16)].count_nonzero()) == 0
+    assert int(ws[: 64 * 1024].count_nonzero()) == 0
+
+
+def test_workspace_reuse_across_shapes():
+    """One workspace serves calls of different shapes in any order (the counter
+    region never overlaps the slots of a previous call)."""
+    k = kern()
+    rng = np.random.default_rng(17)
+    for bits, M, K, N in [(8, 16, 2048, 2048), (8, 1, 2048, 8192), (4, 3, 8192, 256), (4, 1, 4096, 28672),
+                          (8, 2, 2048, 512)]:
+        q, s = quantized(N, K, 128, bits, seed=N)
+        act = rng.standard_normal((M, K)).astype(np.float16)
+        got = run_quant(act, q, s, 128, bits)
+        check_rows(got, oq.packed_matmul(act, q, s, 128, bits), f"reuse int{bits} {M}x{K}x{N}")
