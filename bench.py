@@ -1,20 +1,28 @@
 """Benchmark of liteweight_b200's hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemv]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|gemv] [--model 8b|1b|70b] [--batch B]
 
 Prints ONE JSON line (rank 0). Workloads:
 
+* ``decode`` (default) - greedy decode of a random-init Llama-3-8B
+  architecture, INT4 group-128 weight-only (the reference's format), batch 1,
+  512 uniform-random prompt ids, fp16 KV cache, tensor parallel over the N
+  ranks (one process per GPU, NCCL all-reduce). One step = one decode token
+  for the batch (graph replay of the fused decode step). Metric: decode
+  tokens/s of the whole job (``scaling: strong``: the model and batch are
+  fixed as N grows). ``--model 1b`` (INT8, prompt 128) and ``--model 70b``
+  (INT4, context 2048) select the other decode configurations.
 * ``gemv`` - the dequant GEMV of the Llama-3.2-1B linear shapes (K x N =
   2048x2048, 2048x512, 2048x8192, 8192x2048), INT4 and INT8 with group size
-  128, one activation row (M = 1): one step = those 8 GEMVs, each on its own
-  weight copy from a rotating set larger than L2 (so every step reads its
-  weights from HBM). Metric: algorithmic GB/s (weights + fp16 scales +
-  activation + output, divided by time). Multi-GPU: independent replicas
-  (``scaling: weak``). A per-M sweep (M = 1..256) is reported beside it.
+  128, M = 1: one step = those 8 GEMVs, each on its own weight copy from a
+  rotating set larger than twice the L2. Metric: algorithmic GB/s (weights +
+  fp16 scales + activation + output over time). Multi-GPU: independent
+  replicas (``scaling: weak``). A per-M sweep (M = 1..256) is reported beside it.
 
 ``--impl reference`` times the reference's CPU path for the same workload
 (dequantize the packed weights, fp32 matmul, fp16 result - restated by the
-numpy oracle) on the host cores, rank 0 only.
+numpy oracle) on the host cores, rank 0 only, on a bounded sample.
 """
 
 from __future__ import annotations
@@ -310,6 +318,174 @@ class GemvWorkload:
         return out
 
 
+# ----------------------------------------------------------------- decode workload
+
+MODELS = {
+    "8b": dict(arch="LLAMA_3_8B", bits=4, prompt=512, new=256, name="Llama-3-8B"),
+    "1b": dict(arch="LLAMA_3_2_1B", bits=8, prompt=128, new=256, name="Llama-3.2-1B"),
+    "70b": dict(arch="LLAMA_3_70B", bits=4, prompt=2048, new=256, name="Llama-3-70B"),
+}
+
+
+class DecodeWorkload:
+    unit = "tokens/s"
+
+    def __init__(self, device, dist: "Dist", model: str, batch: int, extra_steps: int):
+        import torch
+        from liteweight_b200 import engine as E
+        cfg = MODELS[model]
+        self.torch, self.E, self.dev, self.cfg = torch, E, device, cfg
+        self.spec = E.LlamaSpec(**getattr(E, cfg["arch"]), bits=cfg["bits"], group_size=GROUP)
+        self.B, self.P, self.T = batch, cfg["prompt"], cfg["new"]
+        self.tp, self.rank = dist.world, dist.rank
+        self.metric = (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only, batch {batch}, "
+                       f"prompt {self.P}, greedy, TP{self.tp})")
+        max_seq = self.P + max(self.T, extra_steps) + 1
+        g = torch.Generator(device=device).manual_seed(20251201)
+        spec = self.spec
+        packed = []
+        for li in range(spec.n_layers):
+            # identical full layer on every rank (same seed), then this rank's shard
+            lw = E.synthetic_layers(E.LlamaSpec(**{**spec.__dict__, "n_layers": 1}), device, seed=1000 + li)[0]
+            packed.append(E.PackedLayer(lw, spec, self.rank, self.tp, device))
+            del lw
+        embed = (torch.randn(spec.vocab, spec.hidden, device=device, generator=g) * 0.02).half()
+        norm = (1.0 + 0.1 * torch.randn(spec.hidden, device=device, generator=g)).half()
+        cos, sin = E.rope_tables(E.default_inv_freq(spec.head_dim, spec.rope_theta), max_seq, 1.0, device)
+        group = None
+        if self.tp > 1:
+            import torch.distributed as tdist
+            group = tdist.group.WORLD
+        self.eng = E.DecodeEngine(spec, packed, embed, norm, None, cos, sin, batch, max_seq, device, self.rank,
+                                  self.tp, group)
+        gp = torch.Generator().manual_seed(7)
+        self.prompt = torch.randint(0, spec.vocab, (batch, self.P), generator=gp)
+        torch.cuda.synchronize()
+
+    def prefill(self):
+        """Load the prompt and run it through the step graph up to the first decode step."""
+        self.eng.start(self.prompt)
+        self.eng.capture()
+        self.eng.step(self.P - 1)
+
+    def step(self, it: int):
+        self.eng.step(1)
+
+    def context(self) -> int:
+        return self.eng.host_pos + 1
+
+    def bytes_per_step(self, ctx: int) -> int:
+        """Weight bytes (this rank's shard, incl. fp16 lm_head shard) + KV bytes read."""
+        sp = self.spec
+        return sp.weight_bytes_per_token() // self.tp + self.B * sp.kv_bytes_per_position() * ctx // self.tp
+
+    def kernel_stats(self, ctx: int) -> dict:
+        """Per kernel class: one step's launches captured alone in a graph,
+        replayed and timed with CUDA events (avg duration per launch)."""
+        torch, sp, eng = self.torch, self.spec, self.eng
+        H, I, hd = sp.hidden, sp.inter // self.tp, sp.head_dim
+        nq, nkv = sp.n_heads // self.tp, sp.n_kv_heads // self.tp
+
+        def wbytes(n, k):
+            return n * k * sp.bits // 8 + 2 * n * (k // GROUP)
+        per_launch = {
+            "qkv": wbytes((nq + 2 * nkv) * hd, H) + 2 * self.B * H,
+            "attn": self.B * 2 * nkv * ctx * hd * 2,
+            "o": wbytes(H, nq * hd) + 2 * self.B * nq * hd,
+            "gu": wbytes(2 * I, H) + 2 * self.B * H,
+            "down": wbytes(H, I) + 2 * self.B * I,
+            "lm_head": (sp.vocab // self.tp) * H * 2 + 2 * self.B * H,
+        }
+        out = {}
+        for name, b in per_launch.items():
+            launches = sum(1 for _, _, n in eng.calls if n == name)
+            g = capture_graph(lambda name=name: eng.enqueue_only(name))
+            ms = time_graph(g, 10) / launches
+            out[name] = {"launches": launches, "bytes": b, "us": round(ms * 1e3, 3),
+                         "GB/s": round(b / (ms * 1e-3) / 1e9, 1)}
+            del g
+        return out
+
+    def e2e(self) -> dict:
+        """The public decode call with host buffers: prompt ids from pinned host
+        memory, prefill + T greedy tokens, generated ids copied back."""
+        torch = self.torch
+        host_ids = self.prompt.to(torch.int32).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        ids = self.eng.generate(host_ids, self.T)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        return {"ms": ms, "tokens": self.B * self.T, "h2d_bytes_per_step": host_ids.numel() * 4,
+                "d2h_bytes_per_step": ids.numel() * 4, "ids": ids}
+
+
+class CpuDecode:
+    """The reference's CPU path for one decode step, on a bounded sample: the
+    oracle's QuantLinear arithmetic (dequantize the packed weights every call,
+    fp32 matmul; liteweight/quantize.py:30-60, :102-135) for the seven linears
+    of one layer at batch 1, split by output rows over the host cores, plus
+    the fp16 lm_head; per-token time = layers x layer time + lm_head time
+    (norms, RoPE and attention at batch 1 are <1% of the arithmetic and left
+    out)."""
+
+    def __init__(self, model: str, batch: int = 1):
+        from liteweight_b200 import engine as E
+        from oracle import quant as oq
+        cfg = MODELS[model]
+        self.spec = E.LlamaSpec(**getattr(E, cfg["arch"]), bits=cfg["bits"], group_size=GROUP)
+        self.oq, self.B = oq, batch
+        rng = np.random.default_rng(3)
+        self.lin = []
+        for name, n, k in self.spec.linear_shapes():
+            if self.spec.bits == 4:
+                q = rng.integers(0, 256, (n, k // 2), dtype=np.uint8)
+            else:
+                q = rng.integers(-127, 128, (n, k), dtype=np.int8)
+            s = (rng.random((n, k // GROUP)) * 2e-3 + 1e-4).astype(np.float16)
+            self.lin.append((name, q, s, rng.standard_normal((batch, k)).astype(np.float16)))
+        self.cores = os.cpu_count() or 1
+        self.pool = ThreadPoolExecutor(self.cores)
+        self.lm_rows = 8192
+        self.lm = (rng.standard_normal((self.lm_rows, self.spec.hidden)) * 0.02).astype(np.float16)
+        self.h = rng.standard_normal((batch, self.spec.hidden)).astype(np.float16)
+
+    def _rows(self, fn, n):
+        blocks = np.array_split(np.arange(n), self.cores)
+        return np.concatenate(list(self.pool.map(fn, blocks)), axis=1)
+
+    def linear(self, i: int) -> float:
+        name, q, s, act = self.lin[i]
+        t = time.perf_counter()
+        self._rows(lambda r: self.oq.packed_matmul(act, q[r], s[r], GROUP, self.spec.bits), q.shape[0])
+        return time.perf_counter() - t
+
+    def lm_head_seconds(self) -> float:
+        t = time.perf_counter()
+        self._rows(lambda r: (self.h.astype(np.float32) @ self.lm[r].astype(np.float32).T).astype(np.float16),
+                   self.lm_rows)
+        return (time.perf_counter() - t) * self.spec.vocab / self.lm_rows
+
+    def measure(self, min_seconds: float = 10.0) -> dict:
+        t0 = time.perf_counter()
+        sums = [0.0] * len(self.lin)
+        n = 0
+        while n == 0 or time.perf_counter() - t0 < min_seconds:
+            for i in range(len(self.lin)):
+                sums[i] += self.linear(i)
+            n += 1
+        layer = sum(sums) / n
+        lm = self.lm_head_seconds()
+        tok_s = self.B / (self.spec.n_layers * layer + lm)
+        return {"value": round(tok_s, 5), "unit": "tokens/s", "cores": self.cores, "kind": "port",
+                "layer_seconds": round(layer, 3), "lm_head_seconds": round(lm, 3),
+                "sample": f"{n} pass(es) over the 7 quantized linears of one layer (dequantize + fp32 matmul, "
+                          f"rows split over {self.cores} threads) + the fp16 lm_head on {self.lm_rows} vocab rows "
+                          f"scaled to {self.spec.vocab}; per token = {self.spec.n_layers} layers + lm_head"}
+
+
 # ----------------------------------------------------------------- CPU baseline (reference path)
 
 class CpuGemv:
@@ -377,7 +553,7 @@ def smi_gpu_id(local_rank: int) -> str:
     return vis[local_rank] if local_rank < len(vis) else str(local_rank)
 
 
-def run_reference(args, dist: Dist):
+def run_reference_gemv(args, dist: Dist):
     if dist.rank != 0:
         return
     cpu = CpuGemv()
@@ -398,7 +574,7 @@ def run_reference(args, dist: Dist):
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, dist: Dist):
+def run_gemv(args, dist: Dist):
     import torch
     from liteweight_b200 import _native as nat
     from liteweight_b200 import build as lwbuild
@@ -468,21 +644,143 @@ def run_ours(args, dist: Dist):
     dist.close()
 
 
+def run_decode(args, dist: Dist):
+    import torch
+    from liteweight_b200 import _native as nat
+    from liteweight_b200 import build as lwbuild
+    from liteweight_b200.perf import b200_measured
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the product has no CPU path)")
+    dev = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(dev)
+    dist.init("nccl")
+    lwbuild.build()
+    nat.lib()
+    wl = DecodeWorkload(dev, dist, args.model, args.batch, args.warmup + args.steps)
+    if dist.world > 1:   # NCCL communicator up before graph capture
+        t = torch.zeros(1, device=dev)
+        dist.pg.all_reduce(t)
+        torch.cuda.synchronize()
+    wl.prefill()
+    for it in range(args.warmup):
+        wl.step(it)
+    torch.cuda.synchronize()
+    dist.barrier(dev)
+    torch.cuda.synchronize()
+    ctx0 = wl.context()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(smi_gpu_id(dist.local_rank)) as clk:
+        e0.record()
+        for it in range(args.steps):
+            wl.step(it)
+        e1.record()
+        torch.cuda.synchronize()
+    dist.barrier(dev)
+    ms = e0.elapsed_time(e1)
+    ms_max = dist.max(ms, dev)
+    ctx_mid = ctx0 + args.steps // 2
+    value = wl.B * args.steps / (ms_max * 1e-3)
+    step_ms = ms_max / args.steps
+    peak, peak_src = b200_measured(ROOT / "MEASURED_PEAKS.json")
+    # per-kernel timing (kernel classes replayed alone), then the end-to-end call
+    kstats = wl.kernel_stats(ctx_mid)
+    dom = max(kstats, key=lambda k: kstats[k]["us"] * kstats[k]["launches"])
+    d = kstats[dom]
+    achieved = d["GB/s"]
+    roofline = {"bound": "hbm", "kernel": f"fused GEMV {dom}" if dom != "attn" else "attention",
+                "achieved": achieved, "peak": peak.peak_mem_bandwidth_gbs, "peak_source": peak_src, "unit": "GB/s",
+                "frac": round(achieved / peak.peak_mem_bandwidth_gbs, 4), "algorithmic_bytes_per_launch": d["bytes"],
+                "avg_launch_us": d["us"], "traffic": traffic_for(f"decode_{args.model}_{dom}")}
+    bstep = wl.bytes_per_step(ctx_mid)
+    decode_roofline = {"bytes_per_step_per_gpu": bstep, "achieved_GBs_per_gpu": round(bstep / (step_ms * 1e-3) / 1e9, 1),
+                       "frac": round(bstep / (step_ms * 1e-3) / 1e9 / peak.peak_mem_bandwidth_gbs, 4),
+                       "roofline_tokens_per_s": round(wl.B * peak.peak_mem_bandwidth_gbs * 1e9 / bstep, 1),
+                       "context_mid": ctx_mid}
+    e = wl.e2e()
+    e2e_ms = dist.max(e["ms"], dev)
+    e2e = {"value": round(e["tokens"] / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+           "h2d_bytes_per_step": e["h2d_bytes_per_step"], "d2h_bytes_per_step": e["d2h_bytes_per_step"],
+           "step": f"one call = prompt {wl.P} ids in, prefill + {wl.T} greedy tokens, ids out",
+           "ms_per_call": round(e2e_ms, 3)}
+    clocks = clk.summary()
+    launches = args.steps * wl.eng.kernels_per_step()
+    if dist.rank != 0:
+        wl.eng.graph = None
+        dist.close()
+        return
+    cpu = CpuDecode(args.model, wl.B).measure() if dist.world == 1 else None
+    line = {"metric": wl.metric, "value": round(value, 2), "unit": "tokens/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": f"int{wl.spec.bits} weights x fp16, fp32 acc",
+            "data": "synthetic (random-init weights, uniform random prompt ids)",
+            "config": {"workload": f"decode {MODELS[args.model]['name']} INT{wl.spec.bits} G{GROUP}",
+                       "model": MODELS[args.model]["name"], "global_batch": wl.B, "prompt": wl.P,
+                       "new_tokens": wl.T, "seq_len": wl.P + wl.T, "parallelism": f"tp{dist.world}",
+                       "l2": f"inputs larger than L2 ({wl.spec.weight_bytes_per_token() / dist.world / 1e9:.2f} GB "
+                             "of weights per GPU per step)"},
+            "roofline": roofline, "decode_roofline": decode_roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": int(launches), "kernels": {k: {kk: v[kk] for kk in ("launches", "us", "GB/s")}
+                                                       for k, v in kstats.items()},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    wl.eng.graph = None
+    dist.close()
+
+
+def run_reference_decode(args, dist: Dist):
+    """The reference's CPU path on the box's cores: every step is one of the 7
+    quantized linears of a layer (rotating), dequantized and matmul'd as the
+    reference does; tokens/s = batch / (layers x summed linear times + lm_head)."""
+    if dist.rank != 0:
+        return
+    cpu = CpuDecode(args.model, args.batch)
+    for i in range(min(args.warmup, 7)):
+        cpu.linear(i % 7)
+    times = [[] for _ in range(7)]
+    t0 = time.perf_counter()
+    for it in range(args.steps):
+        times[it % 7].append(cpu.linear(it % 7))
+    wall = time.perf_counter() - t0
+    layer = sum(sum(t) / len(t) for t in times if t) * (7 / max(1, sum(1 for t in times if t)))
+    lm = cpu.lm_head_seconds()
+    tok_s = args.batch / (cpu.spec.n_layers * layer + lm)
+    cfg = MODELS[args.model]
+    line = {"impl": "reference", "metric": (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only, "
+                                            f"batch {args.batch}, prompt {cfg['prompt']}, greedy, TP{args.gpus})"),
+            "value": round(tok_s, 5), "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": f"int{cfg['bits']} codes, fp32 acc",
+            "data": "synthetic",
+            "config": {"workload": f"decode {cfg['name']} INT{cfg['bits']} G{GROUP}", "global_batch": args.batch},
+            "cpu_baseline": {"value": round(tok_s, 5), "unit": "tokens/s", "cores": cpu.cores, "kind": "port",
+                             "sample": f"{args.steps} linears (rotating over a layer's 7) + fp16 lm_head sample, "
+                                       f"extrapolated to {cpu.spec.n_layers} layers"},
+            "e2e": {"value": round(tok_s, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemv"], default="gemv")
+    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
+    ap.add_argument("--model", choices=sorted(MODELS), default="8b")
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-sweep", action="store_true")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 200 if args.impl == "ours" else 21
+    if args.warmup is None:
+        args.warmup = 10 if args.impl == "ours" else 3
     args.warmup = max(args.warmup, 3)
     dist = Dist()
-    if args.impl == "reference":
-        run_reference(args, dist)
+    if args.workload == "decode":
+        (run_reference_decode if args.impl == "reference" else run_decode)(args, dist)
     else:
-        run_ours(args, dist)
+        (run_reference_gemv if args.impl == "reference" else run_gemv)(args, dist)
 
 
 if __name__ == "__main__":

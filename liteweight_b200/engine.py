@@ -293,7 +293,7 @@ class DecodeEngine:
                            head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv, max_seq=self.S,
                            rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, q_out=self.q,
                            k_cache=self.k_cache[li], v_cache=self.v_cache[li], **pro)
-            calls.append(("gemv", a))
+            calls.append(("gemv", a, "qkv"))
             gemv_args.append(a)
             at = AttentionArgs(q=self.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
                                v_cache=self.v_cache[li].data_ptr(), out=self.attn.data_ptr(),
@@ -301,39 +301,39 @@ class DecodeEngine:
                                counters=self.attn_counters.data_ptr(), pos=self.pos.data_ptr(), batch=B,
                                n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
                                n_split=self.n_split, pdl=self.pdl)
-            calls.append(("attn", at))
+            calls.append(("attn", at, "attn"))
             epi = dict(epilogue=EPI_F32, out_f32=self.psum) if tp else \
                 dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
             a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.nq * hd, group_size=sp.group_size,
                            weight=L.o_w, scales=L.o_s, act=self.attn, lda=self.nq * hd, ldo=H, **epi)
-            calls.append(("gemv", a))
+            calls.append(("gemv", a, "o"))
             gemv_args.append(a)
             if tp:
-                calls.append(("allreduce", self.psum))
+                calls.append(("allreduce", self.psum, "allreduce"))
                 pending = True
             pro = norm_pro()
             a = self._gemv(bits=sp.bits, epilogue=EPI_SWIGLU, N=2 * self.inter, K=H, group_size=sp.group_size,
                            weight=L.gu_w, scales=L.gu_s, gamma=L.post_norm, out=self.act, ldo=self.inter, **pro)
-            calls.append(("gemv", a))
+            calls.append(("gemv", a, "gu"))
             gemv_args.append(a)
             epi = dict(epilogue=EPI_F32, out_f32=self.psum) if tp else \
                 dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
             a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
                            weight=L.d_w, scales=L.d_s, act=self.act, lda=self.inter, ldo=H, **epi)
-            calls.append(("gemv", a))
+            calls.append(("gemv", a, "down"))
             gemv_args.append(a)
             if tp:
-                calls.append(("allreduce", self.psum))
+                calls.append(("allreduce", self.psum, "allreduce"))
                 pending = True
         pro = norm_pro()
         a = self._gemv(bits=16, epilogue=EPI_ARGMAX, N=self.vshard, K=H, group_size=H, weight=self.lm_head,
                        gamma=self.final_norm, out=self.logits, ldo=self.vshard, argmax_keys=self.keys,
                        argmax_offset=self.tp_rank * self.vshard, **pro)
-        calls.append(("gemv", a))
+        calls.append(("gemv", a, "lm_head"))
         gemv_args.append(a)
         if tp:
-            calls.append(("allreduce_max", self.keys))
-        calls.append(("sample", None))
+            calls.append(("allreduce_max", self.keys, "allreduce"))
+        calls.append(("sample", None, "sample"))
         # one workspace shared by the sequential GEMVs of a step
         need = max(int(nat.lib().lw_fused_gemv_workspace_size(ctypes.byref(a))) for a in gemv_args)
         self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
@@ -346,7 +346,7 @@ class DecodeEngine:
     def _enqueue_step(self, sample: bool = True):
         lib = nat.lib()
         s = torch.cuda.current_stream(self.device).cuda_stream
-        for kind, a in self.calls:
+        for kind, a, _name in self.calls:
             if kind == "sample" and not sample:
                 continue
             if kind == "gemv":
@@ -363,7 +363,29 @@ class DecodeEngine:
                     self.pos.data_ptr(), self.done.data_ptr(), self.B, self.spec.hidden, self.pdl, s))
 
     def kernels_per_step(self) -> int:
-        return sum(1 for k, _ in self.calls if k in ("gemv", "attn", "sample"))
+        return sum(1 for k, _, _n in self.calls if k in ("gemv", "attn", "sample"))
+
+    def enqueue_only(self, name: str):
+        """Enqueue just the kernels of one class (qkv, attn, o, gu, down, lm_head)
+        of a step, for per-kernel timing; the outputs are scratch."""
+        lib = nat.lib()
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        for kind, a, n in self.calls:
+            if n != name:
+                continue
+            if kind == "gemv":
+                nat.check("lw_fused_gemv", lib.lw_fused_gemv(ctypes.byref(a), s))
+            elif kind == "attn":
+                nat.check("lw_attention_decode", lib.lw_attention_decode(ctypes.byref(a), s))
+
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+        """Greedy continuation of input_ids [B, P] (host or device); returns the
+        new tokens [B, max_new_tokens] on the host. One graph replay per step,
+        one device->host copy at the end."""
+        self.start(input_ids)
+        self.capture()
+        self.step(input_ids.shape[1] + max_new_tokens - 1)
+        return self.generated(max_new_tokens).to("cpu")
 
     def start(self, prompt: torch.Tensor, forced: torch.Tensor | None = None):
         """Load a prompt (int [B, P]) and optional further forced tokens; position 0."""
@@ -415,7 +437,7 @@ class DecodeEngine:
 
     def pick_next(self):
         """Pick the next token (forced table entry or argmax), embed it, advance."""
-        for kind, a in self.calls:
+        for kind, a, _name in self.calls:
             if kind == "sample":
                 s = torch.cuda.current_stream(self.device).cuda_stream
                 nat.check("lw_sample_tokens", nat.lib().lw_sample_tokens(
@@ -531,12 +553,10 @@ def generate_ids(model, input_ids: torch.Tensor, max_new_tokens: int, temperatur
     if eng is None or eng.S < need:
         eng = engine_from_hf(model, batch=B, max_seq=max(need, 256))
         _ENGINES[key] = eng
-    eng.start(input_ids)
     if temperature == 0.0:
-        eng.capture()
-        eng.step(P + max_new_tokens - 1)
-        out = eng.generated(max_new_tokens).cpu()
+        out = eng.generate(input_ids, max_new_tokens)
     else:
+        eng.start(input_ids)
         # sampling (generate.py:54-59): same kernels; each new token is drawn by
         # torch on the device from the logits and forced into the token table
         for p in range(P + max_new_tokens - 1):
