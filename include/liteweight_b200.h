@@ -165,7 +165,7 @@ size_t lw_fused_gemv_workspace_size(const lw_fused_gemv_args* args);
 /* Split-KV GQA attention of one query per sequence over cache positions
  * 0..*pos (modeling_llama.py:197-222 with repeat_kv): scores scaled by
  * head_dim^-0.5, fp32 softmax, fp16 output [batch][n_q_heads*head_dim].
- * n_split > 1 needs part_o (fp32 [batch][n_q_heads][n_split][head_dim]),
+ * n_split <= 64; n_split > 1 needs part_o (fp32 [batch][n_q_heads][n_split][head_dim]),
  * part_ml (fp32 [batch][n_q_heads][n_split][2]) and counters (int
  * [batch][n_kv_heads], zero before first use, kept zero). */
 typedef struct {

@@ -37,15 +37,21 @@ struct AttnParams {
 };
 
 constexpr int kAttnWarps = 4;
+constexpr int kAttnUnroll = 4;   // positions per warp whose K/V loads are in flight together
+constexpr int kMaxSplit = 64;
 
 // One CTA = one (sequence, kv head, position split). Lanes split the head
-// dimension; each warp walks its positions with an online softmax per query
-// head of the GQA group; warps, then splits, are merged by max-rescaling.
+// dimension; each warp walks its positions kAttnUnroll at a time (all their
+// K/V loads issued before any is used) with an online softmax per query head
+// of the GQA group; warps, then splits, are merged by max-rescaling. The last
+// CTA of a (sequence, kv head) to finish merges the splits.
 template <int HD, int GQ>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnParams p) {
   constexpr int D = HD / 32;
   __shared__ float sm_m[kAttnWarps][GQ], sm_l[kAttnWarps][GQ];
   __shared__ float sm_acc[kAttnWarps][GQ][HD];
+  __shared__ float sm_w[kMaxSplit][GQ];
+  __shared__ float sm_L[GQ];
   __shared__ int sm_last;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -70,28 +76,35 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     for (int d = 0; d < D; ++d) acc[h][d] = 0.f;
   }
   const size_t head_base = ((size_t)b * p.nkv + kvh) * p.S;
-  for (int s = s0 + warp; s < s1; s += kAttnWarps) {
-    const __half* kp = p.k + (head_base + s) * HD + lane * D;
-    const __half* vp = p.v + (head_base + s) * HD + lane * D;
-    float kf[D], vf[D];
+  for (int sb = s0 + warp; sb < s1; sb += kAttnWarps * kAttnUnroll) {
+    __half kh[kAttnUnroll][D], vh[kAttnUnroll][D];
 #pragma unroll
-    for (int d = 0; d < D; ++d) {
-      kf[d] = __half2float(kp[d]);
-      vf[d] = __half2float(vp[d]);
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      const int s = sb + u * kAttnWarps;
+      const size_t off = (head_base + (s < s1 ? s : s0)) * HD + lane * D;
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+        kh[u][d] = p.k[off + d];
+        vh[u][d] = p.v[off + d];
+      }
     }
 #pragma unroll
-    for (int h = 0; h < GQ; ++h) {
-      float dot = 0.f;
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      if (sb + u * kAttnWarps >= s1) break;
 #pragma unroll
-      for (int d = 0; d < D; ++d) dot = fmaf(qf[h][d], kf[d], dot);
-      dot = warp_sum(dot);
-      const float mn = fmaxf(m[h], dot);
-      const float corr = exp2f(m[h] - mn);
-      const float e = exp2f(dot - mn);
-      l[h] = l[h] * corr + e;
+      for (int h = 0; h < GQ; ++h) {
+        float dot = 0.f;
 #pragma unroll
-      for (int d = 0; d < D; ++d) acc[h][d] = fmaf(acc[h][d], corr, e * vf[d]);
-      m[h] = mn;
+        for (int d = 0; d < D; ++d) dot = fmaf(qf[h][d], __half2float(kh[u][d]), dot);
+        dot = warp_sum(dot);
+        const float mn = fmaxf(m[h], dot);
+        const float corr = exp2f(m[h] - mn);
+        const float e = exp2f(dot - mn);
+        l[h] = l[h] * corr + e;
+#pragma unroll
+        for (int d = 0; d < D; ++d) acc[h][d] = fmaf(acc[h][d], corr, e * __half2float(vh[u][d]));
+        m[h] = mn;
+      }
     }
   }
 #pragma unroll
@@ -142,21 +155,35 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   __syncthreads();
   if (!sm_last) return;
   __threadfence();
+  // split weights: all (split, head) maxima and sums fetched in one parallel pass
+  for (int i = threadIdx.x; i < p.nsplit * GQ; i += kAttnWarps * 32) {
+    const int s = i / GQ, h = i - s * GQ;
+    const size_t slot = ((size_t)b * p.nq + kvh * GQ + h) * p.nsplit + s;
+    sm_w[s][h] = __ldcg(p.part_ml + slot * 2);
+  }
+  __syncthreads();
+  if (threadIdx.x < GQ) {
+    const int h = threadIdx.x;
+    float M = -INFINITY;
+    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, sm_w[s][h]);
+    float L = 0.f;
+    for (int s = 0; s < p.nsplit; ++s) {
+      const size_t slot = ((size_t)b * p.nq + kvh * GQ + h) * p.nsplit + s;
+      const float c = (sm_w[s][h] == -INFINITY) ? 0.f : exp2f(sm_w[s][h] - M);
+      sm_w[s][h] = c;
+      L = fmaf(__ldcg(p.part_ml + slot * 2 + 1), c, L);
+    }
+    sm_L[h] = L;
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < GQ * HD; i += kAttnWarps * 32) {
     const int h = i / HD, d = i - h * HD;
     const int head = kvh * GQ + h;
-    const size_t base = ((size_t)b * p.nq + head) * p.nsplit;
-    float M = -INFINITY;
-    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, __ldcg(p.part_ml + (base + s) * 2));
-    float L = 0.f, A = 0.f;
-    for (int s = 0; s < p.nsplit; ++s) {
-      const float ms = __ldcg(p.part_ml + (base + s) * 2);
-      if (ms == -INFINITY) continue;
-      const float c = exp2f(ms - M);
-      L = fmaf(__ldcg(p.part_ml + (base + s) * 2 + 1), c, L);
-      A = fmaf(__ldcg(p.part_o + (base + s) * HD + d), c, A);
-    }
-    p.out[(size_t)b * p.nq * HD + (size_t)head * HD + d] = __float2half_rn(A / L);
+    const float* po = p.part_o + ((size_t)b * p.nq + head) * p.nsplit * HD + d;
+    float A = 0.f;
+#pragma unroll 8
+    for (int s = 0; s < p.nsplit; ++s) A = fmaf(__ldcg(po + (size_t)s * HD), sm_w[s][h], A);
+    p.out[(size_t)b * p.nq * HD + (size_t)head * HD + d] = __float2half_rn(A / sm_L[h]);
   }
   if (threadIdx.x == 0) p.counters[b * p.nkv + kvh] = 0;
 }
@@ -370,6 +397,7 @@ int lw_attention_decode(const lw_attention_args* a, lw_stream_t stream) {
   if (a->batch <= 0 || a->n_kv_heads <= 0 || a->n_q_heads % a->n_kv_heads || a->max_seq <= 0 || a->n_split <= 0)
     return LW_ERR_BAD_SHAPE;
   if (a->n_split > 1 && (!a->part_o || !a->part_ml || !a->counters)) return LW_ERR_WORKSPACE;
+  if (a->n_split > lw::kMaxSplit) return LW_ERR_UNSUPPORTED;
   lw::AttnParams p = {};
   p.q = static_cast<const __half*>(a->q);
   p.k = static_cast<const __half*>(a->k_cache);

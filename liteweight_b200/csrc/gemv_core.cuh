@@ -57,6 +57,10 @@ enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_RESID_NORM = 2 };
 enum { EPI_PLAIN = 0, EPI_ROPE_KV = 1, EPI_SWIGLU = 2, EPI_F32 = 3, EPI_ARGMAX = 4 };
 
 constexpr int kStreamThreads = 256;
+#ifndef LW_PREFETCH_BATCHES
+#define LW_PREFETCH_BATCHES 4
+#endif
+constexpr int kPrefetch = LW_PREFETCH_BATCHES;   // batches of L2 prefetch ahead of the register loads
 constexpr int kMaxM = 32;
 
 struct StreamParams {
@@ -315,6 +319,27 @@ __global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const Strea
     return min(U, min(C - c, g1 - gp));
   };
 
+  // L2 prefetch of the run kPrefetch batches ahead of the register loads:
+  // bytes in flight no longer limited by registers.
+  auto prefetch = [&](int ga, int n) {
+    const int gb = min(g1, ga + n);
+    while (ga < gb) {
+      const int tt = ga / C, c0 = ga - tt * C, cn = min(C - c0, gb - ga);
+      const int r = tt * 16 + lane;
+      if (lane < 16 && r < p.N) {
+        const size_t off = (size_t)c0 * 64;
+        if (off < rowbytes) {
+          const size_t len = min((size_t)cn * 64, rowbytes - off);
+          prefetch_l2(p.w + (size_t)r * rowbytes + off, (uint32_t)len);
+        }
+      }
+      ga += cn;
+    }
+  };
+  int gpf = min(g1, g0 + 2 * U);
+  prefetch(gpf, kPrefetch * U);
+  gpf += kPrefetch * U;
+
   // Weights do not depend on the previous kernel: start both buffers first.
   int gA = g0, nA = batch_len(gA);
   if (nA) load(gA, nA, qa0, qb0, sa0, sb0);
@@ -331,54 +356,61 @@ __global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const Strea
       if (tid < kMaxM) ssq[tid] = 0.f;
       __syncthreads();
     }
-    for (int i = tid; i < p.M * groups8; i += kStreamThreads) {
-      const int m = i / groups8, k = (i - m * groups8) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (k < p.K) {
-        v = ldg_nc(p.act + (size_t)m * p.lda + k);
-        if constexpr (PRO == PRO_RESID_NORM) {
-          // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
-          const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
-          const float ps[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-          __half* hv = reinterpret_cast<__half*>(&v);
+    for (int m = 0; m < p.M; ++m) {
+      float sq = 0.f;
+      for (int i = tid; i < groups8; i += kStreamThreads) {
+        const int k = i * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (k < p.K) {
+          v = ldg_nc(p.act + (size_t)m * p.lda + k);
+          if constexpr (PRO == PRO_RESID_NORM) {
+            // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
+            const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
+            const float ps[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            __half* hv = reinterpret_cast<__half*>(&v);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
-          if (blockIdx.x == 0) *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v;
-        }
-        if constexpr (PRO != PRO_PLAIN) {
-          const __half* hv = reinterpret_cast<const __half*>(&v);
-          float s = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float f = __half2float(hv[e]);
-            s = fmaf(f, f, s);
+            for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
+            if (blockIdx.x == 0) *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v;
           }
-          atomicAdd(&ssq[m], s);
+          if constexpr (PRO != PRO_PLAIN) {
+            const __half* hv = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float f = __half2float(hv[e]);
+              sq = fmaf(f, f, sq);
+            }
+          }
         }
+        if constexpr (BITS == 4) v = perm_int4_pairs(v);
+        const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
+        sts128(act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8, v);
       }
-      if constexpr (BITS == 4) v = perm_int4_pairs(v);
-      const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
-      sts128(act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8, v);
+      if constexpr (PRO != PRO_PLAIN) {
+        sq = warp_sum(sq);
+        if (lane == 0) atomicAdd(&ssq[m], sq);
+      }
     }
     if constexpr (PRO != PRO_PLAIN) {
       __syncthreads();
       // modeling_llama.py:65-68: h = weight * fp16(x * rsqrt(mean(x^2) + eps))
-      for (int i = tid; i < p.M * groups8; i += kStreamThreads) {
-        const int m = i / groups8, k = (i - m * groups8) * 8;
-        if (k >= p.K) continue;
+      for (int m = 0; m < p.M; ++m) {
         const float rstd = 1.0f / sqrtf(ssq[m] / (float)p.K + p.eps);
-        const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
-        __half* dst = act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8;
-        uint4 v = lds128(dst);
-        uint4 gm = ldg_nc(p.gamma + k);
-        if constexpr (BITS == 4) gm = perm_int4_pairs(gm);
-        __half* hv = reinterpret_cast<__half*>(&v);
-        const __half* hg = reinterpret_cast<const __half*>(&gm);
+        for (int i = tid; i < groups8; i += kStreamThreads) {
+          const int k = i * 8;
+          if (k >= p.K) continue;
+          const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
+          __half* dst = act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8;
+          uint4 v = lds128(dst);
+          uint4 gm = ldg_nc(p.gamma + k);
+          if constexpr (BITS == 4) gm = perm_int4_pairs(gm);
+          __half* hv = reinterpret_cast<__half*>(&v);
+          const __half* hg = reinterpret_cast<const __half*>(&gm);
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          hv[e] = __float2half_rn(__half2float(hg[e]) * r16(__half2float(hv[e]) * rstd));
-        sts128(dst, v);
+          for (int e = 0; e < 8; ++e)
+            hv[e] = __float2half_rn(__half2float(hg[e]) * r16(__half2float(hv[e]) * rstd));
+          sts128(dst, v);
+        }
       }
     }
   }
@@ -445,13 +477,21 @@ __global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const Strea
     compute(gA, nA, qa0, qb0, sa0, sb0);
     gA = gnext;
     nA = batch_len(gA);
-    if (nA) load(gA, nA, qa0, qb0, sa0, sb0);
+    if (nA) {
+      load(gA, nA, qa0, qb0, sa0, sb0);
+      prefetch(gpf, nA);
+      gpf += nA;
+    }
     gnext = gA + nA;
     if (!nB) break;
     compute(gB, nB, qa1, qb1, sa1, sb1);
     gB = gnext;
     nB = batch_len(gB);
-    if (nB) load(gB, nB, qa1, qb1, sa1, sb1);
+    if (nB) {
+      load(gB, nB, qa1, qb1, sa1, sb1);
+      prefetch(gpf, nB);
+      gpf += nB;
+    }
     gnext = gB + nB;
   }
   pdl_launch_dependents();

@@ -251,7 +251,7 @@ class DecodeEngine:
         self.keys = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.tokens = torch.full((max_seq + 1, batch), -1, dtype=torch.int32, device=dev)
         # attention split: about two waves of CTAs at full length, >= 32 positions per split
-        self.n_split = max(1, min(-(-2 * 148 // (batch * self.nkv)), -(-max_seq // 32)))
+        self.n_split = max(1, min(64, -(-2 * 148 // (batch * self.nkv)), -(-max_seq // 32)))
         self.part_o = torch.zeros(batch, self.nq, self.n_split, hd, dtype=torch.float32, device=dev)
         self.part_ml = torch.zeros(batch, self.nq, self.n_split, 2, dtype=torch.float32, device=dev)
         self.attn_counters = torch.zeros(batch * self.nkv, dtype=torch.int32, device=dev)
