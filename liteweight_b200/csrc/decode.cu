@@ -313,7 +313,9 @@ int validate(const lw_fused_gemv_args* a) {
   if (a->M <= 0 || a->M > 32 || a->N <= 0 || a->K <= 0) return LW_ERR_BAD_SHAPE;
   if (a->bits != 16 && (!a->scales || a->group_size <= 0 || a->K % a->group_size)) return LW_ERR_BAD_GROUP;
   const int E = a->bits == 4 ? 32 : (a->bits == 8 ? 16 : 8);
-  if ((size_t)a->K * a->bits / 8 % 16 || a->K % 8 || (a->bits != 16 && a->group_size % E)) return LW_ERR_UNSUPPORTED;
+  if ((size_t)a->K * a->bits / 8 % 16 || a->K % 8 ||
+      (a->bits != 16 && (a->group_size % E || lw::group_shift(a->K, a->group_size) < 0)))
+    return LW_ERR_UNSUPPORTED;
   if (!al(a->act, 16) || !al(a->weight, 16) || a->lda % 8) return LW_ERR_ALIGNMENT;
   const int KC = 4 * E;
   if ((size_t)a->M * ((a->K + KC - 1) / KC) * KC * 2 > (size_t)lw::kStageBudget) return LW_ERR_UNSUPPORTED;

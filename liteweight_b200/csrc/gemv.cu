@@ -225,7 +225,7 @@ bool stream_ok(const void* act, const void* w, int K, int G) {
   constexpr int E = lw::WT<BITS>::E;
   const size_t rowbytes = (size_t)K * BITS / 8;
   return (rowbytes % 16 == 0) && (K % 8 == 0) && aligned(w, 16) && aligned(act, 16) &&
-         (BITS == 16 || (G % E == 0));
+         (BITS == 16 || (G % E == 0 && lw::group_shift(K, G) >= 0));
 }
 
 // out[M,N] = act @ W^T (+bias): stream kernel in row blocks, or the generic kernel.

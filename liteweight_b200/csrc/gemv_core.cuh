@@ -57,6 +57,10 @@ enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_RESID_NORM = 2 };
 enum { EPI_PLAIN = 0, EPI_ROPE_KV = 1, EPI_SWIGLU = 2, EPI_F32 = 3, EPI_ARGMAX = 4 };
 
 constexpr int kStreamThreads = 256;
+#ifndef LW_STREAM_MIN_BLOCKS
+#define LW_STREAM_MIN_BLOCKS 2
+#endif
+constexpr int kStreamMinBlocks = LW_STREAM_MIN_BLOCKS;   // CTAs per SM the register budget must allow
 #ifndef LW_PREFETCH_BATCHES
 #define LW_PREFETCH_BATCHES 4
 #endif
@@ -77,6 +81,7 @@ struct StreamParams {
   int tiles;    // ceil(N / 16)
   int per;      // chunks per warp
   int cp;       // staged activation row stride, halves
+  int gshift;   // scale group of element k = k >> gshift (group size a power of two, or 31 when G == K)
   // prologue
   const __half* gamma;     // [K] RMSNorm weight
   float eps;
@@ -154,6 +159,46 @@ LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, ui
       const uint4 av = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp) : z;
       mma16816(acc[mt], qa.x, qb.x, qa.y, qb.y, av.x, av.y);
       mma16816(acc[mt], qa.z, qb.z, qa.w, qb.w, av.z, av.w);
+    }
+  }
+}
+
+// Unscaled piece: exact integer codes times activations, accumulated in fp32
+// by the tensor core; the caller multiplies the chunk sum by the row scale.
+template <int BITS, int MT>
+LW_DEV void gemv_piece_codes(float (&acc)[MT][4], const uint4& qa, const uint4& qb, const __half* arow, int cp,
+                             int g, int M) {
+  const uint32_t* a32 = reinterpret_cast<const uint32_t*>(&qa);
+  const uint32_t* b32 = reinterpret_cast<const uint32_t*>(&qb);
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  if constexpr (BITS == 4) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      uint32_t A[4], B[4];
+      unpack_int4_word(a32[w], A);
+      unpack_int4_word(b32[w], B);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint4 av = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + w * 32) : z;
+        mma16816(acc[mt], A[0], B[0], A[1], B[1], av.x, av.y);
+        mma16816(acc[mt], A[2], B[2], A[3], B[3], av.z, av.w);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint4 av[MT];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) av[mt] = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + j * 32) : z;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t A[2], B[2];
+        dequant_int8_word(a32[2 * j + h], A);
+        dequant_int8_word(b32[2 * j + h], B);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          mma16816(acc[mt], A[0], B[0], A[1], B[1], h ? av[mt].z : av[mt].x, h ? av[mt].w : av[mt].y);
+      }
     }
   }
 }
@@ -271,10 +316,30 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
   }
 }
 
-template <int BITS, int MT, int U, int PRO, int EPI>
-__global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const StreamParams p) {
+// A cursor over a warp's run of flattened (tile, chunk) work.
+struct RunCursor {
+  int t, c, left;
+  LW_DEV int take(int U, int C) {   // next batch: up to U chunks, never crossing a tile
+    int n = min(U, min(C - c, left));
+    if (n <= 0) return 0;
+    left -= n;
+    c += n;
+    if (c == C) {
+      c = 0;
+      ++t;
+    }
+    return n;
+  }
+};
+
+// FOLD: every 4-lane chunk lies in one scale group (G a multiple of the chunk),
+// so the codes are summed unscaled per chunk and the sum is scaled once in fp32.
+// Otherwise every piece is dequantized exactly (fp16 code * scale) first.
+template <int BITS, int MT, int U, int PRO, int EPI, bool FOLD>
+__global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_kernel(const StreamParams p) {
   constexpr int E = WT<BITS>::E;
   constexpr int KC = 4 * E;
+  constexpr bool SCALED = BITS < 16;
   extern __shared__ __align__(16) uint8_t smem[];
   __half* act_s = reinterpret_cast<__half*>(smem);
   __shared__ float ssq[kMaxM];
@@ -287,65 +352,62 @@ __global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const Strea
   const int g0 = min(total, wid * p.per), g1 = min(total, g0 + p.per);
   const size_t rowbytes = (size_t)p.K * BITS / 8;
   const int npieces = (int)(rowbytes / 16);
-  const int ngroups = (BITS < 16) ? p.K / p.G : 1;
+  const int ngroups = SCALED ? p.K / p.G : 1;
 
   uint4 qa0[U], qb0[U], qa1[U], qb1[U];
   uint32_t sa0[U], sb0[U], sa1[U], sb1[U];
 
-  auto load = [&](int gp, int n, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
-    const int tt = gp / C, c0 = gp - tt * C;
-    const int r0 = tt * 16 + g, r1 = r0 + 8;
+  auto load = [&](int bt, int bc, int bn, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
+    const int r0 = bt * 16 + g, r1 = r0 + 8;
     const bool v0 = r0 < p.N, v1 = r1 < p.N;
-    const uint8_t* w0 = p.w + (size_t)(v0 ? r0 : 0) * rowbytes;
-    const uint8_t* w1 = p.w + (size_t)(v1 ? r1 : 0) * rowbytes;
+    const uint8_t* w0 = p.w + (size_t)(v0 ? r0 : 0) * rowbytes + (size_t)bc * 64 + t * 16;
+    const uint8_t* w1 = p.w + (size_t)(v1 ? r1 : 0) * rowbytes + (size_t)bc * 64 + t * 16;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int pc = (c0 + u) * 4 + t;
-      const bool ok = (u < n) && (pc < npieces);
-      qa[u] = (ok && v0) ? ldg_stream(w0 + (size_t)pc * 16) : make_uint4(0, 0, 0, 0);
-      qb[u] = (ok && v1) ? ldg_stream(w1 + (size_t)pc * 16) : make_uint4(0, 0, 0, 0);
-      if constexpr (BITS < 16) {
-        const int grp = ((c0 + u) * KC + t * E) / p.G;
-        sa[u] = (ok && v0) ? bcast_h(p.scales + (size_t)r0 * ngroups + grp) : 0u;
-        sb[u] = (ok && v1) ? bcast_h(p.scales + (size_t)r1 * ngroups + grp) : 0u;
-      } else {
-        sa[u] = sb[u] = 0u;
-      }
-    }
-  };
-  auto batch_len = [&](int gp) -> int {
-    if (gp >= g1) return 0;
-    const int c = gp % C;
-    return min(U, min(C - c, g1 - gp));
-  };
-
-  // L2 prefetch of the run kPrefetch batches ahead of the register loads:
-  // bytes in flight no longer limited by registers.
-  auto prefetch = [&](int ga, int n) {
-    const int gb = min(g1, ga + n);
-    while (ga < gb) {
-      const int tt = ga / C, c0 = ga - tt * C, cn = min(C - c0, gb - ga);
-      const int r = tt * 16 + lane;
-      if (lane < 16 && r < p.N) {
-        const size_t off = (size_t)c0 * 64;
-        if (off < rowbytes) {
-          const size_t len = min((size_t)cn * 64, rowbytes - off);
-          prefetch_l2(p.w + (size_t)r * rowbytes + off, (uint32_t)len);
+      const bool ok = (u < bn) && ((bc + u) * 4 + t < npieces);
+      qa[u] = (ok && v0) ? ldg_stream(w0 + u * 64) : make_uint4(0, 0, 0, 0);
+      qb[u] = (ok && v1) ? ldg_stream(w1 + u * 64) : make_uint4(0, 0, 0, 0);
+      if constexpr (SCALED) {
+        const int grp = ((bc + u) * KC + (FOLD ? 0 : t * E)) >> p.gshift;
+        const bool sok = FOLD ? (u < bn) : ok;
+        const unsigned short* s0 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r0 * ngroups;
+        const unsigned short* s1 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r1 * ngroups;
+        const uint32_t h0 = (sok && v0) ? (uint32_t)__ldg(s0 + grp) : 0u;
+        const uint32_t h1 = (sok && v1) ? (uint32_t)__ldg(s1 + grp) : 0u;
+        if constexpr (FOLD) {
+          sa[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h0)));
+          sb[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h1)));
+        } else {
+          sa[u] = h0 | (h0 << 16);
+          sb[u] = h1 | (h1 << 16);
         }
       }
-      ga += cn;
     }
   };
-  int gpf = min(g1, g0 + 2 * U);
-  prefetch(gpf, kPrefetch * U);
-  gpf += kPrefetch * U;
 
-  // Weights do not depend on the previous kernel: start both buffers first.
-  int gA = g0, nA = batch_len(gA);
-  if (nA) load(gA, nA, qa0, qb0, sa0, sb0);
-  int gB = gA + nA, nB = batch_len(gB);
-  if (nB) load(gB, nB, qa1, qb1, sa1, sb1);
-  int gnext = gB + nB;
+  // Run cursors: loads, and an L2 prefetch kPrefetch batches ahead of them.
+  RunCursor ld{g0 / max(C, 1), g0 - (g0 / max(C, 1)) * C, g1 - g0};
+  RunCursor pf = ld;
+  auto prefetch_next = [&]() {
+    const int pt = pf.t, pc = pf.c;
+    const int n = pf.take(U, C);
+    if (n && lane < 16) {
+      const int r = pt * 16 + lane;
+      const size_t off = (size_t)pc * 64;
+      if (r < p.N && off < rowbytes)
+        prefetch_l2(p.w + (size_t)r * rowbytes + off, (uint32_t)min((size_t)n * 64, rowbytes - off));
+    }
+  };
+
+  // Weights do not depend on the previous kernel: start streaming them first.
+  int tA = ld.t, cA = ld.c, nA = ld.take(U, C);
+  if (nA) load(tA, cA, nA, qa0, qb0, sa0, sb0);
+  int tB = ld.t, cB = ld.c, nB = ld.take(U, C);
+  if (nB) load(tB, cB, nB, qa1, qb1, sa1, sb1);
+  pf.take(U, C);
+  pf.take(U, C);
+#pragma unroll 1
+  for (int i = 0; i < kPrefetch; ++i) prefetch_next();
 
   pdl_wait();
 
@@ -420,11 +482,11 @@ __global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const Strea
   float acc[MT][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-  int seg = g0;  // start of the current tile segment
+  int seg_c0 = g0 - (g0 / max(C, 1)) * C;   // first chunk of the current tile segment
   const __half* abase = act_s + (size_t)g * p.cp + t * 8;
 
-  auto flush = [&](int tile, int end) {
-    const bool whole = (seg == tile * C) && (end == (tile + 1) * C);
+  auto flush = [&](int tile, int end_c) {
+    const bool whole = (seg_c0 == 0) && (end_c == C);
     if (whole) {
       finish_tile<MT, EPI>(p, tile, acc, lane);
     } else {
@@ -461,38 +523,54 @@ __global__ void __launch_bounds__(kStreamThreads) gemv_stream_kernel(const Strea
     }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-    seg = end;
+    seg_c0 = 0;
   };
 
-  auto compute = [&](int gp, int n, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
-    const int tt = gp / C, c0 = gp - tt * C;
+  auto compute = [&](int bt, int bc, int bn, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (u < n) gemv_piece<BITS, MT>(acc, qa[u], qb[u], sa[u], sb[u], abase + (c0 + u) * KC, p.cp, g, p.M);
-    const int end = gp + n;
-    if (end == (tt + 1) * C || end == g1) flush(tt, end);
+    for (int u = 0; u < U; ++u) {
+      if (u < bn) {
+        const __half* arow = abase + (bc + u) * KC;
+        if constexpr (SCALED && FOLD) {
+          float dc[MT][4];
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) dc[mt][0] = dc[mt][1] = dc[mt][2] = dc[mt][3] = 0.f;
+          gemv_piece_codes<BITS, MT>(dc, qa[u], qb[u], arow, p.cp, g, p.M);
+          const float s0f = __uint_as_float(sa[u]), s1f = __uint_as_float(sb[u]);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            acc[mt][0] = fmaf(dc[mt][0], s0f, acc[mt][0]);
+            acc[mt][1] = fmaf(dc[mt][1], s0f, acc[mt][1]);
+            acc[mt][2] = fmaf(dc[mt][2], s1f, acc[mt][2]);
+            acc[mt][3] = fmaf(dc[mt][3], s1f, acc[mt][3]);
+          }
+        } else {
+          gemv_piece<BITS, MT>(acc, qa[u], qb[u], sa[u], sb[u], arow, p.cp, g, p.M);
+        }
+      }
+    }
+    const int end_c = bc + bn;
+    if (end_c == C || bt * C + end_c == g1) flush(bt, end_c);
   };
 
   while (nA) {
-    compute(gA, nA, qa0, qb0, sa0, sb0);
-    gA = gnext;
-    nA = batch_len(gA);
+    compute(tA, cA, nA, qa0, qb0, sa0, sb0);
+    tA = ld.t;
+    cA = ld.c;
+    nA = ld.take(U, C);
     if (nA) {
-      load(gA, nA, qa0, qb0, sa0, sb0);
-      prefetch(gpf, nA);
-      gpf += nA;
+      load(tA, cA, nA, qa0, qb0, sa0, sb0);
+      prefetch_next();
     }
-    gnext = gA + nA;
     if (!nB) break;
-    compute(gB, nB, qa1, qb1, sa1, sb1);
-    gB = gnext;
-    nB = batch_len(gB);
+    compute(tB, cB, nB, qa1, qb1, sa1, sb1);
+    tB = ld.t;
+    cB = ld.c;
+    nB = ld.take(U, C);
     if (nB) {
-      load(gB, nB, qa1, qb1, sa1, sb1);
-      prefetch(gpf, nB);
-      gpf += nB;
+      load(tB, cB, nB, qa1, qb1, sa1, sb1);
+      prefetch_next();
     }
-    gnext = gB + nB;
   }
   pdl_launch_dependents();
 }

@@ -39,6 +39,23 @@ int stage_rows(int K) {
   return std::max(1, std::min(kMaxM, kStageBudget / (kpad * 2)));
 }
 
+// Scale-group shift: element k is in group k >> gshift. -1 when the group size
+// is neither a power of two nor K (the stream kernel does not take it).
+inline int group_shift(int K, int G) {
+  if (G == K) return 31;
+  if (G <= 0 || (G & (G - 1))) return -1;
+  int s = 0;
+  while ((1 << s) < G) ++s;
+  return s;
+}
+
+// Every 4-lane chunk inside one scale group: sum codes unscaled, scale per chunk.
+template <int BITS>
+inline bool fold_scales(int K, int G) {
+  constexpr int KC = 4 * WT<BITS>::E;
+  return BITS < 16 && (G == K || G % KC == 0);
+}
+
 template <int BITS, int MT, int PRO, int EPI>
 cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   constexpr int KC = 4 * WT<BITS>::E;
@@ -48,7 +65,7 @@ cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   const int kpad = pl->kchunks * KC;
   pl->cp = ((size_t)M * (kpad + 32) * 2 <= (size_t)kStageBudget) ? kpad + 32 : kpad;
   pl->smem = (size_t)M * pl->cp * 2;
-  auto kern = gemv_stream_kernel<BITS, MT, kBatch, PRO, EPI>;
+  auto kern = gemv_stream_kernel<BITS, MT, kBatch, PRO, EPI, BITS < 16>;
   cudaError_t e = cudaSuccess;
   if (pl->smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl->smem);
   if (e != cudaSuccess) return e;
@@ -102,10 +119,29 @@ cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaS
     p.counters = nullptr;
     p.slots = nullptr;
   }
+  p.gshift = BITS < 16 ? group_shift(p.K, p.G) : 31;
   dim3 grid(pl.grid), block(kStreamThreads);
-  if (mt == 1) return lw_launch(gemv_stream_kernel<BITS, 1, kBatch, PRO, EPI>, grid, block, pl.smem, s, pdl, p);
-  if (mt == 2) return lw_launch(gemv_stream_kernel<BITS, 2, kBatch, PRO, EPI>, grid, block, pl.smem, s, pdl, p);
-  return lw_launch(gemv_stream_kernel<BITS, 4, kBatch, PRO, EPI>, grid, block, pl.smem, s, pdl, p);
+  const bool fold = fold_scales<BITS>(p.K, p.G);
+  if (pl.smem > 48 * 1024) {   // the variant launched may differ from the one planned with
+    cudaError_t ea = cudaSuccess;
+    if (mt == 1) ea = cudaFuncSetAttribute(fold ? gemv_stream_kernel<BITS, 1, kBatch, PRO, EPI, true>
+                                                : gemv_stream_kernel<BITS, 1, kBatch, PRO, EPI, false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    else if (mt == 2) ea = cudaFuncSetAttribute(fold ? gemv_stream_kernel<BITS, 2, kBatch, PRO, EPI, true>
+                                                     : gemv_stream_kernel<BITS, 2, kBatch, PRO, EPI, false>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    else ea = cudaFuncSetAttribute(fold ? gemv_stream_kernel<BITS, 4, kBatch, PRO, EPI, true>
+                                        : gemv_stream_kernel<BITS, 4, kBatch, PRO, EPI, false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    if (ea != cudaSuccess) return ea;
+  }
+#define LW_GO(MT_)                                                                                          \
+  return fold ? lw_launch(gemv_stream_kernel<BITS, MT_, kBatch, PRO, EPI, true>, grid, block, pl.smem, s, pdl, p) \
+              : lw_launch(gemv_stream_kernel<BITS, MT_, kBatch, PRO, EPI, false>, grid, block, pl.smem, s, pdl, p);
+  if (mt == 1) { LW_GO(1) }
+  if (mt == 2) { LW_GO(2) }
+  LW_GO(4)
+#undef LW_GO
 }
 
 // Workspace bytes a launch of these sizes can use to split tiles.

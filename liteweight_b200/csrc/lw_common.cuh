@@ -110,6 +110,24 @@ LW_DEV void dequant_int4_word(uint32_t q, uint32_t (&o)[4]) {
   o[3] = h2_as_u32(__hfma2(u32_as_h2(h37), k1_16, km72));
 }
 
+// Same unpack without scaling, with the sign flip folded into each LOP3
+// constant: (x & m) ^ c where c = 0x6400.. | 0x0008.. for the low nibbles.
+LW_DEV void unpack_int4_word(uint32_t q, uint32_t (&o)[4]) {
+  const uint32_t y = q >> 8;
+  uint32_t h04, h15, h26, h37;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h04) : "r"(q), "n"(0x000F000F), "n"(0x64086408));
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h15) : "r"(q), "n"(0x00F000F0), "n"(0x64806480));
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h26) : "r"(y), "n"(0x000F000F), "n"(0x64086408));
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h37) : "r"(y), "n"(0x00F000F0), "n"(0x64806480));
+  const __half2 k1032 = __half2half2(__ushort_as_half(0x6408));   // 1032.0
+  const __half2 k1_16 = __half2half2(__ushort_as_half(0x2C00));   // 1/16
+  const __half2 km72 = __half2half2(__ushort_as_half(0xD480));    // -72.0
+  o[0] = h2_as_u32(__hsub2(u32_as_h2(h04), k1032));
+  o[1] = h2_as_u32(__hfma2(u32_as_h2(h15), k1_16, km72));
+  o[2] = h2_as_u32(__hsub2(u32_as_h2(h26), k1032));
+  o[3] = h2_as_u32(__hfma2(u32_as_h2(h37), k1_16, km72));
+}
+
 // 4 INT8 codes (bytes 0..3 = elements k0..k0+3) to two half2 (0,1) (2,3).
 // u = byte ^ 0x80 = code + 128; fp16 bits 0x64uu = 1024 + u; minus 1152.
 LW_DEV void dequant_int8_word(uint32_t q, uint32_t (&o)[2]) {
