@@ -330,7 +330,7 @@ MODELS = {
 class DecodeWorkload:
     unit = "tokens/s"
 
-    def __init__(self, device, dist: "Dist", model: str, batch: int, extra_steps: int):
+    def __init__(self, device, dist: "Dist", model: str, batch: int, extra_steps: int, fold: bool = False):
         import torch
         from liteweight_b200 import engine as E
         cfg = MODELS[model]
@@ -357,7 +357,7 @@ class DecodeWorkload:
             import torch.distributed as tdist
             group = tdist.group.WORLD
         self.eng = E.DecodeEngine(spec, packed, embed, norm, None, cos, sin, batch, max_seq, device, self.rank,
-                                  self.tp, group)
+                                  self.tp, group, fold_scales=fold)
         gp = torch.Generator().manual_seed(7)
         self.prompt = torch.randint(0, spec.vocab, (batch, self.P), generator=gp)
         torch.cuda.synchronize()
@@ -657,7 +657,7 @@ def run_decode(args, dist: Dist):
     dist.init("nccl")
     lwbuild.build()
     nat.lib()
-    wl = DecodeWorkload(dev, dist, args.model, args.batch, args.warmup + args.steps)
+    wl = DecodeWorkload(dev, dist, args.model, args.batch, args.warmup + args.steps, fold=args.fold)
     if dist.world > 1:   # NCCL communicator up before graph capture
         t = torch.zeros(1, device=dev)
         dist.pg.all_reduce(t)
@@ -717,6 +717,7 @@ def run_decode(args, dist: Dist):
             "config": {"workload": f"decode {MODELS[args.model]['name']} INT{wl.spec.bits} G{GROUP}",
                        "model": MODELS[args.model]["name"], "global_batch": wl.B, "prompt": wl.P,
                        "new_tokens": wl.T, "seq_len": wl.P + wl.T, "parallelism": f"tp{dist.world}",
+                       "dequant": "per-chunk fp32 scale" if args.fold else "exact fp16(code*scale)",
                        "l2": f"inputs larger than L2 ({wl.spec.weight_bytes_per_token() / dist.world / 1e9:.2f} GB "
                              "of weights per GPU per step)"},
             "roofline": roofline, "decode_roofline": decode_roofline, "cpu_baseline": cpu, "e2e": e2e,
@@ -770,6 +771,8 @@ def main():
     ap.add_argument("--model", choices=sorted(MODELS), default="8b")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--fold", action="store_true",
+                    help="decode GEMVs scale each chunk sum in fp32 instead of dequantizing exactly")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 200 if args.impl == "ours" else 21

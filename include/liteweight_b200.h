@@ -133,6 +133,9 @@ typedef struct {
   int prologue;      /* LW_PRO_* */
   int epilogue;      /* LW_EPI_* */
   int pdl;           /* 1: programmatic dependent launch (overlaps the previous kernel) */
+  int fold_scales;   /* 0: dequantize exactly (fp16(code * scale), as liteweight does);
+                        1: sum codes * act per 4-lane chunk and scale the chunk sum in fp32
+                        (skips that fp16 rounding; within the row-scaled tolerance, not bit-identical) */
   int M, N, K, group_size;  /* M <= 32 rows */
   int lda, ldo;
   const void* act;      /* fp16 [M][lda] (the residual stream for the norm prologues) */

@@ -49,7 +49,10 @@ inline int group_shift(int K, int G) {
   return s;
 }
 
-// Every 4-lane chunk inside one scale group: sum codes unscaled, scale per chunk.
+// Every 4-lane chunk inside one scale group: the codes may be summed unscaled and
+// each chunk sum scaled once in fp32. This skips the fp16 rounding of code *
+// scale that liteweight's dequantize (and its Triton kernels) apply, so it is an
+// opt-in: the drop-in matmul entry points always dequantize exactly.
 template <int BITS>
 inline bool fold_scales(int K, int G) {
   constexpr int KC = 4 * WT<BITS>::E;
@@ -90,7 +93,8 @@ cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
 // first use, then slots) is used only when the plan splits tiles; without a
 // large enough workspace the plan keeps tiles whole.
 template <int BITS, int PRO, int EPI>
-cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl) {
+cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl,
+                                bool allow_fold = false) {
   StreamPlan pl;
   cudaError_t e;
   const int mt = mt_for(p.M);
@@ -121,7 +125,7 @@ cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaS
   }
   p.gshift = BITS < 16 ? group_shift(p.K, p.G) : 31;
   dim3 grid(pl.grid), block(kStreamThreads);
-  const bool fold = fold_scales<BITS>(p.K, p.G);
+  const bool fold = allow_fold && fold_scales<BITS>(p.K, p.G);
   if (pl.smem > 48 * 1024) {   // the variant launched may differ from the one planned with
     cudaError_t ea = cudaSuccess;
     if (mt == 1) ea = cudaFuncSetAttribute(fold ? gemv_stream_kernel<BITS, 1, kBatch, PRO, EPI, true>

@@ -41,7 +41,7 @@ EPI_PLAIN, EPI_ROPE_KV, EPI_SWIGLU, EPI_F32, EPI_ARGMAX = 0, 1, 2, 3, 4
 class FusedGemvArgs(ctypes.Structure):
     """Mirror of lw_fused_gemv_args (include/liteweight_b200.h)."""
     _fields_ = [
-        ("bits", c_int), ("prologue", c_int), ("epilogue", c_int), ("pdl", c_int),
+        ("bits", c_int), ("prologue", c_int), ("epilogue", c_int), ("pdl", c_int), ("fold_scales", c_int),
         ("M", c_int), ("N", c_int), ("K", c_int), ("group_size", c_int), ("lda", c_int), ("ldo", c_int),
         ("act", c_void_p), ("weight", c_void_p), ("scales", c_void_p), ("bias", c_void_p), ("residual", c_void_p),
         ("out", c_void_p), ("gamma", c_void_p), ("psum", c_void_p), ("x_out", c_void_p),
@@ -215,8 +215,10 @@ class DecodeEngine:
 
     def __init__(self, spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
                  lm_head: torch.Tensor | None, rope_cos: torch.Tensor, rope_sin: torch.Tensor, batch: int,
-                 max_seq: int, device=None, tp_rank: int = 0, tp_size: int = 1, tp_group=None, pdl: bool = True):
+                 max_seq: int, device=None, tp_rank: int = 0, tp_size: int = 1, tp_group=None, pdl: bool = True,
+                 fold_scales: bool = False):
         self.spec, self.B, self.S = spec, batch, max_seq
+        self.fold = int(fold_scales)
         self.device = torch.device(device) if device is not None else embed.device
         self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
         assert spec.n_heads % tp_size == 0 and spec.n_kv_heads % tp_size == 0, "heads must split evenly"
@@ -262,7 +264,7 @@ class DecodeEngine:
     # -------------------------------------------------------------- call table
     def _gemv(self, **kw) -> FusedGemvArgs:
         a = FusedGemvArgs()
-        a.pdl, a.M, a.eps = self.pdl, self.B, self.spec.eps
+        a.pdl, a.M, a.eps, a.fold_scales = self.pdl, self.B, self.spec.eps, self.fold
         for k, v in kw.items():
             setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
         return a
@@ -511,12 +513,12 @@ def engine_from_hf(model, batch: int, max_seq: int, tp_rank: int = 0, tp_size: i
 def build_engine(spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
                  lm_head: torch.Tensor | None, inv_freq: torch.Tensor, batch: int, max_seq: int, device,
                  attention_scaling: float = 1.0, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
-                 pdl: bool = True) -> DecodeEngine:
+                 pdl: bool = True, fold_scales: bool = False) -> DecodeEngine:
     """Engine from unsharded LayerWeights (liteweight-format tensors, any device)."""
     packed = [PackedLayer(lw, spec, tp_rank, tp_size, device) for lw in layers]
     cos, sin = rope_tables(inv_freq, max_seq, attention_scaling, device)
     return DecodeEngine(spec, packed, embed, final_norm, lm_head, cos, sin, batch, max_seq, device, tp_rank,
-                        tp_size, tp_group, pdl)
+                        tp_size, tp_group, pdl, fold_scales)
 
 
 def synthetic_layers(spec: LlamaSpec, device, seed: int = 0, std: float = 0.02) -> list:

@@ -28,7 +28,8 @@ def _t(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
 
 
-def engine_from_oracle(w: ol.LlamaWeights, bits: int, group: int, batch: int, max_seq: int, graph_pdl=True):
+def engine_from_oracle(w: ol.LlamaWeights, bits: int, group: int, batch: int, max_seq: int, graph_pdl=True,
+                       fold=False):
     from liteweight_b200 import engine as E
     s = w.shape
     spec = E.LlamaSpec(hidden=s.hidden, inter=s.inter, n_layers=s.n_layers, n_heads=s.n_heads,
@@ -41,7 +42,7 @@ def engine_from_oracle(w: ol.LlamaWeights, bits: int, group: int, batch: int, ma
         layers.append(E.LayerWeights(in_norm=_t(L.in_norm), post_norm=_t(L.post_norm), **lin))
     lm = None if w.lm_head is w.embed else _t(w.lm_head)
     return E.build_engine(spec, layers, _t(w.embed), _t(w.norm), lm, torch.from_numpy(w.inv_freq), batch, max_seq,
-                          DEV, attention_scaling=w.attention_scaling, pdl=graph_pdl)
+                          DEV, attention_scaling=w.attention_scaling, pdl=graph_pdl, fold_scales=fold)
 
 
 def run_engine(eng, prompt, steps, forced=None, graph=True):
@@ -119,20 +120,21 @@ def random_model(hidden, inter, layers, heads, kv, hd, vocab, bits, seed):
                            inv_freq=inv)
 
 
+@pytest.mark.parametrize("fold", [False, True])
 @pytest.mark.parametrize("bits,batch,hd,heads,kv", [(4, 1, 64, 8, 2), (8, 3, 64, 8, 2), (4, 4, 128, 8, 1),
                                                     (8, 1, 128, 4, 4)])
-def test_random_model_vs_oracle(bits, batch, hd, heads, kv):
+def test_random_model_vs_oracle(bits, batch, hd, heads, kv, fold):
     """Free-running greedy decode; the oracle replays the engine's own tokens
     (teacher forcing), so every step's logits are compared on equal inputs.
     Vocab 1000 (not a multiple of 16) exercises the ragged lm_head tile."""
     w = random_model(512, 1536, 3, heads, kv, hd, 1000, bits, seed=bits * 10 + batch)
     P, T = 5, 7
     prompt = np.random.default_rng(batch).integers(0, 1000, (batch, P))
-    eng = engine_from_oracle(w, bits, 128, batch=batch, max_seq=48)
+    eng = engine_from_oracle(w, bits, 128, batch=batch, max_seq=48, fold=fold)
     got = run_engine(eng, prompt, P + T - 1)
     gen = eng.generated(T).cpu().numpy()
     oracle = ol.teacher_forced_logits(w, prompt, gen)
-    assert_rows(got, oracle, f"bits={bits} B={batch} hd={hd}")
+    assert_rows(got, oracle, f"bits={bits} B={batch} hd={hd} fold={fold}")
 
 
 def test_graph_equals_eager_and_long_context():
