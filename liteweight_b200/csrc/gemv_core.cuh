@@ -109,18 +109,28 @@ LW_DEV uint32_t bcast_h(const __half* p) {
   return (uint32_t)s | ((uint32_t)s << 16);
 }
 
+// Activation fragments come from shared memory rows arow[mt] (lane row g + 8*mt,
+// clamped to the last real row: batch columns >= M are computed and dropped,
+// so they may read any valid data). Out-of-range weight pieces meet the zero
+// padding of the staged activation, so no operand needs zeroing.
+template <int MT>
+LW_DEV uint4 act16(const __half* const (&arow)[MT], int mt, int off) {
+  return *reinterpret_cast<const uint4*>(arow[mt] + off);
+}
+
+// Exact dequant: fp16(code) * fp16(scale) in fp16 (one rounding of the exact
+// product, bit-identical to liteweight's dequantize), fp32 tensor-core sums.
 template <int BITS, int MT>
 LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, uint32_t sa, uint32_t sb,
-                       const __half* arow, int cp, int g, int M) {
+                       const __half* const (&arow)[MT], int off) {
   const uint32_t* a32 = reinterpret_cast<const uint32_t*>(&qa);
   const uint32_t* b32 = reinterpret_cast<const uint32_t*>(&qb);
-  const uint4 z = make_uint4(0, 0, 0, 0);
   if constexpr (BITS == 4) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       uint32_t A[4], B[4];
-      dequant_int4_word(a32[w], A);
-      dequant_int4_word(b32[w], B);
+      unpack_int4_word(a32[w], A);
+      unpack_int4_word(b32[w], B);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         A[i] = hmul2_u32(A[i], sa);
@@ -128,7 +138,7 @@ LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, ui
       }
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        const uint4 av = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + w * 32) : z;
+        const uint4 av = act16(arow, mt, off + w * 32);
         mma16816(acc[mt], A[0], B[0], A[1], B[1], av.x, av.y);
         mma16816(acc[mt], A[2], B[2], A[3], B[3], av.z, av.w);
       }
@@ -138,7 +148,7 @@ LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, ui
     for (int j = 0; j < 2; ++j) {
       uint4 av[MT];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) av[mt] = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + j * 32) : z;
+      for (int mt = 0; mt < MT; ++mt) av[mt] = act16(arow, mt, off + j * 32);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t A[2], B[2];
@@ -156,7 +166,7 @@ LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, ui
   } else {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      const uint4 av = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp) : z;
+      const uint4 av = act16(arow, mt, off);
       mma16816(acc[mt], qa.x, qb.x, qa.y, qb.y, av.x, av.y);
       mma16816(acc[mt], qa.z, qb.z, qa.w, qb.w, av.z, av.w);
     }
@@ -166,11 +176,10 @@ LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, ui
 // Unscaled piece: exact integer codes times activations, accumulated in fp32
 // by the tensor core; the caller multiplies the chunk sum by the row scale.
 template <int BITS, int MT>
-LW_DEV void gemv_piece_codes(float (&acc)[MT][4], const uint4& qa, const uint4& qb, const __half* arow, int cp,
-                             int g, int M) {
+LW_DEV void gemv_piece_codes(float (&acc)[MT][4], const uint4& qa, const uint4& qb,
+                             const __half* const (&arow)[MT], int off) {
   const uint32_t* a32 = reinterpret_cast<const uint32_t*>(&qa);
   const uint32_t* b32 = reinterpret_cast<const uint32_t*>(&qb);
-  const uint4 z = make_uint4(0, 0, 0, 0);
   if constexpr (BITS == 4) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
@@ -179,7 +188,7 @@ LW_DEV void gemv_piece_codes(float (&acc)[MT][4], const uint4& qa, const uint4& 
       unpack_int4_word(b32[w], B);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        const uint4 av = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + w * 32) : z;
+        const uint4 av = act16(arow, mt, off + w * 32);
         mma16816(acc[mt], A[0], B[0], A[1], B[1], av.x, av.y);
         mma16816(acc[mt], A[2], B[2], A[3], B[3], av.z, av.w);
       }
@@ -189,7 +198,7 @@ LW_DEV void gemv_piece_codes(float (&acc)[MT][4], const uint4& qa, const uint4& 
     for (int j = 0; j < 2; ++j) {
       uint4 av[MT];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) av[mt] = (g + 8 * mt < M) ? lds128(arow + mt * 8 * cp + j * 32) : z;
+      for (int mt = 0; mt < MT; ++mt) av[mt] = act16(arow, mt, off + j * 32);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t A[2], B[2];
@@ -357,29 +366,30 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   uint4 qa0[U], qb0[U], qa1[U], qb1[U];
   uint32_t sa0[U], sb0[U], sa1[U], sb1[U];
 
+  // Rows past N are clamped to N-1 (computed, never stored); pieces past K are
+  // clamped to the last piece (they meet zero activations). No selects.
   auto load = [&](int bt, int bc, int bn, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
-    const int r0 = bt * 16 + g, r1 = r0 + 8;
-    const bool v0 = r0 < p.N, v1 = r1 < p.N;
-    const uint8_t* w0 = p.w + (size_t)(v0 ? r0 : 0) * rowbytes + (size_t)bc * 64 + t * 16;
-    const uint8_t* w1 = p.w + (size_t)(v1 ? r1 : 0) * rowbytes + (size_t)bc * 64 + t * 16;
+    const int r0 = min(bt * 16 + g, p.N - 1), r1 = min(bt * 16 + g + 8, p.N - 1);
+    const uint8_t* w0 = p.w + (size_t)r0 * rowbytes;
+    const uint8_t* w1 = p.w + (size_t)r1 * rowbytes;
+    const unsigned short* s0 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r0 * ngroups;
+    const unsigned short* s1 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r1 * ngroups;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const bool ok = (u < bn) && ((bc + u) * 4 + t < npieces);
-      qa[u] = (ok && v0) ? ldg_stream(w0 + u * 64) : make_uint4(0, 0, 0, 0);
-      qb[u] = (ok && v1) ? ldg_stream(w1 + u * 64) : make_uint4(0, 0, 0, 0);
-      if constexpr (SCALED) {
-        const int grp = ((bc + u) * KC + (FOLD ? 0 : t * E)) >> p.gshift;
-        const bool sok = FOLD ? (u < bn) : ok;
-        const unsigned short* s0 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r0 * ngroups;
-        const unsigned short* s1 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r1 * ngroups;
-        const uint32_t h0 = (sok && v0) ? (uint32_t)__ldg(s0 + grp) : 0u;
-        const uint32_t h1 = (sok && v1) ? (uint32_t)__ldg(s1 + grp) : 0u;
-        if constexpr (FOLD) {
-          sa[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h0)));
-          sb[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h1)));
-        } else {
-          sa[u] = h0 | (h0 << 16);
-          sb[u] = h1 | (h1 << 16);
+      if (u < bn) {
+        const int pc = min((bc + u) * 4 + t, npieces - 1);
+        qa[u] = ldg_stream(w0 + (size_t)pc * 16);
+        qb[u] = ldg_stream(w1 + (size_t)pc * 16);
+        if constexpr (SCALED) {
+          const int grp = min(((bc + u) * KC + (FOLD ? 0 : t * E)) >> p.gshift, ngroups - 1);
+          const uint32_t h0 = __ldg(s0 + grp), h1 = __ldg(s1 + grp);
+          if constexpr (FOLD) {
+            sa[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h0)));
+            sb[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h1)));
+          } else {
+            sa[u] = h0 | (h0 << 16);
+            sb[u] = h1 | (h1 << 16);
+          }
         }
       }
     }
@@ -483,7 +493,9 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
   int seg_c0 = g0 - (g0 / max(C, 1)) * C;   // first chunk of the current tile segment
-  const __half* abase = act_s + (size_t)g * p.cp + t * 8;
+  const __half* arow[MT];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) arow[mt] = act_s + (size_t)min(g + 8 * mt, p.M - 1) * p.cp + t * 8;
 
   auto flush = [&](int tile, int end_c) {
     const bool whole = (seg_c0 == 0) && (end_c == C);
@@ -530,12 +542,12 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (u < bn) {
-        const __half* arow = abase + (bc + u) * KC;
+        const int off = (bc + u) * KC;
         if constexpr (SCALED && FOLD) {
           float dc[MT][4];
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) dc[mt][0] = dc[mt][1] = dc[mt][2] = dc[mt][3] = 0.f;
-          gemv_piece_codes<BITS, MT>(dc, qa[u], qb[u], arow, p.cp, g, p.M);
+          gemv_piece_codes<BITS, MT>(dc, qa[u], qb[u], arow, off);
           const float s0f = __uint_as_float(sa[u]), s1f = __uint_as_float(sb[u]);
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
@@ -545,7 +557,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
             acc[mt][3] = fmaf(dc[mt][3], s1f, acc[mt][3]);
           }
         } else {
-          gemv_piece<BITS, MT>(acc, qa[u], qb[u], sa[u], sb[u], arow, p.cp, g, p.M);
+          gemv_piece<BITS, MT>(acc, qa[u], qb[u], sa[u], sb[u], arow, off);
         }
       }
     }
