@@ -133,8 +133,8 @@ LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, ui
       unpack_int4_word(b32[w], B);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        A[i] = hmul2_u32(A[i], sa);
-        B[i] = hmul2_u32(B[i], sb);
+        A[i] = hmul2_rn(A[i], sa);
+        B[i] = hmul2_rn(B[i], sb);
       }
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
@@ -154,10 +154,10 @@ LW_DEV void gemv_piece(float (&acc)[MT][4], const uint4& qa, const uint4& qb, ui
         uint32_t A[2], B[2];
         dequant_int8_word(a32[2 * j + h], A);
         dequant_int8_word(b32[2 * j + h], B);
-        A[0] = hmul2_u32(A[0], sa);
-        A[1] = hmul2_u32(A[1], sa);
-        B[0] = hmul2_u32(B[0], sb);
-        B[1] = hmul2_u32(B[1], sb);
+        A[0] = hmul2_rn(A[0], sa);
+        A[1] = hmul2_rn(A[1], sa);
+        B[0] = hmul2_rn(B[0], sb);
+        B[1] = hmul2_rn(B[1], sb);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
           mma16816(acc[mt], A[0], B[0], A[1], B[1], h ? av[mt].z : av[mt].x, h ? av[mt].w : av[mt].y);

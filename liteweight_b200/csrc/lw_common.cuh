@@ -82,63 +82,60 @@ LW_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint3
 
 LW_DEV uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 LW_DEV __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-LW_DEV uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
-}
 
 // ---------------------------------------------------------------- dequant
 
-// 8 INT4 codes in one 32-bit word (code i = nibble i = element k0 + i) to four
-// half2 holding exact small integers, paired (0,4) (1,5) (2,6) (3,7).
-// Trick: with u = nibble ^ 8 = code + 8 in 0..15, the fp16 with bits
+// INT4: 8 codes in one 32-bit word (code i = nibble i = element k0 + i) are
+// unpacked to four half2 holding the exact small integers, paired (0,4) (1,5)
+// (2,6) (3,7). With u = nibble ^ 8 = code + 8 in 0..15, the fp16 with bits
 // 0x6400 | u is 1024 + u, so subtracting 1032 gives the signed code; the
 // nibbles at bits 4..7 land as 1024 + 16u and are rescaled by an exact fma.
-LW_DEV void dequant_int4_word(uint32_t q, uint32_t (&o)[4]) {
-  const uint32_t x = q ^ 0x88888888u;
-  const uint32_t y = x >> 8;
-  const uint32_t MAGIC = 0x64006400u;
-  uint32_t h04 = (x & 0x000F000Fu) | MAGIC;
-  uint32_t h15 = (x & 0x00F000F0u) | MAGIC;
-  uint32_t h26 = (y & 0x000F000Fu) | MAGIC;
-  uint32_t h37 = (y & 0x00F000F0u) | MAGIC;
-  const __half2 k1032 = __half2half2(__ushort_as_half(0x6408));   // 1032.0
-  const __half2 k1_16 = __half2half2(__ushort_as_half(0x2C00));   // 1/16
-  const __half2 km72 = __half2half2(__ushort_as_half(0xD480));    // -72.0
-  o[0] = h2_as_u32(__hsub2(u32_as_h2(h04), k1032));
-  o[1] = h2_as_u32(__hfma2(u32_as_h2(h15), k1_16, km72));
-  o[2] = h2_as_u32(__hsub2(u32_as_h2(h26), k1032));
-  o[3] = h2_as_u32(__hfma2(u32_as_h2(h37), k1_16, km72));
+// Same unpack without scaling, in PTX: the sign flip is folded into each LOP3
+// constant ((x & m) ^ c, c = 0x6400.. | 0x0008..), the fp16 constants live in
+// registers (1032 and the (1/16, -72) rescale of the high nibbles).
+LW_DEV void unpack_int4_word(uint32_t q, uint32_t (&o)[4]) {
+  const uint32_t k1032 = 0x64086408u, k1_16 = 0x2C002C00u, km72 = 0xD480D480u;
+  asm("{\n"
+      " .reg .b32 y, a, b, c, d;\n"
+      " shr.u32 y, %4, 8;\n"
+      " lop3.b32 a, %4, 0x000F000F, 0x64086408, 0x6a;\n"
+      " lop3.b32 b, %4, 0x00F000F0, 0x64806480, 0x6a;\n"
+      " lop3.b32 c, y, 0x000F000F, 0x64086408, 0x6a;\n"
+      " lop3.b32 d, y, 0x00F000F0, 0x64806480, 0x6a;\n"
+      " sub.f16x2 %0, a, %5;\n"
+      " fma.rn.f16x2 %1, b, %6, %7;\n"
+      " sub.f16x2 %2, c, %5;\n"
+      " fma.rn.f16x2 %3, d, %6, %7;\n"
+      "}\n"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(q), "r"(k1032), "r"(k1_16), "r"(km72));
 }
 
-// Same unpack without scaling, with the sign flip folded into each LOP3
-// constant: (x & m) ^ c where c = 0x6400.. | 0x0008.. for the low nibbles.
-LW_DEV void unpack_int4_word(uint32_t q, uint32_t (&o)[4]) {
-  const uint32_t y = q >> 8;
-  uint32_t h04, h15, h26, h37;
-  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h04) : "r"(q), "n"(0x000F000F), "n"(0x64086408));
-  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h15) : "r"(q), "n"(0x00F000F0), "n"(0x64806480));
-  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h26) : "r"(y), "n"(0x000F000F), "n"(0x64086408));
-  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(h37) : "r"(y), "n"(0x00F000F0), "n"(0x64806480));
-  const __half2 k1032 = __half2half2(__ushort_as_half(0x6408));   // 1032.0
-  const __half2 k1_16 = __half2half2(__ushort_as_half(0x2C00));   // 1/16
-  const __half2 km72 = __half2half2(__ushort_as_half(0xD480));    // -72.0
-  o[0] = h2_as_u32(__hsub2(u32_as_h2(h04), k1032));
-  o[1] = h2_as_u32(__hfma2(u32_as_h2(h15), k1_16, km72));
-  o[2] = h2_as_u32(__hsub2(u32_as_h2(h26), k1032));
-  o[3] = h2_as_u32(__hfma2(u32_as_h2(h37), k1_16, km72));
+// fp16x2 product, round to nearest (one rounding of the exact product).
+LW_DEV uint32_t hmul2_rn(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
 // 4 INT8 codes (bytes 0..3 = elements k0..k0+3) to two half2 (0,1) (2,3).
 // u = byte ^ 0x80 = code + 128; fp16 bits 0x64uu = 1024 + u; minus 1152.
 LW_DEV void dequant_int8_word(uint32_t q, uint32_t (&o)[2]) {
-  const uint32_t x = q ^ 0x80808080u;
-  const __half2 k1152 = __half2half2(__ushort_as_half(0x6480));   // 1152.0
-  o[0] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(x, 0x64646464u, 0x4140)), k1152));
-  o[1] = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(x, 0x64646464u, 0x4342)), k1152));
+  const uint32_t k1152 = 0x64806480u, magic = 0x64646464u;
+  asm("{\n"
+      " .reg .b32 x, a, b;\n"
+      " xor.b32 x, %2, 0x80808080;\n"
+      " prmt.b32 a, x, %4, 0x4140;\n"
+      " prmt.b32 b, x, %4, 0x4342;\n"
+      " sub.f16x2 %0, a, %3;\n"
+      " sub.f16x2 %1, b, %3;\n"
+      "}\n"
+      : "=r"(o[0]), "=r"(o[1])
+      : "r"(q), "r"(k1152), "r"(magic));
 }
 
 // Permute 8 halves (h0..h7) to (h0,h4)(h1,h5)(h2,h6)(h3,h7): the element
-// pairing that dequant_int4_word produces.
+// pairing that unpack_int4_word produces.
 LW_DEV uint4 perm_int4_pairs(uint4 v) {
   uint4 o;
   o.x = __byte_perm(v.x, v.z, 0x5410);
