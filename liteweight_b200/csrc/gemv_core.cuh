@@ -398,14 +398,16 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   // Run cursors: loads, and an L2 prefetch kPrefetch batches ahead of them.
   RunCursor ld{g0 / max(C, 1), g0 - (g0 / max(C, 1)) * C, g1 - g0};
   RunCursor pf = ld;
+  // Each of the 32 lanes prefetches one 64-byte piece-pair line: rows g and
+  // g+8 of the batch, chunk t (lanes hold 16 rows x 2 chunks of U = 2).
   auto prefetch_next = [&]() {
     const int pt = pf.t, pc = pf.c;
     const int n = pf.take(U, C);
-    if (n && lane < 16) {
-      const int r = pt * 16 + lane;
-      const size_t off = (size_t)pc * 64;
-      if (r < p.N && off < rowbytes)
-        prefetch_l2(p.w + (size_t)r * rowbytes + off, (uint32_t)min((size_t)n * 64, rowbytes - off));
+    if (n) {
+      const int row = min(pt * 16 + (lane & 15), p.N - 1);
+      const int ch = min(pc + (lane >> 4), pc + n - 1);
+      const size_t off = min((size_t)ch * 64, rowbytes - 16);
+      prefetch_l2_line(p.w + (size_t)row * rowbytes + off);
     }
   };
 

@@ -53,10 +53,9 @@ LW_DEV void sts128(void* p, uint4 v) {
                "r"(v.w));
 }
 
-// Fire-and-forget bulk prefetch of [p, p + bytes) into L2 (16-byte multiples).
-LW_DEV void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
+// Per-thread prefetch of the cache line holding p into L2 (one LSU instruction;
+// the bulk prefetch is warp-uniform and serialises per-lane addresses).
+LW_DEV void prefetch_l2_line(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 // Programmatic dependent launch: wait for the previous kernel in the stream
 // (no-op when the launch did not opt in) / let the next one start its prologue.
