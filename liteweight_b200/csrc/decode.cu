@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   __shared__ float sm_m[kAttnWarps][GQ], sm_l[kAttnWarps][GQ];
   __shared__ float sm_acc[kAttnWarps][GQ][HD];
   __shared__ float sm_w[kMaxSplit][GQ];
+  __shared__ float sm_ls[kMaxSplit][GQ];
   __shared__ float sm_L[GQ];
   __shared__ int sm_last;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -159,7 +160,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   for (int i = threadIdx.x; i < p.nsplit * GQ; i += kAttnWarps * 32) {
     const int s = i / GQ, h = i - s * GQ;
     const size_t slot = ((size_t)b * p.nq + kvh * GQ + h) * p.nsplit + s;
-    sm_w[s][h] = __ldcg(p.part_ml + slot * 2);
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + slot * 2));
+    sm_w[s][h] = ml.x;
+    sm_ls[s][h] = ml.y;
   }
   __syncthreads();
   if (threadIdx.x < GQ) {
@@ -168,10 +171,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, sm_w[s][h]);
     float L = 0.f;
     for (int s = 0; s < p.nsplit; ++s) {
-      const size_t slot = ((size_t)b * p.nq + kvh * GQ + h) * p.nsplit + s;
       const float c = (sm_w[s][h] == -INFINITY) ? 0.f : exp2f(sm_w[s][h] - M);
       sm_w[s][h] = c;
-      L = fmaf(__ldcg(p.part_ml + slot * 2 + 1), c, L);
+      L = fmaf(sm_ls[s][h], c, L);
     }
     sm_L[h] = L;
   }
