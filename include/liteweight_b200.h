@@ -165,22 +165,19 @@ typedef struct {
 int lw_fused_gemv(const lw_fused_gemv_args* args, lw_stream_t stream);
 size_t lw_fused_gemv_workspace_size(const lw_fused_gemv_args* args);
 
-/* Split-KV GQA attention of one query per sequence over cache positions
- * 0..*pos (modeling_llama.py:197-222 with repeat_kv): scores scaled by
+/* GQA attention of one query per sequence over cache positions 0..*pos
+ * (modeling_llama.py:197-222 with repeat_kv): scores scaled by
  * head_dim^-0.5, fp32 softmax, fp16 output [batch][n_q_heads*head_dim].
- * n_split <= 64; n_split > 1 needs part_o (fp32 [batch][n_q_heads][n_split][head_dim]),
- * part_ml (fp32 [batch][n_q_heads][n_split][2]) and counters (int
- * [batch][n_kv_heads], zero before first use, kept zero). */
+ * head_dim 64 or 128; n_q_heads / n_kv_heads in {1, 2, 4, 8}. Each
+ * (sequence, kv head) is one 8-CTA thread-block cluster whose CTAs split the
+ * positions and merge through distributed shared memory: no workspace. */
 typedef struct {
   const void* q;
-  const void* k_cache;
+  const void* k_cache;   /* fp16 [batch][n_kv_heads][max_seq][head_dim] */
   const void* v_cache;
   void* out;
-  float* part_o;
-  float* part_ml;
-  int* counters;
   const int* pos;
-  int batch, n_q_heads, n_kv_heads, head_dim, max_seq, n_split, pdl;
+  int batch, n_q_heads, n_kv_heads, head_dim, max_seq, pdl;
 } lw_attention_args;
 
 int lw_attention_decode(const lw_attention_args* args, lw_stream_t stream);

@@ -19,6 +19,9 @@
 // norm prologue adds them to the residual.
 #include "gemv_host.cuh"
 
+#include <cooperative_groups.h>
+#include <type_traits>
+
 namespace lw {
 
 // ------------------------------------------------------------- attention
@@ -28,38 +31,42 @@ struct AttnParams {
   const __half* k;     // [B][nkv][S][hd] (this layer)
   const __half* v;
   __half* out;         // [B][nq * hd]
-  float* part_o;       // [B][nq][nsplit][hd]
-  float* part_ml;      // [B][nq][nsplit][2] (running max in log2 units, sum)
-  int* counters;       // [B][nkv], zero before the first launch, left zero
   const int* pos;      // attend over positions 0..*pos
-  int B, nq, nkv, S, nsplit;
+  int B, nq, nkv, S;
   float scale_log2;    // head_dim^-0.5 * log2(e)
 };
 
-constexpr int kAttnWarps = 4;
-constexpr int kAttnUnroll = 4;   // positions per warp whose K/V loads are in flight together
-constexpr int kMaxSplit = 64;
+// Cluster attention: one thread-block cluster of kAttnCluster CTAs per
+// (sequence, kv head); CTA r of the cluster and warp w of the CTA own
+// positions [base + (r * W + w) * P, ... + P) of every round of
+// kAttnCluster * W * P positions. A warp issues the K/V loads of a whole
+// round (P positions, D halves each per lane) before using any, and those of
+// the next round before computing this one. Lanes split the head dimension;
+// per position the q.k dots of the GQA group are warp-reduced, then an online
+// softmax per query head updates (m, l, acc). Warps merge through shared
+// memory, then the cluster's CTAs merge through distributed shared memory
+// after a cluster barrier - no global round trips, no counters.
+constexpr int kAttnWarps = 8;
+constexpr int kAttnCluster = 8;
+constexpr int kAttnPos = 8;   // positions per warp per round
 
-// One CTA = one (sequence, kv head, position split). Lanes split the head
-// dimension; each warp walks its positions kAttnUnroll at a time (all their
-// K/V loads issued before any is used) with an online softmax per query head
-// of the GQA group; warps, then splits, are merged by max-rescaling. The last
-// CTA of a (sequence, kv head) to finish merges the splits.
 template <int HD, int GQ>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnParams p) {
+  namespace cg = cooperative_groups;
   constexpr int D = HD / 32;
-  __shared__ float sm_m[kAttnWarps][GQ], sm_l[kAttnWarps][GQ];
-  __shared__ float sm_acc[kAttnWarps][GQ][HD];
-  __shared__ float sm_w[kMaxSplit][GQ];
-  __shared__ float sm_ls[kMaxSplit][GQ];
-  __shared__ float sm_L[GQ];
-  __shared__ int sm_last;
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  constexpr int W = kAttnWarps;
+  __shared__ float sm_m[W][GQ], sm_l[W][GQ];
+  __shared__ float sm_acc[W][GQ][HD];
+  __shared__ float cta_m[GQ], cta_l[GQ];
+  __shared__ float cta_acc[GQ][HD];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   const int len = *p.pos + 1;
-  const int chunk = (len + p.nsplit - 1) / p.nsplit;
-  const int s0 = split * chunk, s1 = min(len, s0 + chunk);
+  const int per_round = kAttnCluster * W * kAttnPos;
+  const int first = (rank * W + warp) * kAttnPos;
 
   float qf[GQ][D];
 #pragma unroll
@@ -76,38 +83,72 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 #pragma unroll
     for (int d = 0; d < D; ++d) acc[h][d] = 0.f;
   }
-  const size_t head_base = ((size_t)b * p.nkv + kvh) * p.S;
-  for (int sb = s0 + warp; sb < s1; sb += kAttnWarps * kAttnUnroll) {
-    __half kh[kAttnUnroll][D], vh[kAttnUnroll][D];
+  const __half* kb = p.k + ((size_t)b * p.nkv + kvh) * p.S * HD + lane * D;
+  const __half* vb = p.v + ((size_t)b * p.nkv + kvh) * p.S * HD + lane * D;
+  using VecT = typename std::conditional<D == 4, uint2, uint32_t>::type;
+  VecT kr[2][kAttnPos], vr[2][kAttnPos];
+  auto load_round = [&](int base, VecT (&kk)[kAttnPos], VecT (&vv)[kAttnPos]) {
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const int s = sb + u * kAttnWarps;
-      const size_t off = (head_base + (s < s1 ? s : s0)) * HD + lane * D;
-#pragma unroll
-      for (int d = 0; d < D; ++d) {
-        kh[u][d] = p.k[off + d];
-        vh[u][d] = p.v[off + d];
-      }
+    for (int j = 0; j < kAttnPos; ++j) {
+      const int s = min(base + first + j, len - 1);   // clamped: positions past len are skipped below
+      kk[j] = *reinterpret_cast<const VecT*>(kb + (size_t)s * HD);
+      vv[j] = *reinterpret_cast<const VecT*>(vb + (size_t)s * HD);
     }
+  };
+  auto process = [&](int base, const VecT (&kk)[kAttnPos], const VecT (&vv)[kAttnPos]) {
+    const int n = min(kAttnPos, len - (base + first));
+    if (n <= 0) return;
+    float dot[kAttnPos][GQ];
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      if (sb + u * kAttnWarps >= s1) break;
+    for (int j = 0; j < kAttnPos; ++j) {
+      const __half* kh = reinterpret_cast<const __half*>(&kk[j]);
 #pragma unroll
       for (int h = 0; h < GQ; ++h) {
-        float dot = 0.f;
+        float a = 0.f;
 #pragma unroll
-        for (int d = 0; d < D; ++d) dot = fmaf(qf[h][d], __half2float(kh[u][d]), dot);
-        dot = warp_sum(dot);
-        const float mn = fmaxf(m[h], dot);
-        const float corr = exp2f(m[h] - mn);
-        const float e = exp2f(dot - mn);
-        l[h] = l[h] * corr + e;
-#pragma unroll
-        for (int d = 0; d < D; ++d) acc[h][d] = fmaf(acc[h][d], corr, e * __half2float(vh[u][d]));
-        m[h] = mn;
+        for (int d = 0; d < D; ++d) a = fmaf(qf[h][d], __half2float(kh[d]), a);
+        dot[j][h] = a;
       }
     }
+#pragma unroll
+    for (int j = 0; j < kAttnPos; ++j)
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) dot[j][h] = warp_sum(dot[j][h]);
+#pragma unroll
+    for (int h = 0; h < GQ; ++h) {
+      float mr = m[h];
+#pragma unroll
+      for (int j = 0; j < kAttnPos; ++j)
+        if (j < n) mr = fmaxf(mr, dot[j][h]);
+      const float corr = exp2f(m[h] - mr);
+      l[h] *= corr;
+#pragma unroll
+      for (int d = 0; d < D; ++d) acc[h][d] *= corr;
+#pragma unroll
+      for (int j = 0; j < kAttnPos; ++j) {
+        if (j < n) {
+          const float e = exp2f(dot[j][h] - mr);
+          l[h] += e;
+          const __half* vh = reinterpret_cast<const __half*>(&vv[j]);
+#pragma unroll
+          for (int d = 0; d < D; ++d) acc[h][d] = fmaf(e, __half2float(vh[d]), acc[h][d]);
+        }
+      }
+      m[h] = mr;
+    }
+  };
+  const int rounds = (len + per_round - 1) / per_round;
+  load_round(0, kr[0], vr[0]);
+  for (int r = 0; r < rounds; r += 2) {
+    if (r + 1 < rounds) load_round((r + 1) * per_round, kr[1], vr[1]);
+    process(r * per_round, kr[0], vr[0]);
+    if (r + 1 >= rounds) break;
+    if (r + 2 < rounds) load_round((r + 2) * per_round, kr[0], vr[0]);
+    process((r + 1) * per_round, kr[1], vr[1]);
   }
+  pdl_launch_dependents();
+
+  // warps -> CTA
 #pragma unroll
   for (int h = 0; h < GQ; ++h) {
     if (lane == 0) {
@@ -118,76 +159,45 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     for (int d = 0; d < D; ++d) sm_acc[warp][h][lane * D + d] = acc[h][d];
   }
   __syncthreads();
-  pdl_launch_dependents();
-  // merge the warps: thread -> (h, dim) pairs
-  for (int i = threadIdx.x; i < GQ * HD; i += kAttnWarps * 32) {
+  for (int i = threadIdx.x; i < GQ * HD; i += W * 32) {
     const int h = i / HD, d = i - h * HD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][h]);
+    for (int w = 0; w < W; ++w) M = fmaxf(M, sm_m[w][h]);
     float L = 0.f, A = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) {
+      for (int w = 0; w < W; ++w) {
         const float c = exp2f(sm_m[w][h] - M);
         L = fmaf(sm_l[w][h], c, L);
         A = fmaf(sm_acc[w][h][d], c, A);
       }
     }
-    const int head = kvh * GQ + h;
-    if (p.nsplit == 1) {
-      p.out[(size_t)b * p.nq * HD + (size_t)head * HD + d] = __float2half_rn(A / L);
-    } else {
-      const size_t slot = ((size_t)b * p.nq + head) * p.nsplit + split;
-      p.part_o[slot * HD + d] = A;
-      if (d == 0) {
-        p.part_ml[slot * 2] = M;
-        p.part_ml[slot * 2 + 1] = L;
-      }
+    cta_acc[h][d] = A;
+    if (d == 0) {
+      cta_m[h] = M;
+      cta_l[h] = L;
     }
   }
-  if (p.nsplit == 1) return;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int old = atomicAdd(p.counters + b * p.nkv + kvh, 1);
-    sm_last = (old == p.nsplit - 1);
-  }
-  __syncthreads();
-  if (!sm_last) return;
-  __threadfence();
-  // split weights: all (split, head) maxima and sums fetched in one parallel pass
-  for (int i = threadIdx.x; i < p.nsplit * GQ; i += kAttnWarps * 32) {
-    const int s = i / GQ, h = i - s * GQ;
-    const size_t slot = ((size_t)b * p.nq + kvh * GQ + h) * p.nsplit + s;
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + slot * 2));
-    sm_w[s][h] = ml.x;
-    sm_ls[s][h] = ml.y;
-  }
-  __syncthreads();
-  if (threadIdx.x < GQ) {
-    const int h = threadIdx.x;
-    float M = -INFINITY;
-    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, sm_w[s][h]);
-    float L = 0.f;
-    for (int s = 0; s < p.nsplit; ++s) {
-      const float c = (sm_w[s][h] == -INFINITY) ? 0.f : exp2f(sm_w[s][h] - M);
-      sm_w[s][h] = c;
-      L = fmaf(sm_ls[s][h], c, L);
-    }
-    sm_L[h] = L;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < GQ * HD; i += kAttnWarps * 32) {
+  // CTAs of the cluster -> output: CTA r finishes elements r, r + CL, ...
+  cluster.sync();
+  for (int i = rank * (W * 32) + threadIdx.x; i < GQ * HD; i += kAttnCluster * W * 32) {
     const int h = i / HD, d = i - h * HD;
-    const int head = kvh * GQ + h;
-    const float* po = p.part_o + ((size_t)b * p.nq + head) * p.nsplit * HD + d;
-    float A = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < p.nsplit; ++s) A = fmaf(__ldcg(po + (size_t)s * HD), sm_w[s][h], A);
-    p.out[(size_t)b * p.nq * HD + (size_t)head * HD + d] = __float2half_rn(A / sm_L[h]);
+    float M = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kAttnCluster; ++c) M = fmaxf(M, *cluster.map_shared_rank(&cta_m[h], c));
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int c = 0; c < kAttnCluster; ++c) {
+      const float mc = *cluster.map_shared_rank(&cta_m[h], c);
+      if (mc == -INFINITY) continue;
+      const float w = exp2f(mc - M);
+      L = fmaf(*cluster.map_shared_rank(&cta_l[h], c), w, L);
+      A = fmaf(*cluster.map_shared_rank(&cta_acc[h][d], c), w, A);
+    }
+    p.out[(size_t)b * p.nq * HD + (size_t)(kvh * GQ + h) * HD + d] = __float2half_rn(A / L);
   }
-  if (threadIdx.x == 0) p.counters[b * p.nkv + kvh] = 0;
+  cluster.sync();   // keep this CTA's shared memory alive until every remote read is done
 }
 
 // ------------------------------------------------------------- tokens
@@ -356,8 +366,25 @@ int validate(const lw_fused_gemv_args* a) {
 
 template <int HD, int GQ>
 cudaError_t attn_launch(const lw::AttnParams& p, cudaStream_t s, bool pdl) {
-  dim3 grid(p.nsplit, p.nkv, p.B), block(lw::kAttnWarps * 32);
-  return lw_launch(lw::attn_decode_kernel<HD, GQ>, grid, block, 0, s, pdl, p);
+  lw_count_launch();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(lw::kAttnCluster, p.nkv, p.B);
+  cfg.blockDim = dim3(lw::kAttnWarps * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = lw::kAttnCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  int na = 1;
+  if (pdl) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, lw::attn_decode_kernel<HD, GQ>, p);
 }
 
 }  // namespace
@@ -399,24 +426,19 @@ size_t lw_fused_gemv_workspace_size(const lw_fused_gemv_args* a) {
 
 int lw_attention_decode(const lw_attention_args* a, lw_stream_t stream) {
   if (!a || !a->q || !a->k_cache || !a->v_cache || !a->out || !a->pos) return LW_ERR_NULL_POINTER;
-  if (a->batch <= 0 || a->n_kv_heads <= 0 || a->n_q_heads % a->n_kv_heads || a->max_seq <= 0 || a->n_split <= 0)
+  if (a->batch <= 0 || a->n_kv_heads <= 0 || a->n_q_heads % a->n_kv_heads || a->max_seq <= 0)
     return LW_ERR_BAD_SHAPE;
-  if (a->n_split > 1 && (!a->part_o || !a->part_ml || !a->counters)) return LW_ERR_WORKSPACE;
-  if (a->n_split > lw::kMaxSplit) return LW_ERR_UNSUPPORTED;
+
   lw::AttnParams p = {};
   p.q = static_cast<const __half*>(a->q);
   p.k = static_cast<const __half*>(a->k_cache);
   p.v = static_cast<const __half*>(a->v_cache);
   p.out = static_cast<__half*>(a->out);
-  p.part_o = a->part_o;
-  p.part_ml = a->part_ml;
-  p.counters = a->counters;
   p.pos = a->pos;
   p.B = a->batch;
   p.nq = a->n_q_heads;
   p.nkv = a->n_kv_heads;
   p.S = a->max_seq;
-  p.nsplit = a->n_split;
   p.scale_log2 = (1.0f / sqrtf((float)a->head_dim)) * 1.4426950408889634f;
   const int gq = a->n_q_heads / a->n_kv_heads;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

@@ -57,10 +57,9 @@ class FusedGemvArgs(ctypes.Structure):
 class AttentionArgs(ctypes.Structure):
     """Mirror of lw_attention_args (include/liteweight_b200.h)."""
     _fields_ = [
-        ("q", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p), ("out", c_void_p),
-        ("part_o", c_void_p), ("part_ml", c_void_p), ("counters", c_void_p), ("pos", c_void_p),
+        ("q", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p), ("out", c_void_p), ("pos", c_void_p),
         ("batch", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("max_seq", c_int),
-        ("n_split", c_int), ("pdl", c_int),
+        ("pdl", c_int),
     ]
 
 
@@ -252,11 +251,6 @@ class DecodeEngine:
         self.done = torch.zeros(1, dtype=torch.int32, device=dev)
         self.keys = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.tokens = torch.full((max_seq + 1, batch), -1, dtype=torch.int32, device=dev)
-        # attention split: about two waves of CTAs at full length, >= 32 positions per split
-        self.n_split = max(1, min(64, -(-2 * 148 // (batch * self.nkv)), -(-max_seq // 32)))
-        self.part_o = torch.zeros(batch, self.nq, self.n_split, hd, dtype=torch.float32, device=dev)
-        self.part_ml = torch.zeros(batch, self.nq, self.n_split, 2, dtype=torch.float32, device=dev)
-        self.attn_counters = torch.zeros(batch * self.nkv, dtype=torch.int32, device=dev)
         self._build_calls()
         self.graph = None
         self.host_pos = 0
@@ -298,11 +292,9 @@ class DecodeEngine:
             calls.append(("gemv", a, "qkv"))
             gemv_args.append(a)
             at = AttentionArgs(q=self.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
-                               v_cache=self.v_cache[li].data_ptr(), out=self.attn.data_ptr(),
-                               part_o=self.part_o.data_ptr(), part_ml=self.part_ml.data_ptr(),
-                               counters=self.attn_counters.data_ptr(), pos=self.pos.data_ptr(), batch=B,
-                               n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
-                               n_split=self.n_split, pdl=self.pdl)
+                               v_cache=self.v_cache[li].data_ptr(), out=self.attn.data_ptr(), pos=self.pos.data_ptr(),
+                               batch=B, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
+                               pdl=self.pdl)
             calls.append(("attn", at, "attn"))
             epi = dict(epilogue=EPI_F32, out_f32=self.psum) if tp else \
                 dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])

@@ -13,7 +13,7 @@ from liteweight_b200 import build as lwbuild
 def test_struct_layout_matches_library():
     lwbuild.build()
     E.check_abi()
-    assert ctypes.sizeof(E.FusedGemvArgs) == 224 and ctypes.sizeof(E.AttentionArgs) == 96
+    assert ctypes.sizeof(E.FusedGemvArgs) == 224 and ctypes.sizeof(E.AttentionArgs) == 64
 
 
 @pytest.mark.parametrize("hd", [64, 128])
