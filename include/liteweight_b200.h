@@ -80,6 +80,18 @@ int lw_gemm_w4a16(const void* act, const void* qweight, const void* scales, cons
                   void* out, int M, int N, int K, int group_size, void* workspace,
                   size_t workspace_bytes, lw_stream_t stream);
 
+/* lw_gemm_w4a16 without a caller workspace, for callers that cannot allocate
+ * device memory (a runtime whose device memory is all planned at start-up, a
+ * plugin host that forbids cudaMalloc after initialisation, code that only
+ * receives its inputs and outputs). No counterpart in the reference. Its
+ * scratch is a fixed 4 MiB array inside the library, held on every GPU that
+ * loads it until exit; problems needing more (lw_gemm_workspace_size) return
+ * LW_ERR_WORKSPACE. The first call on a device looks the array up, so make
+ * it before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race. */
+int lw_gemm_w4a16_noalloc(const void* act, const void* qweight, const void* scales, const void* bias,
+                          void* out, int M, int N, int K, int group_size, lw_stream_t stream);
+
 /* Workspace bytes the matmul entry points can use for these sizes (bits = 4,
  * 8 or 16); 0 when no tile is split. Needs a current CUDA device. No
  * counterpart in the reference (its Triton kernels need no scratch). */

@@ -29,6 +29,7 @@ _SIGNATURES: dict[str, list] = {
     "lw_gemm_w8a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p, ctypes.c_size_t, c_void_p],
     "lw_gemm_w4a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p, ctypes.c_size_t, c_void_p],
     "lw_gemm_f16": [c_void_p] * 3 + [c_int] * 3 + [c_void_p, ctypes.c_size_t, c_void_p],
+    "lw_gemm_w4a16_noalloc": [c_void_p] * 5 + [c_int] * 4 + [c_void_p],
     "lw_gemm_f16_kn": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
     "lw_dequant_w8": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
     "lw_dequant_w4": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
