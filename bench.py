@@ -330,7 +330,8 @@ MODELS = {
 class DecodeWorkload:
     unit = "tokens/s"
 
-    def __init__(self, device, dist: "Dist", model: str, batch: int, extra_steps: int, fold: bool = False):
+    def __init__(self, device, dist: "Dist", model: str, batch: int, extra_steps: int, fold: bool = False,
+                 exchange: str = "peer"):
         import torch
         from liteweight_b200 import engine as E
         cfg = MODELS[model]
@@ -357,7 +358,7 @@ class DecodeWorkload:
             import torch.distributed as tdist
             group = tdist.group.WORLD
         self.eng = E.DecodeEngine(spec, packed, embed, norm, None, cos, sin, batch, max_seq, device, self.rank,
-                                  self.tp, group, fold_scales=fold)
+                                  self.tp, group, fold_scales=fold, exchange=exchange)
         gp = torch.Generator().manual_seed(7)
         self.prompt = torch.randint(0, spec.vocab, (batch, self.P), generator=gp)
         torch.cuda.synchronize()
@@ -657,7 +658,8 @@ def run_decode(args, dist: Dist):
     dist.init("nccl")
     lwbuild.build()
     nat.lib()
-    wl = DecodeWorkload(dev, dist, args.model, args.batch, args.warmup + args.steps, fold=args.fold)
+    wl = DecodeWorkload(dev, dist, args.model, args.batch, args.warmup + args.steps, fold=args.fold,
+                        exchange=args.exchange)
     if dist.world > 1:   # NCCL communicator up before graph capture
         t = torch.zeros(1, device=dev)
         dist.pg.all_reduce(t)
@@ -677,6 +679,7 @@ def run_decode(args, dist: Dist):
         e1.record()
         torch.cuda.synchronize()
     dist.barrier(dev)
+    wl.eng.check()
     ms = e0.elapsed_time(e1)
     ms_max = dist.max(ms, dev)
     ctx_mid = ctx0 + args.steps // 2
@@ -706,7 +709,7 @@ def run_decode(args, dist: Dist):
     clocks = clk.summary()
     launches = args.steps * wl.eng.kernels_per_step()
     if dist.rank != 0:
-        wl.eng.graph = None
+        wl.eng.close()
         dist.close()
         return
     cpu = CpuDecode(args.model, wl.B).measure() if dist.world == 1 else None
@@ -718,6 +721,9 @@ def run_decode(args, dist: Dist):
                        "model": MODELS[args.model]["name"], "global_batch": wl.B, "prompt": wl.P,
                        "new_tokens": wl.T, "seq_len": wl.P + wl.T, "parallelism": f"tp{dist.world}",
                        "dequant": "per-chunk fp32 scale" if args.fold else "exact fp16(code*scale)",
+                       "all_reduce": ("none" if dist.world == 1 else
+                                      "in-kernel peer-memory exchange over NVLink" if args.exchange == "peer"
+                                      else "NCCL all_reduce in the step graph"),
                        "l2": f"inputs larger than L2 ({wl.spec.weight_bytes_per_token() / dist.world / 1e9:.2f} GB "
                              "of weights per GPU per step)"},
             "roofline": roofline, "decode_roofline": decode_roofline, "cpu_baseline": cpu, "e2e": e2e,
@@ -725,7 +731,7 @@ def run_decode(args, dist: Dist):
                                                        for k, v in kstats.items()},
             "clocks": clocks}
     print(json.dumps(line), flush=True)
-    wl.eng.graph = None
+    wl.eng.close()
     dist.close()
 
 
@@ -773,6 +779,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--fold", action="store_true",
                     help="decode GEMVs scale each chunk sum in fp32 instead of dequantizing exactly")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="tensor-parallel all-reduce: in-kernel through peer memory, or NCCL between kernels")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 200 if args.impl == "ours" else 21

@@ -5,9 +5,10 @@
  * Conventions
  *   - Plain device pointers and sizes; tensors are row-major and contiguous.
  *   - fp16 = IEEE binary16 (2 bytes); int8/uint8 are raw bytes.
- *   - Every entry point enqueues work on `stream` (a cudaStream_t; NULL = the
- *     legacy default stream), never synchronises the host and never allocates
- *     device memory, so it can be captured in a CUDA graph.
+ *   - Every compute entry point enqueues work on `stream` (a cudaStream_t;
+ *     NULL = the legacy default stream), never synchronises the host and
+ *     never allocates device memory, so it can be captured in a CUDA graph.
+ *     The lw_peer_* setup calls are the exception and say so.
  *   - Every entry point returns an lw_status (0 = success). Nothing calls
  *     exit(), traps on the device or prints.
  *
@@ -128,7 +129,10 @@ int lw_dequant_w4(const void* qweight, const void* scales, void* out, int N, int
 enum {
   LW_PRO_PLAIN = 0,      /* act as given */
   LW_PRO_NORM = 1,       /* RMSNorm(act) * gamma (modeling_llama.py:63-68) */
-  LW_PRO_RESID_NORM = 2  /* x_out = act + fp16(psum) (CTA 0 writes it), then RMSNorm */
+  LW_PRO_RESID_NORM = 2, /* x_out = act + fp16(psum) (CTA 0 writes it), then RMSNorm */
+  LW_PRO_PEER_RESID_NORM = 3  /* as LW_PRO_RESID_NORM with psum = the sum over r = 0..world-1,
+                                 in rank order (fp32), of the partials of exchange xin (src =
+                                 8-byte words [world][M][K]), each read once its flag is current */
 };
 
 /* What the fused GEMV does with each output. */
@@ -137,8 +141,52 @@ enum {
   LW_EPI_ROPE_KV = 1,  /* q|k|v rows (rope-pair order): RoPE q,k; q -> q_out, k,v -> cache at *pos */
   LW_EPI_SWIGLU = 2,   /* gate|up rows interleaved by 8: out[i] = silu(gate_i) * up_i */
   LW_EPI_F32 = 3,      /* out_f32 = y unrounded (tensor-parallel partial sum) */
-  LW_EPI_ARGMAX = 4    /* out = fp16 logits; argmax_keys[m] = max(key) (first max wins) */
+  LW_EPI_ARGMAX = 4,   /* out = fp16 logits; argmax_keys[m] = max(key) (first max wins) */
+  LW_EPI_PEER_F32 = 5, /* y unrounded as flagged words [M][ldo] into xout->dst[d] on every rank d */
+  LW_EPI_PEER_ARGMAX = 6  /* as LW_EPI_ARGMAX; the last CTA then sends this rank's keys as flagged
+                             words [M] to xout->dst[d] on every rank d */
 };
+
+/* ---- tensor-parallel exchange through peer memory --------------------------
+ * Replaces the NCCL all-reduce of the o_proj / down_proj partial sums and the
+ * all-reduce MAX of the argmax keys of a vocabulary-sharded lm_head (no
+ * counterpart in the reference, which runs on one device). An exchange is one
+ * all-reduce point of a step. Every rank owns a receive buffer per exchange in
+ * device memory from lw_peer_alloc, which the other ranks map with
+ * lw_peer_export / lw_peer_import (CUDA IPC over NVLink).
+ *
+ * Each value travels as one 8-byte word that also carries a flag, so it is
+ * either wholly old or wholly new (8-byte stores and loads are single-copy
+ * atomic): a partial sum as (flag << 32) | fp32 bits, a key as (flag16 << 48)
+ * | 48-bit key. The producer stores its words straight into every rank's
+ * buffer; the consumer re-reads each word until its flag is this exchange's
+ * flag for this step. No fences, counters or resets are needed.
+ *   flag   = s * tags_per_step + tag + 1 (32-bit; 1 if that wraps to 0)
+ *   flag16 = flag % 65535 + 1
+ * where s = *step, the number of decode steps every rank has completed (the
+ * sampler advances it), and tag numbers the exchange within the step.
+ * Waits are bounded: after timeout_ns the kernel sets *error =
+ * LW_ERR_TIMEOUT and carries on with whatever data is there.
+ * Plain peer loads and stores only (no multicast objects). */
+#define LW_MAX_RANKS 8
+
+typedef struct {
+  int world;            /* ranks taking part, 1..LW_MAX_RANKS */
+  int rank;             /* this rank */
+  void* dst[LW_MAX_RANKS];  /* this rank's slot in rank d's receive buffer (mapped here) */
+  const int* step;      /* device: decode steps completed; the same on every rank */
+  int tag, tags_per_step;
+  int* arrivals;        /* LW_EPI_PEER_ARGMAX: local int, zero before first use and left zero */
+} lw_exchange_out;
+
+typedef struct {
+  int world;
+  int tag, tags_per_step;
+  const void* src;      /* local receive buffer: the world ranks' slots */
+  const int* step;
+  int* error;           /* device: set to LW_ERR_TIMEOUT when a wait gives up (may be NULL) */
+  long long timeout_ns; /* wait limit */
+} lw_exchange_in;
 
 typedef struct {
   int bits;          /* 4, 8 (liteweight formats) or 16 (fp16 weight) */
@@ -172,6 +220,8 @@ typedef struct {
   unsigned long long* argmax_keys; /* [M], zero before the launch (LW_EPI_ARGMAX) */
   void* workspace;      /* as for lw_gemm_w8a16 */
   size_t workspace_bytes;
+  const lw_exchange_in* xin;    /* LW_PRO_PEER_RESID_NORM; read at the call */
+  const lw_exchange_out* xout;  /* LW_EPI_PEER_*; read at the call */
 } lw_fused_gemv_args;
 
 int lw_fused_gemv(const lw_fused_gemv_args* args, lw_stream_t stream);
@@ -195,7 +245,8 @@ typedef struct {
 int lw_attention_decode(const lw_attention_args* args, lw_stream_t stream);
 
 /* sizeof(lw_fused_gemv_args) for which = 0, sizeof(lw_attention_args) for
- * which = 1, else 0: lets a binding check its struct layout at load time. */
+ * which = 1, sizeof(lw_exchange_out) for 2, sizeof(lw_exchange_in) for 3,
+ * else 0: lets a binding check its struct layouts at load time. */
 size_t lw_struct_size(int which);
 
 /* x[b] = embed[tokens[*pos][b]] (tokens int32 [max_seq+1][batch]). */
@@ -205,9 +256,27 @@ int lw_embed_tokens(const int* tokens, const void* embed, void* x, const int* po
 /* Next token per sequence: tokens[*pos+1][b] if it is >= 0 (a prompt token),
  * else the argmax decoded from keys[b], which is then stored there; writes
  * its embedding to x, clears keys and advances *pos by one (done: an int
- * kept zero between calls). generate.py:49-52 (greedy pick). */
+ * kept zero between calls). generate.py:49-52 (greedy pick).
+ * step (may be NULL): advanced by one with *pos; never reset, it numbers the
+ * steps for the exchanges. xin (may be NULL): the pick is the maximum of the
+ * world ranks' keys of a tensor-parallel exchange (src = flagged words
+ * [world][batch]), each read once its flag is current; keys (this rank's
+ * lm_head keys) is still cleared. */
 int lw_sample_tokens(int* tokens, unsigned long long* keys, const void* embed, void* x, int* pos, int* done,
-                     int batch, int hidden, int pdl, lw_stream_t stream);
+                     int* step, const lw_exchange_in* xin, int batch, int hidden, int pdl, lw_stream_t stream);
+
+/* ---- peer memory for the exchanges (setup calls: these allocate, map and
+ * synchronise; they are not stream-ordered and must not be graph-captured) */
+
+/* cudaMalloc'd, zeroed device memory that other processes can map. */
+int lw_peer_alloc(size_t bytes, void** ptr);
+int lw_peer_free(void* ptr);
+/* Bytes of the opaque handle lw_peer_export writes (a cudaIpcMemHandle_t). */
+size_t lw_peer_handle_size(void);
+int lw_peer_export(void* ptr, void* handle);
+/* Map another process's lw_peer_alloc block on this process's current device. */
+int lw_peer_import(const void* handle, void** ptr);
+int lw_peer_close(void* ptr);
 
 #ifdef __cplusplus
 }

@@ -15,9 +15,10 @@
 // embedding as the next step's residual stream and advances the position.
 // Every kernel reads the position from device memory, so one captured CUDA
 // graph replays any step. With tensor parallelism the o/down projections
-// write fp32 partial sums instead (all-reduced by the caller) and the next
-// norm prologue adds them to the residual.
-#include "gemv_host.cuh"
+// produce fp32 partial sums instead, either written locally for an NCCL
+// all-reduce by the caller or pushed to every rank through peer memory
+// (decode_tp.cu), and the next norm prologue adds their sum to the residual.
+#include "fused_host.cuh"
 
 #include <cooperative_groups.h>
 #include <type_traits>
@@ -217,34 +218,67 @@ __global__ void embed_kernel(const int* __restrict__ tokens, const __half* __res
 // table holds one (>= 0, a prompt token), else the argmax of the logits
 // (first index of the maximum, torch.argmax semantics; generate.py:51-52).
 // Writes it to the table, loads its embedding as the next residual stream,
-// clears the argmax key and, in the last block to finish, advances *pos.
-__global__ void sample_kernel(int* __restrict__ tokens, unsigned long long* __restrict__ keys,
-                              const __half* __restrict__ embed, __half* __restrict__ x, int* pos,
-                              int* done, int B, int H) {
+// clears the argmax key and, in the last block to finish, advances *pos (and
+// *step). With a tensor-parallel exchange the keys are max'd in by every
+// rank's lm_head: wait until all of them have arrived.
+struct SampleParams {
+  int* tokens;
+  unsigned long long* keys;
+  const __half* embed;
+  __half* x;
+  int* pos;
+  int* done;
+  int* step;             // may be null
+  int B, H;
+  int in_world;          // 0: the local keys are the pick
+  int in_tag, in_tags;
+  const unsigned long long* in_src;  // flagged keys [in_world][B]
+  int* in_error;
+  long long in_timeout_ns;
+};
+
+__global__ void sample_kernel(const SampleParams p) {
   pdl_wait();
   __shared__ int s_tok;
   const int b = blockIdx.x;
-  const int p_next = *pos + 1;
+  const int p_next = *p.pos + 1;
   if (threadIdx.x == 0) {
-    int tok = tokens[(size_t)p_next * B + b];
+    int tok = p.tokens[(size_t)p_next * p.B + b];
     if (tok < 0) {
-      tok = (int)(0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull));
-      tokens[(size_t)p_next * B + b] = tok;
+      unsigned long long key = 0;
+      if (p.in_world) {
+        // the maximum of every rank's key, each read once its flag is current
+        const unsigned long long f16 = exchange_flag16(exchange_flag(*p.step, p.in_tag, p.in_tags));
+        WaitBudget wb;
+        for (int r = 0; r < p.in_world; ++r) {
+          unsigned long long w;
+          do {
+            w = ld_volatile_u64(p.in_src + (size_t)r * p.B + b);
+          } while ((w >> 48) != f16 && wb.keep_waiting(p.in_timeout_ns, p.in_error));
+          w &= 0xFFFFFFFFFFFFull;
+          key = w > key ? w : key;
+        }
+      } else {
+        key = __ldcg(p.keys + b);
+      }
+      tok = (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+      p.tokens[(size_t)p_next * p.B + b] = tok;
     }
-    keys[b] = 0ull;
+    p.keys[b] = 0ull;
     s_tok = tok;
   }
   __syncthreads();
-  const uint4* src = reinterpret_cast<const uint4*>(embed + (size_t)s_tok * H);
-  uint4* dst = reinterpret_cast<uint4*>(x + (size_t)b * H);
-  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+  const uint4* src = reinterpret_cast<const uint4*>(p.embed + (size_t)s_tok * p.H);
+  uint4* dst = reinterpret_cast<uint4*>(p.x + (size_t)b * p.H);
+  for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = src[i];
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const int old = atomicAdd(done, 1);
-    if (old == B - 1) {
-      *pos = p_next;
-      *done = 0;
+    const int old = atomicAdd(p.done, 1);
+    if (old == p.B - 1) {
+      *p.pos = p_next;
+      if (p.step) *p.step += 1;
+      *p.done = 0;
     }
   }
 }
@@ -257,50 +291,6 @@ namespace {
 
 inline bool al(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-lw::StreamParams to_stream(const lw_fused_gemv_args* a) {
-  lw::StreamParams p = {};
-  p.act = static_cast<const __half*>(a->act);
-  p.w = static_cast<const uint8_t*>(a->weight);
-  p.scales = static_cast<const __half*>(a->scales);
-  p.bias = static_cast<const __half*>(a->bias);
-  p.residual = static_cast<const __half*>(a->residual);
-  p.out = static_cast<__half*>(a->out);
-  p.lda = a->lda;
-  p.ldo = a->ldo;
-  p.M = a->M;
-  p.N = a->N;
-  p.K = a->K;
-  p.G = a->bits == 16 ? a->K : a->group_size;
-  p.gamma = static_cast<const __half*>(a->gamma);
-  p.eps = a->eps;
-  p.psum = a->psum;
-  p.x_out = static_cast<__half*>(a->x_out);
-  p.rope_cos = static_cast<const __half*>(a->rope_cos);
-  p.rope_sin = static_cast<const __half*>(a->rope_sin);
-  p.pos = a->pos;
-  p.head_dim = a->head_dim;
-  p.n_q_heads = a->n_q_heads;
-  p.n_kv_heads = a->n_kv_heads;
-  p.max_seq = a->max_seq;
-  p.q_out = static_cast<__half*>(a->q_out);
-  p.k_cache = static_cast<__half*>(a->k_cache);
-  p.v_cache = static_cast<__half*>(a->v_cache);
-  p.out_f32 = a->out_f32;
-  p.argmax_keys = a->argmax_keys;
-  p.argmax_offset = a->argmax_offset;
-  return p;
-}
-
-template <int BITS, int PRO, int EPI>
-cudaError_t fused_launch(const lw_fused_gemv_args* a, cudaStream_t s) {
-  return lw::launch_stream_block<BITS, PRO, EPI>(to_stream(a), a->workspace, a->workspace_bytes, s, a->pdl != 0,
-                                                a->fold_scales != 0);
-}
-
-template <int BITS, int PRO, int EPI>
-size_t fused_ws(const lw_fused_gemv_args* a) {
-  return lw::stream_workspace<BITS, PRO, EPI>(a->M, a->N, a->K);
-}
 
 // The (bits, prologue, epilogue) combinations the decode step uses.
 #define LW_FUSED_TABLE(X)                                   \
@@ -336,8 +326,32 @@ int validate(const lw_fused_gemv_args* a) {
     if (!a->gamma || !al(a->gamma, 16)) return LW_ERR_NULL_POINTER;
     if (a->prologue == LW_PRO_RESID_NORM && (!a->psum || !a->x_out || !al(a->psum, 16) || !al(a->x_out, 16)))
       return LW_ERR_NULL_POINTER;
+    if (a->prologue == LW_PRO_PEER_RESID_NORM) {
+      const lw_exchange_in* x = a->xin;
+      if (!x || !x->src || !x->step || !a->x_out) return LW_ERR_NULL_POINTER;
+      if (x->world < 1 || x->world > LW_MAX_RANKS || x->timeout_ns <= 0 || x->tags_per_step <= 0 ||
+          x->tag < 0 || x->tag >= x->tags_per_step)
+        return LW_ERR_BAD_SHAPE;
+      if (!al(x->src, 16) || !al(a->x_out, 16)) return LW_ERR_ALIGNMENT;
+    }
+  }
+  if (a->epilogue == LW_EPI_PEER_F32 || a->epilogue == LW_EPI_PEER_ARGMAX) {
+    const lw_exchange_out* x = a->xout;
+    if (!x || !x->step) return LW_ERR_NULL_POINTER;
+    if (x->world < 1 || x->world > LW_MAX_RANKS || x->rank < 0 || x->rank >= x->world ||
+        x->tags_per_step <= 0 || x->tag < 0 || x->tag >= x->tags_per_step)
+      return LW_ERR_BAD_SHAPE;
+    for (int d = 0; d < x->world; ++d) {
+      if (!x->dst[d]) return LW_ERR_NULL_POINTER;
+      if (!al(x->dst[d], 8)) return LW_ERR_ALIGNMENT;
+    }
+    if (a->epilogue == LW_EPI_PEER_F32 && a->ldo < a->N) return LW_ERR_BAD_SHAPE;
+    if (a->epilogue == LW_EPI_PEER_ARGMAX && (!a->out || !a->argmax_keys || !x->arrivals)) return LW_ERR_NULL_POINTER;
   }
   switch (a->epilogue) {
+    case LW_EPI_PEER_F32:
+    case LW_EPI_PEER_ARGMAX:
+      break;
     case LW_EPI_PLAIN:
       if (!a->out) return LW_ERR_NULL_POINTER;
       break;
@@ -401,10 +415,11 @@ int lw_fused_gemv(const lw_fused_gemv_args* a, lw_stream_t stream) {
 #define X(B_, P_, E_)                                                         \
   if (!found && a->bits == B_ && a->prologue == P_ && a->epilogue == E_) {  \
     found = true;                                                           \
-    e = fused_launch<B_, P_, E_>(a, s);                                     \
+    e = lw::fused_launch<B_, P_, E_>(a, s);                                 \
   }
   LW_FUSED_TABLE(X)
 #undef X
+  if (!found) found = lw::tp_fused_launch(a, s, &e);
   if (!found) return LW_ERR_UNSUPPORTED;
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
@@ -417,10 +432,11 @@ size_t lw_fused_gemv_workspace_size(const lw_fused_gemv_args* a) {
 #define X(B_, P_, E_)                                                         \
   if (!found && a->bits == B_ && a->prologue == P_ && a->epilogue == E_) {  \
     found = true;                                                           \
-    r = fused_ws<B_, P_, E_>(a);                                            \
+    r = lw::fused_ws<B_, P_, E_>(a);                                        \
   }
   LW_FUSED_TABLE(X)
 #undef X
+  if (!found) lw::tp_fused_ws(a, &r);
   return r;
 }
 
@@ -461,6 +477,8 @@ int lw_attention_decode(const lw_attention_args* a, lw_stream_t stream) {
 size_t lw_struct_size(int which) {
   if (which == 0) return sizeof(lw_fused_gemv_args);
   if (which == 1) return sizeof(lw_attention_args);
+  if (which == 2) return sizeof(lw_exchange_out);
+  if (which == 3) return sizeof(lw_exchange_in);
   return 0;
 }
 
@@ -478,14 +496,36 @@ int lw_embed_tokens(const int* tokens, const void* embed, void* x, const int* po
 }
 
 int lw_sample_tokens(int* tokens, unsigned long long* keys, const void* embed, void* x, int* pos, int* done,
-                     int batch, int hidden, int pdl, lw_stream_t stream) {
+                     int* step, const lw_exchange_in* xin, int batch, int hidden, int pdl, lw_stream_t stream) {
   if (!tokens || !keys || !embed || !x || !pos || !done) return LW_ERR_NULL_POINTER;
   if (batch <= 0 || hidden <= 0 || hidden % 8) return LW_ERR_BAD_SHAPE;
   if (!al(embed, 16) || !al(x, 16)) return LW_ERR_ALIGNMENT;
+  lw::SampleParams p = {};
+  p.tokens = tokens;
+  p.keys = keys;
+  p.embed = static_cast<const __half*>(embed);
+  p.x = static_cast<__half*>(x);
+  p.pos = pos;
+  p.done = done;
+  p.step = step;
+  p.B = batch;
+  p.H = hidden;
+  if (xin) {
+    if (!xin->src || !step) return LW_ERR_NULL_POINTER;
+    if (xin->world < 1 || xin->world > LW_MAX_RANKS || xin->timeout_ns <= 0 || xin->tags_per_step <= 0 ||
+        xin->tag < 0 || xin->tag >= xin->tags_per_step)
+      return LW_ERR_BAD_SHAPE;
+    if (!al(xin->src, 8)) return LW_ERR_ALIGNMENT;
+    p.in_world = xin->world;
+    p.in_tag = xin->tag;
+    p.in_tags = xin->tags_per_step;
+    p.in_src = static_cast<const unsigned long long*>(xin->src);
+    p.in_error = xin->error;
+    p.in_timeout_ns = xin->timeout_ns;
+  }
   cudaGetLastError();
   cudaError_t e = lw_launch(lw::sample_kernel, dim3(batch), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
-                            pdl != 0, tokens, keys, static_cast<const __half*>(embed), static_cast<__half*>(x), pos,
-                            done, batch, hidden);
+                            pdl != 0, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
 }

@@ -337,7 +337,7 @@ const char* lw_status_string(int status) {
   }
 }
 
-int lw_abi_version(void) { return 100; }
+int lw_abi_version(void) { return 110; }
 
 unsigned long long lw_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 

@@ -53,8 +53,14 @@ struct WT<16> {
   static constexpr int E = 8;
 };
 
-enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_RESID_NORM = 2 };
-enum { EPI_PLAIN = 0, EPI_ROPE_KV = 1, EPI_SWIGLU = 2, EPI_F32 = 3, EPI_ARGMAX = 4 };
+enum { PRO_PLAIN = 0, PRO_NORM = 1, PRO_RESID_NORM = 2, PRO_PEER_RESID_NORM = 3 };
+enum { EPI_PLAIN = 0, EPI_ROPE_KV = 1, EPI_SWIGLU = 2, EPI_F32 = 3, EPI_ARGMAX = 4, EPI_PEER_F32 = 5,
+       EPI_PEER_ARGMAX = 6 };
+
+template <int PRO>
+constexpr bool kResidPro = PRO == PRO_RESID_NORM || PRO == PRO_PEER_RESID_NORM;
+template <int EPI>
+constexpr bool kPeerEpi = EPI == EPI_PEER_F32 || EPI == EPI_PEER_ARGMAX;
 
 constexpr int kStreamThreads = 256;
 #ifndef LW_STREAM_MIN_BLOCKS
@@ -102,6 +108,17 @@ struct StreamParams {
   float* slots;            // [tiles][max_slots][32 lanes][4 * MT]
   int* counters;           // [tiles], zero before the first launch, left zero
   int max_slots;
+  // tensor-parallel exchange, consumer (PRO_PEER_RESID_NORM): flagged words
+  int in_world, in_tag, in_tags;
+  const unsigned long long* in_src;    // local [in_world][M][K]
+  const int* in_step;                  // decode steps completed
+  int* in_error;
+  long long in_timeout_ns;
+  // tensor-parallel exchange, producer (EPI_PEER_*)
+  int out_world, out_tag, out_tags;
+  const int* out_step;
+  unsigned long long* out_dst[kMaxRanks];  // this rank's slot on rank d: [M][ldo] or [M] words
+  int* out_arrivals;                   // EPI_PEER_ARGMAX: local, zero, left zero
 };
 
 LW_DEV uint32_t bcast_h(const __half* p) {
@@ -223,10 +240,10 @@ LW_DEV float silu_f32(float x) { return x / (1.0f + expf(-x)); }
 // Epilogue for one tile: v[mt][i] holds D(row, col) with rows n_lo = 16*tile +
 // g (i = 0, 1) and n_hi = n_lo + 8 (i = 2, 3), cols m = 8*mt + 2t (+1 for odd i).
 template <int MT, int EPI>
-LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4], int lane) {
+LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4], int lane, uint32_t flag) {
   const int g = lane >> 2, t = lane & 3;
   const int n_lo = tile * 16 + g, n_hi = n_lo + 8;
-  if constexpr (EPI == EPI_PLAIN || EPI == EPI_F32) {
+  if constexpr (EPI == EPI_PLAIN || EPI == EPI_F32 || EPI == EPI_PEER_F32) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -236,6 +253,12 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
         if (m < p.M && n < p.N) {
           if constexpr (EPI == EPI_F32) {
             p.out_f32[(size_t)m * p.ldo + n] = v[mt][i];
+          } else if constexpr (EPI == EPI_PEER_F32) {
+            // straight into every rank's receive buffer (peer stores over NVLink)
+            const unsigned long long word = ((unsigned long long)flag << 32) | __float_as_uint(v[mt][i]);
+#pragma unroll
+            for (int d = 0; d < kMaxRanks; ++d)
+              if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + (size_t)m * p.ldo + n, word);
           } else {
             float y = r16(v[mt][i]);
             if (p.bias) y = r16(y + __half2float(p.bias[n]));
@@ -295,7 +318,7 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
         const float a = r16(silu_f32(gt));
         p.out[(size_t)m * p.ldo + i_out] = __float2half_rn(a * up);
       }
-  } else if constexpr (EPI == EPI_ARGMAX) {
+  } else if constexpr (EPI == EPI_ARGMAX || EPI == EPI_PEER_ARGMAX) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -423,6 +446,12 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
 
   pdl_wait();
 
+  // the previous kernels are complete: the step number is final
+  uint32_t in_flag = 0, out_flag = 0;
+  if constexpr (PRO == PRO_PEER_RESID_NORM) in_flag = exchange_flag(*p.in_step, p.in_tag, p.in_tags);
+  if constexpr (kPeerEpi<EPI>) out_flag = exchange_flag(*p.out_step, p.out_tag, p.out_tags);
+  WaitBudget wb;
+
   // ---- stage the activation (M rows, K padded to the chunk) in lane order
   {
     const int groups8 = C * KC / 8;
@@ -437,11 +466,27 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
         uint4 v = make_uint4(0, 0, 0, 0);
         if (k < p.K) {
           v = ldg_nc(p.act + (size_t)m * p.lda + k);
-          if constexpr (PRO == PRO_RESID_NORM) {
+          if constexpr (kResidPro<PRO>) {
             // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
-            const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
-            const float ps[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            float ps[8];
+            if constexpr (PRO == PRO_RESID_NORM) {
+              const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
+              const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
+              ps[0] = a.x; ps[1] = a.y; ps[2] = a.z; ps[3] = a.w;
+              ps[4] = b.x; ps[5] = b.y; ps[6] = b.z; ps[7] = b.w;
+            } else {
+              // the all-reduce itself: the world partials, summed in rank order,
+              // each word read once it carries this step's flag
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+              for (int r = 0; r < p.in_world; ++r) {
+                float pr[8];
+                read_flagged8(p.in_src + ((size_t)r * p.M + m) * p.K + k, in_flag, pr, wb, p.in_timeout_ns,
+                              p.in_error);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ps[e] += pr[e];
+              }
+            }
             __half* hv = reinterpret_cast<__half*>(&v);
 #pragma unroll
             for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
@@ -502,7 +547,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   auto flush = [&](int tile, int end_c) {
     const bool whole = (seg_c0 == 0) && (end_c == C);
     if (whole) {
-      finish_tile<MT, EPI>(p, tile, acc, lane);
+      finish_tile<MT, EPI>(p, tile, acc, lane, out_flag);
     } else {
       const int first = (tile * C) / p.per;
       const int last = ((tile + 1) * C - 1) / p.per;
@@ -531,7 +576,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
             sum[mt][3] += f.w;
           }
         }
-        finish_tile<MT, EPI>(p, tile, sum, lane);
+        finish_tile<MT, EPI>(p, tile, sum, lane, out_flag);
         if (lane == 0) p.counters[tile] = 0;
       }
     }
@@ -584,6 +629,28 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
     if (nB) {
       load(tB, cB, nB, qa1, qb1, sa1, sb1);
       prefetch_next();
+    }
+  }
+  if constexpr (EPI == EPI_PEER_ARGMAX) {
+    // The last CTA to finish (every CTA's atomicMax is then in the local keys)
+    // sends this rank's keys to every rank as flagged words.
+    __shared__ int s_last;
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      s_last = atomicAdd(p.out_arrivals, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const unsigned long long f16 = (unsigned long long)exchange_flag16(out_flag) << 48;
+      for (int m = tid; m < p.M; m += kStreamThreads) {
+        const unsigned long long word = (__ldcg(p.argmax_keys + m) & 0xFFFFFFFFFFFFull) | f16;
+#pragma unroll
+        for (int d = 0; d < kMaxRanks; ++d)
+          if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + m, word);
+      }
+      if (tid == 0) *p.out_arrivals = 0;
     }
   }
   pdl_launch_dependents();

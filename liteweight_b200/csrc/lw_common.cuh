@@ -62,6 +62,77 @@ LW_DEV void prefetch_l2_line(const void* p) { asm volatile("prefetch.global.L2 [
 LW_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 LW_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ---------------------------------------------------------------- peer exchange
+
+constexpr int kMaxRanks = LW_MAX_RANKS;
+
+// Flag of exchange `tag` at step `step` (never 0: receive buffers start zeroed).
+LW_DEV uint32_t exchange_flag(int step, int tag, int tags_per_step) {
+  const uint32_t f = (uint32_t)step * (uint32_t)tags_per_step + (uint32_t)tag + 1u;
+  return f ? f : 1u;
+}
+LW_DEV uint32_t exchange_flag16(uint32_t flag) { return flag % 65535u + 1u; }
+
+// 8-byte stores / loads that are single-copy atomic and coherent at system
+// scope (the word may live on, or be written from, another GPU).
+LW_DEV void st_relaxed_sys_u64(void* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+LW_DEV void ld_volatile_v2u64(const void* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+LW_DEV unsigned long long ld_volatile_u64(const void* p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+LW_DEV unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// A thread's bounded wait for flagged words: `live` turns false, for good,
+// once the thread has waited timeout_ns in total (from its first miss) or
+// kMaxIters polls; *error is then set to LW_ERR_TIMEOUT. A thread that gave
+// up reads what is there without waiting.
+struct WaitBudget {
+  unsigned long long t0 = 0;
+  uint32_t iters = 0;
+  bool live = true;
+  LW_DEV bool keep_waiting(long long timeout_ns, int* error) {
+    constexpr uint32_t kMaxIters = 1u << 24;
+    if (!live) return false;
+    if (t0 == 0) t0 = globaltimer_ns();
+    ++iters;
+    if ((iters & 63u) == 0u &&
+        ((long long)(globaltimer_ns() - t0) > timeout_ns || iters >= kMaxIters)) {
+      live = false;
+      if (error) atomicExch(error, (int)LW_ERR_TIMEOUT);
+      return false;
+    }
+    if (iters > 256u) __nanosleep(64);
+    return true;
+  }
+};
+
+// 8 consecutive flagged fp32 words whose flags all equal `flag` (bounded).
+LW_DEV void read_flagged8(const unsigned long long* src, uint32_t flag, float (&v)[8], WaitBudget& wb,
+                          long long timeout_ns, int* error) {
+  unsigned long long w[8];
+  for (;;) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ld_volatile_v2u64(src + 2 * i, w[2 * i], w[2 * i + 1]);
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ok &= (uint32_t)(w[i] >> 32) == flag;
+    if (ok || !wb.keep_waiting(timeout_ns, error)) break;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float((uint32_t)w[i]);
+}
+
 // ---------------------------------------------------------------- tensor core
 
 // D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col).

@@ -18,9 +18,13 @@ KVCache, generate.py:22-25).
 
 Tensor parallelism (``tp_size > 1``, one process per GPU): q/k/v and gate/up
 are split by output rows (heads / intermediate), o and down by input
-columns; o/down write fp32 partial sums that an NCCL all-reduce sums, and the
-next norm prologue adds them to the residual. The lm_head is split by
-vocabulary rows; the per-rank argmax keys are max-reduced.
+columns, the lm_head by vocabulary rows. The o/down fp32 partial sums and
+the per-rank argmax keys are all-reduced, by default through peer memory
+inside the kernels (``exchange="peer"``: the producing GEMV stores its
+partial into every rank's receive buffer over NVLink, the next norm prologue
+waits for all of them and sums them in rank order; include/liteweight_b200.h,
+tensor-parallel exchange), or by NCCL all-reduces between the kernels
+(``exchange="nccl"``).
 """
 
 from __future__ import annotations
@@ -34,8 +38,27 @@ from liteweight_b200 import _native as nat
 
 c_int, c_void_p, c_float, c_size_t = ctypes.c_int, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
 
-PRO_PLAIN, PRO_NORM, PRO_RESID_NORM = 0, 1, 2
-EPI_PLAIN, EPI_ROPE_KV, EPI_SWIGLU, EPI_F32, EPI_ARGMAX = 0, 1, 2, 3, 4
+PRO_PLAIN, PRO_NORM, PRO_RESID_NORM, PRO_PEER_RESID_NORM = 0, 1, 2, 3
+EPI_PLAIN, EPI_ROPE_KV, EPI_SWIGLU, EPI_F32, EPI_ARGMAX, EPI_PEER_F32, EPI_PEER_ARGMAX = 0, 1, 2, 3, 4, 5, 6
+MAX_RANKS = 8
+
+
+class ExchangeOut(ctypes.Structure):
+    """Mirror of lw_exchange_out (include/liteweight_b200.h)."""
+    _fields_ = [("world", c_int), ("rank", c_int), ("dst", c_void_p * MAX_RANKS), ("step", c_void_p),
+                ("tag", c_int), ("tags_per_step", c_int), ("arrivals", c_void_p)]
+
+
+class ExchangeIn(ctypes.Structure):
+    """Mirror of lw_exchange_in (include/liteweight_b200.h)."""
+    _fields_ = [("world", c_int), ("tag", c_int), ("tags_per_step", c_int), ("src", c_void_p), ("step", c_void_p),
+                ("error", c_void_p), ("timeout_ns", ctypes.c_longlong)]
+
+
+def exchange_flag(step: int, tag: int, tags_per_step: int) -> int:
+    """Flag word of exchange `tag` at step `step` (as the kernels compute it)."""
+    f = (step * tags_per_step + tag + 1) & 0xFFFFFFFF
+    return f or 1
 
 
 class FusedGemvArgs(ctypes.Structure):
@@ -51,6 +74,7 @@ class FusedGemvArgs(ctypes.Structure):
         ("q_out", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
         ("out_f32", c_void_p), ("argmax_keys", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("xin", c_void_p), ("xout", c_void_p),
     ]
 
 
@@ -67,14 +91,20 @@ nat.register("lw_fused_gemv", [ctypes.POINTER(FusedGemvArgs), c_void_p])
 nat.register("lw_fused_gemv_workspace_size", [ctypes.POINTER(FusedGemvArgs)], c_size_t)
 nat.register("lw_attention_decode", [ctypes.POINTER(AttentionArgs), c_void_p])
 nat.register("lw_embed_tokens", [c_void_p] * 4 + [c_int] * 3 + [c_void_p])
-nat.register("lw_sample_tokens", [c_void_p] * 6 + [c_int] * 3 + [c_void_p])
+nat.register("lw_sample_tokens", [c_void_p] * 8 + [c_int] * 3 + [c_void_p])
 nat.register("lw_struct_size", [c_int], c_size_t)
+nat.register("lw_peer_alloc", [c_size_t, ctypes.POINTER(c_void_p)])
+nat.register("lw_peer_free", [c_void_p])
+nat.register("lw_peer_handle_size", [], c_size_t)
+nat.register("lw_peer_export", [c_void_p, c_void_p])
+nat.register("lw_peer_import", [c_void_p, ctypes.POINTER(c_void_p)])
+nat.register("lw_peer_close", [c_void_p])
 
 
 def check_abi() -> None:
     """The ctypes mirrors must have the library's struct sizes."""
     lib = nat.lib()
-    for which, cls in ((0, FusedGemvArgs), (1, AttentionArgs)):
+    for which, cls in ((0, FusedGemvArgs), (1, AttentionArgs), (2, ExchangeOut), (3, ExchangeIn)):
         got = int(lib.lw_struct_size(which))
         if got != ctypes.sizeof(cls):
             raise RuntimeError(f"{cls.__name__}: ctypes size {ctypes.sizeof(cls)} != library size {got}")
@@ -209,13 +239,109 @@ def default_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
 
 # ------------------------------------------------------------------ engine
 
+def _align(v: int, a: int) -> int:
+    return (v + a - 1) // a * a
+
+
+class PeerExchange:
+    """Receive buffers of every exchange of one rank's decode step, in one
+    block of device memory that the other ranks map (CUDA IPC), plus this
+    rank's mappings of their blocks.
+
+    Values travel as flagged 8-byte words (include/liteweight_b200.h,
+    tensor-parallel exchange). Block layout (bytes): keys [world][batch] words
+    | two slot sets, each [world][batch][hidden] words. Partial-sum exchange e
+    (o_proj of layer e // 2, or its down_proj) uses slot set e % 2: a rank can
+    only be one exchange ahead of another (it cannot produce exchange e + 1
+    before it has consumed e, which needs every rank's e), so a set is never
+    overwritten while a rank still reads it, and the flags tell a word of
+    exchange e from one of e - 2. The keys exchange is the last tag.
+    """
+
+    def __init__(self, group, rank: int, world: int, batch: int, hidden: int, n_partial: int, device,
+                 timeout_s: float = 10.0):
+        assert 1 <= world <= MAX_RANKS
+        self.rank, self.world, self.group, self.device = rank, world, group, torch.device(device)
+        self.n_partial = n_partial
+        self.tags = n_partial + 1
+        self.slot_off = _align(8 * world * batch, 256)
+        self.set_bytes = _align(8 * world * batch * hidden, 256)
+        self.part_bytes = 8 * batch * hidden
+        self.total = self.slot_off + 2 * self.set_bytes
+        lib = nat.lib()
+        with torch.cuda.device(self.device):
+            ptr = c_void_p()
+            nat.check("lw_peer_alloc", lib.lw_peer_alloc(self.total, ctypes.byref(ptr)))
+            self.base = ptr.value
+            handle = (ctypes.c_ubyte * int(lib.lw_peer_handle_size()))()
+            nat.check("lw_peer_export", lib.lw_peer_export(self.base, handle))
+            handles = [None] * world
+            torch.distributed.all_gather_object(handles, bytes(handle), group=group)
+            self.peers = []
+            for d in range(world):
+                if d == rank:
+                    self.peers.append(self.base)
+                    continue
+                q = c_void_p()
+                nat.check("lw_peer_import", lib.lw_peer_import(handles[d], ctypes.byref(q)))
+                self.peers.append(q.value)
+        self.step = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.error = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.arrivals = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.outs, self.ins = [], []
+        for e in range(self.tags):
+            out = ExchangeOut(world=world, rank=rank, step=self.step.data_ptr(), tag=e, tags_per_step=self.tags,
+                              arrivals=self.arrivals.data_ptr())
+            for d in range(world):
+                own = self.part_bytes * rank if e < n_partial else 8 * batch * rank
+                out.dst[d] = self.peers[d] + self._recv_offset(e) + own
+            self.outs.append(out)
+            self.ins.append(ExchangeIn(world=world, tag=e, tags_per_step=self.tags,
+                                       src=self.base + self._recv_offset(e), step=self.step.data_ptr(),
+                                       error=self.error.data_ptr(), timeout_ns=int(timeout_s * 1e9)))
+        self.closed = False
+
+    def _recv_offset(self, e: int) -> int:
+        return self.slot_off + (e % 2) * self.set_bytes if e < self.n_partial else 0
+
+    def out_ptr(self, e: int) -> int:
+        return ctypes.addressof(self.outs[e])
+
+    def in_ptr(self, e: int) -> int:
+        return ctypes.addressof(self.ins[e])
+
+    def check(self) -> None:
+        """Raise if a device-side wait of an exchange gave up (a rank stopped producing)."""
+        err = int(self.error.item())
+        if err:
+            raise nat.LiteweightError("peer exchange", err, "a wait for another rank timed out")
+
+    def close(self) -> None:
+        """Unmap the other ranks' blocks and free this one. Collective: every
+        rank calls it after its last step (barriers keep a block alive until no
+        rank can still write into it)."""
+        if self.closed:
+            return
+        lib = nat.lib()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            torch.distributed.barrier(group=self.group)
+            for d, p in enumerate(self.peers):
+                if d != self.rank:
+                    nat.check("lw_peer_close", lib.lw_peer_close(p))
+            torch.distributed.barrier(group=self.group)
+            nat.check("lw_peer_free", lib.lw_peer_free(self.base))
+        self.closed = True
+
+
 class DecodeEngine:
     """Batched greedy decode of a Llama model on one GPU (or one tensor-parallel rank)."""
 
     def __init__(self, spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
                  lm_head: torch.Tensor | None, rope_cos: torch.Tensor, rope_sin: torch.Tensor, batch: int,
                  max_seq: int, device=None, tp_rank: int = 0, tp_size: int = 1, tp_group=None, pdl: bool = True,
-                 fold_scales: bool = False):
+                 fold_scales: bool = False, exchange: str = "peer", exchange_timeout_s: float = 10.0):
+        assert exchange in ("peer", "nccl")
         self.spec, self.B, self.S = spec, batch, max_seq
         self.fold = int(fold_scales)
         self.device = torch.device(device) if device is not None else embed.device
@@ -251,6 +377,12 @@ class DecodeEngine:
         self.done = torch.zeros(1, dtype=torch.int32, device=dev)
         self.keys = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.tokens = torch.full((max_seq + 1, batch), -1, dtype=torch.int32, device=dev)
+        self.step_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.exchange = None
+        if tp_size > 1 and exchange == "peer":
+            self.exchange = PeerExchange(tp_group, tp_rank, tp_size, batch, H, 2 * len(layers), dev,
+                                         exchange_timeout_s)
+            self.step_count = self.exchange.step
         self._build_calls()
         self.graph = None
         self.host_pos = 0
@@ -266,21 +398,31 @@ class DecodeEngine:
     def _build_calls(self):
         sp, B, H, hd = self.spec, self.B, self.spec.hidden, self.spec.head_dim
         tp = self.tp_size > 1
+        ex = self.exchange
         calls = []
         xs = [self.x, self.x2]
         cur = 0           # index of the buffer holding the residual stream
-        pending = False   # an all-reduced partial waits to be added to the residual
+        pending = None    # exchange whose all-reduced partial waits to be added to the residual
         gemv_args = []
 
         def norm_pro():
             nonlocal cur, pending
-            if pending:
+            if pending is not None:
                 d = dict(prologue=PRO_RESID_NORM, act=xs[cur], psum=self.psum, x_out=xs[1 - cur], lda=H)
+                if ex is not None:
+                    d.update(prologue=PRO_PEER_RESID_NORM, xin=ex.in_ptr(pending))
                 cur = 1 - cur
-                pending = False
+                pending = None
             else:
                 d = dict(prologue=PRO_NORM, act=xs[cur], lda=H)
             return d
+
+        def partial_epi(e):
+            if not tp:
+                return dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
+            if ex is not None:
+                return dict(epilogue=EPI_PEER_F32, xout=ex.out_ptr(e))
+            return dict(epilogue=EPI_F32, out_f32=self.psum)
 
         for li, L in enumerate(self.layers):
             pro = norm_pro()
@@ -296,36 +438,38 @@ class DecodeEngine:
                                batch=B, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
                                pdl=self.pdl)
             calls.append(("attn", at, "attn"))
-            epi = dict(epilogue=EPI_F32, out_f32=self.psum) if tp else \
-                dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
             a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.nq * hd, group_size=sp.group_size,
-                           weight=L.o_w, scales=L.o_s, act=self.attn, lda=self.nq * hd, ldo=H, **epi)
+                           weight=L.o_w, scales=L.o_s, act=self.attn, lda=self.nq * hd, ldo=H,
+                           **partial_epi(2 * li))
             calls.append(("gemv", a, "o"))
             gemv_args.append(a)
             if tp:
-                calls.append(("allreduce", self.psum, "allreduce"))
-                pending = True
+                if ex is None:
+                    calls.append(("allreduce", self.psum, "allreduce"))
+                pending = 2 * li
             pro = norm_pro()
             a = self._gemv(bits=sp.bits, epilogue=EPI_SWIGLU, N=2 * self.inter, K=H, group_size=sp.group_size,
                            weight=L.gu_w, scales=L.gu_s, gamma=L.post_norm, out=self.act, ldo=self.inter, **pro)
             calls.append(("gemv", a, "gu"))
             gemv_args.append(a)
-            epi = dict(epilogue=EPI_F32, out_f32=self.psum) if tp else \
-                dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
             a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
-                           weight=L.d_w, scales=L.d_s, act=self.act, lda=self.inter, ldo=H, **epi)
+                           weight=L.d_w, scales=L.d_s, act=self.act, lda=self.inter, ldo=H,
+                           **partial_epi(2 * li + 1))
             calls.append(("gemv", a, "down"))
             gemv_args.append(a)
             if tp:
-                calls.append(("allreduce", self.psum, "allreduce"))
-                pending = True
+                if ex is None:
+                    calls.append(("allreduce", self.psum, "allreduce"))
+                pending = 2 * li + 1
         pro = norm_pro()
-        a = self._gemv(bits=16, epilogue=EPI_ARGMAX, N=self.vshard, K=H, group_size=H, weight=self.lm_head,
-                       gamma=self.final_norm, out=self.logits, ldo=self.vshard, argmax_keys=self.keys,
-                       argmax_offset=self.tp_rank * self.vshard, **pro)
+        head = dict(epilogue=EPI_ARGMAX, argmax_keys=self.keys)
+        if ex is not None:
+            head.update(epilogue=EPI_PEER_ARGMAX, xout=ex.out_ptr(2 * len(self.layers)))
+        a = self._gemv(bits=16, N=self.vshard, K=H, group_size=H, weight=self.lm_head, gamma=self.final_norm,
+                       out=self.logits, ldo=self.vshard, argmax_offset=self.tp_rank * self.vshard, **head, **pro)
         calls.append(("gemv", a, "lm_head"))
         gemv_args.append(a)
-        if tp:
+        if tp and ex is None:
             calls.append(("allreduce_max", self.keys, "allreduce"))
         calls.append(("sample", None, "sample"))
         # one workspace shared by the sequential GEMVs of a step
@@ -334,7 +478,23 @@ class DecodeEngine:
         for a in gemv_args:
             a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
         self.calls = calls
+        self.stat_args = {id(a): self._stat_variant(a) for a in gemv_args}
         self.x_in = self.x   # layer 0 reads the residual stream from self.x; sample writes it there
+        self.sample_xin = ex.in_ptr(2 * len(self.layers)) if ex is not None else None
+
+    def _stat_variant(self, a: FusedGemvArgs) -> FusedGemvArgs:
+        """The same GEMV with its exchange replaced by local buffers, for timing
+        one kernel class alone (a lone exchange would never be answered)."""
+        if a.prologue != PRO_PEER_RESID_NORM and a.epilogue not in (EPI_PEER_F32, EPI_PEER_ARGMAX):
+            return a
+        b = FusedGemvArgs.from_buffer_copy(a)
+        if b.prologue == PRO_PEER_RESID_NORM:
+            b.prologue, b.psum, b.xin = PRO_RESID_NORM, self.psum.data_ptr(), None
+        if b.epilogue == EPI_PEER_F32:
+            b.epilogue, b.out_f32, b.xout = EPI_F32, self.psum.data_ptr(), None
+        elif b.epilogue == EPI_PEER_ARGMAX:
+            b.epilogue, b.xout = EPI_ARGMAX, None
+        return b
 
     # -------------------------------------------------------------- execution
     def _enqueue_step(self, sample: bool = True):
@@ -352,9 +512,13 @@ class DecodeEngine:
             elif kind == "allreduce_max":
                 torch.distributed.all_reduce(a, op=torch.distributed.ReduceOp.MAX, group=self.tp_group)
             elif kind == "sample":
-                nat.check("lw_sample_tokens", lib.lw_sample_tokens(
-                    self.tokens.data_ptr(), self.keys.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
-                    self.pos.data_ptr(), self.done.data_ptr(), self.B, self.spec.hidden, self.pdl, s))
+                self._sample(s)
+
+    def _sample(self, s):
+        nat.check("lw_sample_tokens", nat.lib().lw_sample_tokens(
+            self.tokens.data_ptr(), self.keys.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
+            self.pos.data_ptr(), self.done.data_ptr(), self.step_count.data_ptr(), self.sample_xin, self.B,
+            self.spec.hidden, self.pdl, s))
 
     def kernels_per_step(self) -> int:
         return sum(1 for k, _, _n in self.calls if k in ("gemv", "attn", "sample"))
@@ -368,7 +532,7 @@ class DecodeEngine:
             if n != name:
                 continue
             if kind == "gemv":
-                nat.check("lw_fused_gemv", lib.lw_fused_gemv(ctypes.byref(a), s))
+                nat.check("lw_fused_gemv", lib.lw_fused_gemv(ctypes.byref(self.stat_args[id(a)]), s))
             elif kind == "attn":
                 nat.check("lw_attention_decode", lib.lw_attention_decode(ctypes.byref(a), s))
 
@@ -379,7 +543,21 @@ class DecodeEngine:
         self.start(input_ids)
         self.capture()
         self.step(input_ids.shape[1] + max_new_tokens - 1)
-        return self.generated(max_new_tokens).to("cpu")
+        out = self.generated(max_new_tokens).to("cpu")
+        self.check()
+        return out
+
+    def check(self) -> None:
+        """Raise if a tensor-parallel exchange wait gave up (reads a device flag: syncs)."""
+        if self.exchange is not None:
+            self.exchange.check()
+
+    def close(self) -> None:
+        """Release the graph and, with a peer exchange, the shared block
+        (collective over the tensor-parallel group)."""
+        self.graph = None
+        if self.exchange is not None:
+            self.exchange.close()
 
     def start(self, prompt: torch.Tensor, forced: torch.Tensor | None = None):
         """Load a prompt (int [B, P]) and optional further forced tokens; position 0."""
@@ -431,12 +609,7 @@ class DecodeEngine:
 
     def pick_next(self):
         """Pick the next token (forced table entry or argmax), embed it, advance."""
-        for kind, a, _name in self.calls:
-            if kind == "sample":
-                s = torch.cuda.current_stream(self.device).cuda_stream
-                nat.check("lw_sample_tokens", nat.lib().lw_sample_tokens(
-                    self.tokens.data_ptr(), self.keys.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
-                    self.pos.data_ptr(), self.done.data_ptr(), self.B, self.spec.hidden, self.pdl, s))
+        self._sample(torch.cuda.current_stream(self.device).cuda_stream)
         self.host_pos += 1
 
     def generated(self, new_tokens: int) -> torch.Tensor:
@@ -505,12 +678,12 @@ def engine_from_hf(model, batch: int, max_seq: int, tp_rank: int = 0, tp_size: i
 def build_engine(spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
                  lm_head: torch.Tensor | None, inv_freq: torch.Tensor, batch: int, max_seq: int, device,
                  attention_scaling: float = 1.0, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
-                 pdl: bool = True, fold_scales: bool = False) -> DecodeEngine:
+                 pdl: bool = True, fold_scales: bool = False, exchange: str = "peer") -> DecodeEngine:
     """Engine from unsharded LayerWeights (liteweight-format tensors, any device)."""
     packed = [PackedLayer(lw, spec, tp_rank, tp_size, device) for lw in layers]
     cos, sin = rope_tables(inv_freq, max_seq, attention_scaling, device)
     return DecodeEngine(spec, packed, embed, final_norm, lm_head, cos, sin, batch, max_seq, device, tp_rank,
-                        tp_size, tp_group, pdl, fold_scales)
+                        tp_size, tp_group, pdl, fold_scales, exchange)
 
 
 def synthetic_layers(spec: LlamaSpec, device, seed: int = 0, std: float = 0.02) -> list:

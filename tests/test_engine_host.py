@@ -13,7 +13,8 @@ from liteweight_b200 import build as lwbuild
 def test_struct_layout_matches_library():
     lwbuild.build()
     E.check_abi()
-    assert ctypes.sizeof(E.FusedGemvArgs) == 224 and ctypes.sizeof(E.AttentionArgs) == 64
+    assert ctypes.sizeof(E.FusedGemvArgs) == 240 and ctypes.sizeof(E.AttentionArgs) == 64
+    assert ctypes.sizeof(E.ExchangeOut) == 96 and ctypes.sizeof(E.ExchangeIn) == 48
 
 
 @pytest.mark.parametrize("hd", [64, 128])
@@ -77,3 +78,12 @@ def test_bytes_per_token_match_the_plan():
     assert abs(b8 / 1e9 - 4.650) < 0.01, b8
     assert abs(b1 / 1e9 - 1.514) < 0.01, b1
     assert abs(b70 / 1e9 - 37.40) < 0.05, b70
+
+
+def test_exchange_flags():
+    """Flags are never 0 (receive buffers start zeroed) and differ between the
+    exchanges of a step and between consecutive steps."""
+    tags = 65
+    seen = {E.exchange_flag(s, t, tags) for s in range(3) for t in range(tags)}
+    assert len(seen) == 3 * tags and 0 not in seen
+    assert E.exchange_flag(0xFFFFFFFF // tags, tags - 1, tags) != 0

@@ -1,0 +1,262 @@
+"""Tensor-parallel decode: the partition algorithm on CPU (gloo) and the engine on two GPUs (NCCL).
+
+The engine splits q/k/v (by heads) and gate/up (by intermediate rows) over
+ranks, o and down by input columns with fp32 partial sums that are
+all-reduced and added to the fp16 residual, and the lm_head by vocabulary
+rows with the greedy pick made by an all-reduce MAX over 64-bit keys
+(fp16 order key << 32 | 0xFFFFFFFF - global index, so ties go to the lowest
+index). The CPU test runs that algorithm in numpy on two gloo ranks, on the
+shard buffers liteweight_b200.engine.PackedLayer builds, and checks the
+logits and greedy tokens against the unsharded oracle decode; the GPU test
+runs the real engine on two GPUs with both all-reduce paths (the in-kernel
+peer-memory exchange and NCCL all-reduces in the step graph).
+"""
+
+import datetime
+import gc
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import llama as ol
+from oracle import quant as oq
+
+F32, F16 = np.float32, np.float16
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def random_model(hidden, inter, layers, heads, kv, hd, vocab, bits, seed) -> ol.LlamaWeights:
+    rng = np.random.default_rng(seed)
+    shape = ol.LlamaShape(hidden=hidden, inter=inter, n_layers=layers, n_heads=heads, n_kv_heads=kv, head_dim=hd,
+                          vocab=vocab)
+    quant = oq.quantize_int4 if bits == 4 else oq.quantize_int8
+
+    def lin(n, k):
+        q, s = quant((rng.standard_normal((n, k)) * 0.02).astype(F16), 128)
+        return ol.QLinear(q, s, bits, 128)
+
+    Ls = [ol.LlamaLayer(in_norm=(1 + 0.1 * rng.standard_normal(hidden)).astype(F16),
+                        post_norm=(1 + 0.1 * rng.standard_normal(hidden)).astype(F16),
+                        q=lin(heads * hd, hidden), k=lin(kv * hd, hidden), v=lin(kv * hd, hidden),
+                        o=lin(hidden, heads * hd), gate=lin(inter, hidden), up=lin(inter, hidden),
+                        down=lin(hidden, inter)) for _ in range(layers)]
+    embed = (rng.standard_normal((vocab, hidden)) * 0.02).astype(F16)
+    inv = (1.0 / (500000.0 ** (np.arange(0, hd, 2) / hd))).astype(F32)
+    return ol.LlamaWeights(shape=shape, embed=embed, layers=Ls,
+                           norm=(1 + 0.1 * rng.standard_normal(hidden)).astype(F16), lm_head=embed, inv_freq=inv)
+
+
+def _spec(w: ol.LlamaWeights, bits: int):
+    from liteweight_b200 import engine as E
+    s = w.shape
+    return E.LlamaSpec(hidden=s.hidden, inter=s.inter, n_layers=s.n_layers, n_heads=s.n_heads,
+                       n_kv_heads=s.n_kv_heads, head_dim=s.head_dim, vocab=s.vocab, bits=bits, group_size=128,
+                       eps=s.eps)
+
+
+def _layer_weights(w: ol.LlamaWeights, to):
+    from liteweight_b200 import engine as E
+    return [E.LayerWeights(in_norm=to(L.in_norm), post_norm=to(L.post_norm),
+                           **{n: (to(getattr(L, n).qweight), to(getattr(L, n).scales))
+                              for n in ("q", "k", "v", "o", "gate", "up", "down")}) for L in w.layers]
+
+
+def argmax_key(logits_f16: np.ndarray, offset: int) -> np.ndarray:
+    """Per row, the largest 64-bit key of a vocabulary shard: fp16 order key
+    (sign-flipped bits, so unsigned order = numeric order) in the high word,
+    0xFFFFFFFF - global index in the low word."""
+    b = logits_f16.view(np.uint16).astype(np.uint64)
+    order = np.where(b & 0x8000, (~b) & 0xFFFF, b | 0x8000)
+    idx = np.arange(logits_f16.shape[-1], dtype=np.uint64) + np.uint64(offset)
+    keys = (order << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - idx)
+    return keys.max(axis=-1).astype(np.int64)   # top bit clear: order < 2^16
+
+
+def _deq(w, s, bits):
+    return (oq.dequantize_int4 if bits == 4 else oq.dequantize_int8)(w, s, 128).astype(F32)
+
+
+def _tp_rank_decode(rank, world, w, bits, prompt, new_tokens):
+    """One rank of the tensor-parallel decode, in numpy, on the engine's shard buffers."""
+    from liteweight_b200 import engine as E
+    s = w.shape
+    hd, H = s.head_dim, s.hidden
+    nq, nkv, inter, vs = s.n_heads // world, s.n_kv_heads // world, s.inter // world, s.vocab // world
+    to = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    packs = [E.PackedLayer(lw, _spec(w, bits), rank, world, "cpu") for lw in _layer_weights(w, to)]
+    inv_q = torch.argsort(E.rope_pair_order(nq, hd, "cpu")).numpy()
+    inv_kv = torch.argsort(E.rope_pair_order(nkv, hd, "cpu")).numpy()
+    lin = []
+    for pk in packs:
+        qkv = _deq(pk.qkv_w.numpy(), pk.qkv_s.numpy(), bits)
+        q, k, v = np.split(qkv, [nq * hd, (nq + nkv) * hd])
+        gu = _deq(pk.gu_w.numpy(), pk.gu_s.numpy(), bits).reshape(inter // 8, 2, 8, H)
+        lin.append(dict(q=q[inv_q], k=k[inv_kv], v=v[inv_kv], gate=gu[:, 0].reshape(inter, H),
+                        up=gu[:, 1].reshape(inter, H), o=_deq(pk.o_w.numpy(), pk.o_s.numpy(), bits),
+                        down=_deq(pk.d_w.numpy(), pk.d_s.numpy(), bits)))
+    lm = w.lm_head[rank * vs:(rank + 1) * vs].astype(F32)
+    B, P = prompt.shape
+    S = P + new_tokens
+    kc = [np.zeros((B, nkv, S, hd), F16) for _ in packs]
+    vc = [np.zeros((B, nkv, S, hd), F16) for _ in packs]
+
+    def mm(x, wt):
+        return x.astype(F32) @ wt.T
+
+    def all_reduce_f32(a):
+        t = torch.from_numpy(np.ascontiguousarray(a, dtype=F32))
+        dist.all_reduce(t)
+        return t.numpy()
+
+    def resid(x, psum):   # x_new = fp16(x + fp16(psum))
+        return (x.astype(F32) + psum.astype(F16).astype(F32)).astype(F16)
+
+    tok = prompt[:, 0]
+    logits_out, gen = [], []
+    for pos in range(S - 1):
+        x = w.embed[tok].astype(F16)
+        cos, sin = ol.rope_tables(w.inv_freq, np.array([pos]), w.attention_scaling)
+        for li, (pk, L) in enumerate(zip(packs, lin)):
+            h = ol.rmsnorm(x, pk.in_norm.numpy(), s.eps)
+            q = ol.apply_rope(mm(h, L["q"]).astype(F16).reshape(B, nq, hd), cos[0], sin[0])
+            kc[li][:, :, pos] = ol.apply_rope(mm(h, L["k"]).astype(F16).reshape(B, nkv, hd), cos[0], sin[0])
+            vc[li][:, :, pos] = mm(h, L["v"]).astype(F16).reshape(B, nkv, hd)
+            a = ol.attention(q, kc[li], vc[li], pos + 1)
+            x = resid(x, all_reduce_f32(mm(a, L["o"])))
+            h = ol.rmsnorm(x, pk.post_norm.numpy(), s.eps)
+            act = (ol.silu_f16(mm(h, L["gate"]).astype(F16)).astype(F32) * mm(h, L["up"]).astype(F16)).astype(F16)
+            x = resid(x, all_reduce_f32(mm(act, L["down"])))
+        logits = mm(ol.rmsnorm(x, w.norm, s.eps), lm).astype(F16)
+        keys = torch.from_numpy(argmax_key(logits, rank * vs))
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX)
+        nxt = 0xFFFFFFFF - (keys.numpy() & 0xFFFFFFFF)
+        if pos >= P - 1:
+            full = [torch.empty(B, vs, dtype=torch.float16) for _ in range(world)]
+            dist.all_gather(full, torch.from_numpy(logits))
+            logits_out.append(torch.cat(full, 1).numpy())
+            gen.append(nxt)
+        tok = prompt[:, pos + 1] if pos + 1 < P else nxt
+    return np.stack(logits_out), np.stack(gen, 1)
+
+
+def _gloo_worker(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        w = random_model(256, 512, 2, 4, 2, 64, 384, 4, seed=11)
+        prompt = np.random.default_rng(2).integers(0, 384, (2, 4))
+        logits, gen = _tp_rank_decode(rank, world, w, 4, prompt, 4)
+        if rank == 0:
+            np.savez(out_path, logits=logits, gen=gen, prompt=prompt)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_argmax_key_order():
+    v = np.array([[-1.0, 0.0, -0.0, 2.0, 2.0, -3.0]], F16)
+    k = argmax_key(v, 100)
+    assert 0xFFFFFFFF - (int(k[0]) & 0xFFFFFFFF) == 103          # first of the tied maxima
+    lo = argmax_key(np.array([[-5.0, -4.0]], F16), 0)
+    hi = argmax_key(np.array([[-4.5]], F16), 7)
+    assert lo[0] > hi[0]                                            # -4 beats -4.5 across shards
+
+
+def test_gloo_tp2_decode_matches_unsharded_oracle():
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        out = os.path.join(d, "tp.npz")
+        mp.start_processes(_gloo_worker, args=(2, port, out), nprocs=2, start_method="spawn", join=True)
+        r = dict(np.load(out))
+    w = random_model(256, 512, 2, 4, 2, 64, 384, 4, seed=11)
+    ref = ol.teacher_forced_logits(w, r["prompt"], r["gen"])
+    got = r["logits"].reshape(-1, 384).astype(np.float64)
+    o = ref.reshape(-1, 384).astype(np.float64)
+    assert np.all(np.abs(got - o) <= oq.row_tolerance(o))
+    assert np.array_equal(r["gen"].T, np.stack([ol.greedy(x) for x in r["logits"]]))
+
+
+# ---------------------------------------------------------------- GPU, NCCL
+
+_GPU_MODEL = dict(hidden=512, inter=1024, layers=2, heads=8, kv=4, hd=64, vocab=1024, bits=4, seed=4)
+
+
+def _nccl_worker(rank, world, port, out_path, exchange):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    from liteweight_b200 import engine as E
+    w = random_model(**_GPU_MODEL)
+    to = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    t1 = torch.zeros(1, device=dev)
+    dist.all_reduce(t1)          # communicator up before graph capture
+    eng = E.build_engine(_spec(w, 4), _layer_weights(w, to), to(w.embed), to(w.norm), None,
+                         torch.from_numpy(w.inv_freq), 2, 64, dev, tp_rank=rank, tp_size=world,
+                         tp_group=dist.group.WORLD, exchange=exchange)
+    P, T = 6, 5
+    prompt = np.random.default_rng(3).integers(0, w.shape.vocab, (2, P))
+    shards = []
+    for rep in range(2):         # a second generation reuses the graph and the exchange counters
+        eng.start(torch.from_numpy(prompt))
+        eng.capture()
+        shards = []
+        for p in range(P + T - 1):
+            eng.step(1)
+            if p >= P - 1:
+                full = [torch.empty_like(eng.logits) for _ in range(world)]
+                dist.all_gather(full, eng.logits)
+                shards.append(torch.cat(full, dim=1).float().cpu().numpy())
+    torch.cuda.synchronize()
+    eng.check()
+    gen_t = eng.generated(T).to(torch.int64).contiguous()
+    gen = gen_t.cpu().numpy()
+    gens = [torch.empty_like(gen_t) for _ in range(world)]
+    dist.all_gather(gens, gen_t)
+    if rank == 0:
+        np.savez(out_path, logits=np.stack(shards), tokens=gen, prompt=prompt,
+                 same=all(bool(torch.equal(g, gens[0])) for g in gens))
+    eng.close()                  # collective; releases the graph (NCCL calls in the "nccl" mode)
+    del eng
+    gc.collect()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run_tp2(exchange):
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        out = os.path.join(d, "tp2.npz")
+        mp.start_processes(_nccl_worker, args=(2, port, out, exchange), nprocs=2, start_method="spawn", join=True)
+        return dict(np.load(out))
+
+
+@pytest.mark.gpu
+def test_tp2_decode_matches_oracle():
+    """TP=2 decode with the in-kernel peer exchange: the same bits as the NCCL
+    all-reduce path (a sum of two partials does not depend on its order), and
+    within the row tolerance of the unsharded oracle."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    peer, nccl = _run_tp2("peer"), _run_tp2("nccl")
+    for r in (peer, nccl):
+        assert bool(r["same"]), "ranks picked different tokens"
+    assert np.array_equal(peer["logits"], nccl["logits"])
+    assert np.array_equal(peer["tokens"], nccl["tokens"])
+    w = random_model(**_GPU_MODEL)
+    ref = ol.teacher_forced_logits(w, peer["prompt"], peer["tokens"])
+    g = peer["logits"].reshape(-1, ref.shape[-1]).astype(np.float64)
+    o = ref.reshape(-1, ref.shape[-1]).astype(np.float64)
+    tol = oq.row_tolerance(o)
+    assert np.all(np.abs(g - o) <= tol), float((np.abs(g - o) / tol).max())
