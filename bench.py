@@ -8,7 +8,9 @@ Prints ONE JSON line (rank 0). Workloads:
 * ``decode`` (default) - greedy decode of a random-init Llama-3-8B
   architecture, INT4 group-128 weight-only (the reference's format), batch 1,
   512 uniform-random prompt ids, fp16 KV cache, tensor parallel over the N
-  ranks (one process per GPU, NCCL all-reduce). One step = one decode token
+  ranks (one process per GPU; the all-reduces run inside the GEMV kernels
+  over NVLink peer memory, or as NCCL all-reduces with ``--exchange nccl``).
+  One step = one decode token
   for the batch (graph replay of the fused decode step). Metric: decode
   tokens/s of the whole job (``scaling: strong``: the model and batch are
   fixed as N grows). ``--model 1b`` (INT8, prompt 128) and ``--model 70b``
@@ -331,13 +333,17 @@ class DecodeWorkload:
     unit = "tokens/s"
 
     def __init__(self, device, dist: "Dist", model: str, batch: int, extra_steps: int, fold: bool = False,
-                 exchange: str = "peer"):
+                 exchange: str = "peer", prompt: int | None = None, new: int | None = None,
+                 layers: int | None = None):
         import torch
         from liteweight_b200 import engine as E
         cfg = MODELS[model]
         self.torch, self.E, self.dev, self.cfg = torch, E, device, cfg
-        self.spec = E.LlamaSpec(**getattr(E, cfg["arch"]), bits=cfg["bits"], group_size=GROUP)
-        self.B, self.P, self.T = batch, cfg["prompt"], cfg["new"]
+        arch = dict(getattr(E, cfg["arch"]))
+        if layers:
+            arch["n_layers"] = layers
+        self.spec = E.LlamaSpec(**arch, bits=cfg["bits"], group_size=GROUP)
+        self.B, self.P, self.T = batch, prompt or cfg["prompt"], new or cfg["new"]
         self.tp, self.rank = dist.world, dist.rank
         self.metric = (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only, batch {batch}, "
                        f"prompt {self.P}, greedy, TP{self.tp})")
@@ -659,7 +665,7 @@ def run_decode(args, dist: Dist):
     lwbuild.build()
     nat.lib()
     wl = DecodeWorkload(dev, dist, args.model, args.batch, args.warmup + args.steps, fold=args.fold,
-                        exchange=args.exchange)
+                        exchange=args.exchange, prompt=args.prompt, new=args.new, layers=args.layers)
     if dist.world > 1:   # NCCL communicator up before graph capture
         t = torch.zeros(1, device=dev)
         dist.pg.all_reduce(t)
@@ -694,7 +700,7 @@ def run_decode(args, dist: Dist):
     roofline = {"bound": "hbm", "kernel": f"fused GEMV {dom}" if dom != "attn" else "attention",
                 "achieved": achieved, "peak": peak.peak_mem_bandwidth_gbs, "peak_source": peak_src, "unit": "GB/s",
                 "frac": round(achieved / peak.peak_mem_bandwidth_gbs, 4), "algorithmic_bytes_per_launch": d["bytes"],
-                "avg_launch_us": d["us"], "traffic": traffic_for(f"decode_{args.model}_{dom}")}
+                "avg_launch_us": d["us"], "traffic": traffic_for(f"decode_{args.model}_tp{dist.world}_{dom}")}
     bstep = wl.bytes_per_step(ctx_mid)
     decode_roofline = {"bytes_per_step_per_gpu": bstep, "achieved_GBs_per_gpu": round(bstep / (step_ms * 1e-3) / 1e9, 1),
                        "frac": round(bstep / (step_ms * 1e-3) / 1e9 / peak.peak_mem_bandwidth_gbs, 4),
@@ -781,6 +787,10 @@ def main():
                     help="decode GEMVs scale each chunk sum in fp32 instead of dequantizing exactly")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="tensor-parallel all-reduce: in-kernel through peer memory, or NCCL between kernels")
+    ap.add_argument("--prompt", type=int, default=None, help="prompt length (profiling runs; default: the config's)")
+    ap.add_argument("--new", type=int, default=None, help="new tokens of the e2e call (profiling runs)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers (small profiling cases only: the line is then not the config's number)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 200 if args.impl == "ours" else 21

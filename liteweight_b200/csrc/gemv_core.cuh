@@ -479,13 +479,10 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
               // each word read once it carries this step's flag
 #pragma unroll
               for (int e = 0; e < 8; ++e) ps[e] = 0.f;
-              for (int r = 0; r < p.in_world; ++r) {
-                float pr[8];
-                read_flagged8(p.in_src + ((size_t)r * p.M + m) * p.K + k, in_flag, pr, wb, p.in_timeout_ns,
-                              p.in_error);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) ps[e] += pr[e];
-              }
+              const size_t rstride = (size_t)p.M * p.K;
+              for (int r = 0; r < p.in_world; r += 2)
+                add_flagged8<2>(p.in_src + r * rstride + (size_t)m * p.K + k, rstride, min(2, p.in_world - r),
+                                in_flag, ps, wb, p.in_timeout_ns, p.in_error);
             }
             __half* hv = reinterpret_cast<__half*>(&v);
 #pragma unroll

@@ -117,20 +117,34 @@ struct WaitBudget {
   }
 };
 
-// 8 consecutive flagged fp32 words whose flags all equal `flag` (bounded).
-LW_DEV void read_flagged8(const unsigned long long* src, uint32_t flag, float (&v)[8], WaitBudget& wb,
-                          long long timeout_ns, int* error) {
-  unsigned long long w[8];
-  for (;;) {
+// Adds, in rank order, the 8 consecutive flagged fp32 words of ranks
+// r0 .. r0 + nr - 1 (nr <= RB; rank j's words at src + j * rank_stride) to
+// acc, each read once its flag equals `flag` (bounded). The loads of all nr
+// ranks are issued before the first flag is checked.
+template <int RB>
+LW_DEV void add_flagged8(const unsigned long long* src, size_t rank_stride, int nr, uint32_t flag,
+                         float (&acc)[8], WaitBudget& wb, long long timeout_ns, int* error) {
+  unsigned long long w[RB][8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ld_volatile_v2u64(src + 2 * i, w[2 * i], w[2 * i + 1]);
-    bool ok = true;
+  for (int j = 0; j < RB; ++j)
+    if (j < nr) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ok &= (uint32_t)(w[i] >> 32) == flag;
-    if (ok || !wb.keep_waiting(timeout_ns, error)) break;
+      for (int i = 0; i < 4; ++i) ld_volatile_v2u64(src + j * rank_stride + 2 * i, w[j][2 * i], w[j][2 * i + 1]);
+    }
+#pragma unroll
+  for (int j = 0; j < RB; ++j) {
+    if (j >= nr) break;
+    for (;;) {
+      bool ok = true;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ok &= (uint32_t)(w[j][i] >> 32) == flag;
+      if (ok || !wb.keep_waiting(timeout_ns, error)) break;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ld_volatile_v2u64(src + j * rank_stride + 2 * i, w[j][2 * i], w[j][2 * i + 1]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += __uint_as_float((uint32_t)w[j][i]);
   }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float((uint32_t)w[i]);
 }
 
 // ---------------------------------------------------------------- tensor core
