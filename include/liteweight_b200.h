@@ -53,6 +53,12 @@ int lw_abi_version(void);
  * (telemetry; no counterpart in the reference). */
 unsigned long long lw_launch_count(void);
 
+/* Reads and clears the library's device-side error flags on the current
+ * device: LW_ERR_TIMEOUT if a bounded wait inside one of its kernels gave up
+ * since the last call (that launch's results are invalid), else LW_OK.
+ * Synchronises the device. No counterpart in the reference. */
+int lw_take_device_error(void);
+
 /* ---- dequant matmul: out[M,N] = act[M,K] @ dequant(W)[N,K]^T (+ bias) ----
  * fp32 accumulation of fp16 activations times fp16 dequantized weights, one
  * fp16 rounding at the end, then `+ bias` in fp16 when bias != NULL. This is

@@ -25,6 +25,7 @@ _SIGNATURES: dict[str, list] = {
     "lw_status_string": [c_int],
     "lw_abi_version": [],
     "lw_launch_count": [],
+    "lw_take_device_error": [],
     "lw_gemm_workspace_size": [c_int] * 4,
     "lw_gemm_w8a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p, ctypes.c_size_t, c_void_p],
     "lw_gemm_w4a16": [c_void_p] * 5 + [c_int] * 4 + [c_void_p, ctypes.c_size_t, c_void_p],

@@ -403,6 +403,8 @@ cudaError_t attn_launch(const lw::AttnParams& p, cudaStream_t s, bool pdl) {
 
 }  // namespace
 
+int lw_decode_take_error() { return lw_tu_take_error(); }
+
 extern "C" {
 
 int lw_fused_gemv(const lw_fused_gemv_args* a, lw_stream_t stream) {

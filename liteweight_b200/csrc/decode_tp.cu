@@ -53,3 +53,5 @@ bool tp_fused_ws(const lw_fused_gemv_args* a, size_t* bytes) {
 }
 
 }  // namespace lw
+
+int lw_decode_tp_take_error() { return lw_tu_take_error(); }

@@ -320,6 +320,10 @@ cudaError_t launch_kn(GemvParams p, cudaStream_t s) {
 
 }  // namespace
 
+// Device error flags of the other translation units that launch kernels.
+int lw_decode_take_error();
+int lw_decode_tp_take_error();
+
 extern "C" {
 
 const char* lw_status_string(int status) {
@@ -338,6 +342,13 @@ const char* lw_status_string(int status) {
 }
 
 int lw_abi_version(void) { return 110; }
+
+int lw_take_device_error(void) {
+  const int mine = lw_tu_take_error();
+  const int dec = lw_decode_take_error();
+  const int tp = lw_decode_tp_take_error();
+  return mine ? mine : (dec ? dec : tp);
+}
 
 unsigned long long lw_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 

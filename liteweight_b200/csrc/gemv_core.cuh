@@ -108,6 +108,7 @@ struct StreamParams {
   float* slots;            // [tiles][max_slots][32 lanes][4 * MT]
   int* counters;           // [tiles], zero before the first launch, left zero
   int max_slots;
+  int ring_slots;          // gemv_tma_kernel: shared-memory slots per warp
   // tensor-parallel exchange, consumer (PRO_PEER_RESID_NORM): flagged words
   int in_world, in_tag, in_tags;
   const unsigned long long* in_src;    // local [in_world][M][K]
@@ -348,6 +349,139 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
   }
 }
 
+// Stages the activation (M rows, K padded to whole chunks) into act_s in the
+// element order the unpack produces (lane order), applying the prologue:
+// RMSNorm (modeling_llama.py:65-68 rounding points), optionally after adding
+// the all-reduced partial sum to the residual (CTA 0 writes the new residual).
+// Called by all NT threads of the CTA; ends with a CTA barrier.
+template <int BITS, int PRO, int NT>
+LW_DEV void stage_activation(const StreamParams& p, __half* act_s, float* ssq, uint32_t in_flag, WaitBudget& wb) {
+  constexpr int E = WT<BITS>::E;
+  constexpr int KC = 4 * E;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int C = p.kchunks;
+  const int groups8 = C * KC / 8;
+  if constexpr (PRO != PRO_PLAIN) {
+    if (tid < kMaxM) ssq[tid] = 0.f;
+    __syncthreads();
+  }
+  for (int m = 0; m < p.M; ++m) {
+    float sq = 0.f;
+    for (int i = tid; i < groups8; i += NT) {
+      const int k = i * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (k < p.K) {
+        v = ldg_nc(p.act + (size_t)m * p.lda + k);
+        if constexpr (kResidPro<PRO>) {
+          // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
+          float ps[8];
+          if constexpr (PRO == PRO_RESID_NORM) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
+            ps[0] = a.x; ps[1] = a.y; ps[2] = a.z; ps[3] = a.w;
+            ps[4] = b.x; ps[5] = b.y; ps[6] = b.z; ps[7] = b.w;
+          } else {
+            // the all-reduce itself: the world partials, summed in rank order,
+            // each word read once it carries this step's flag
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+            const size_t rstride = (size_t)p.M * p.K;
+            for (int r = 0; r < p.in_world; r += 2)
+              add_flagged8<2>(p.in_src + r * rstride + (size_t)m * p.K + k, rstride, min(2, p.in_world - r),
+                              in_flag, ps, wb, p.in_timeout_ns, p.in_error);
+          }
+          __half* hv = reinterpret_cast<__half*>(&v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
+          if (blockIdx.x == 0) *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v;
+        }
+        if constexpr (PRO != PRO_PLAIN) {
+          const __half* hv = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float f = __half2float(hv[e]);
+            sq = fmaf(f, f, sq);
+          }
+        }
+      }
+      if constexpr (BITS == 4) v = perm_int4_pairs(v);
+      const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
+      sts128(act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8, v);
+    }
+    if constexpr (PRO != PRO_PLAIN) {
+      sq = warp_sum(sq);
+      if (lane == 0) atomicAdd(&ssq[m], sq);
+    }
+  }
+  if constexpr (PRO != PRO_PLAIN) {
+    __syncthreads();
+    // modeling_llama.py:65-68: h = weight * fp16(x * rsqrt(mean(x^2) + eps))
+    for (int m = 0; m < p.M; ++m) {
+      const float rstd = 1.0f / sqrtf(ssq[m] / (float)p.K + p.eps);
+      for (int i = tid; i < groups8; i += NT) {
+        const int k = i * 8;
+        if (k >= p.K) continue;
+        const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
+        __half* dst = act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8;
+        uint4 v = lds128(dst);
+        uint4 gm = ldg_nc(p.gamma + k);
+        if constexpr (BITS == 4) gm = perm_int4_pairs(gm);
+        __half* hv = reinterpret_cast<__half*>(&v);
+        const __half* hg = reinterpret_cast<const __half*>(&gm);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          hv[e] = __float2half_rn(__half2float(hg[e]) * r16(__half2float(hv[e]) * rstd));
+        sts128(dst, v);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// A warp's tile segment [seg_c0, end_c) is done: a whole tile runs the
+// epilogue directly; a split tile writes its fp32 fragment to its slot, and
+// the last contributor sums the slots in slot order and runs the epilogue.
+template <int MT, int EPI>
+LW_DEV void flush_tile(const StreamParams& p, int tile, int seg_c0, int end_c, int wid, const float (&acc)[MT][4],
+                       int lane, uint32_t out_flag) {
+  const int C = p.kchunks;
+  const bool whole = (seg_c0 == 0) && (end_c == C);
+  if (whole) {
+    finish_tile<MT, EPI>(p, tile, acc, lane, out_flag);
+    return;
+  }
+  const int first = (tile * C) / p.per;
+  const int last = ((tile + 1) * C - 1) / p.per;
+  const int slot = wid - first, nslot = last - first + 1;
+  float* base = p.slots + (size_t)tile * p.max_slots * 32 * 4 * MT;
+  float4* mine = reinterpret_cast<float4*>(base + ((size_t)slot * 32 + lane) * 4 * MT);
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) mine[mt] = make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
+  __threadfence();
+  int old = 0;
+  if (lane == 0) old = atomicAdd(p.counters + tile, 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old == nslot - 1) {
+    __threadfence();
+    float sum[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) sum[mt][0] = sum[mt][1] = sum[mt][2] = sum[mt][3] = 0.f;
+    for (int s = 0; s < nslot; ++s) {
+      const float4* src = reinterpret_cast<const float4*>(base + ((size_t)s * 32 + lane) * 4 * MT);
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const float4 f = __ldcg(src + mt);
+        sum[mt][0] += f.x;
+        sum[mt][1] += f.y;
+        sum[mt][2] += f.z;
+        sum[mt][3] += f.w;
+      }
+    }
+    finish_tile<MT, EPI>(p, tile, sum, lane, out_flag);
+    if (lane == 0) p.counters[tile] = 0;
+  }
+}
+
 // A cursor over a warp's run of flattened (tile, chunk) work.
 struct RunCursor {
   int t, c, left;
@@ -386,26 +520,48 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   const int npieces = (int)(rowbytes / 16);
   const int ngroups = SCALED ? p.K / p.G : 1;
 
+  // ---- the warp's run [g0, g1) of flattened (tile, chunk) work, cut into
+  // tile segments. A segment sets its row and scale pointers once and steps
+  // through batches of U chunks; loads run two batches ahead of the tensor
+  // cores (register double buffer) and L2 prefetches kPrefetch batches ahead
+  // of the loads. Rows past N are clamped to N-1 (computed, never stored);
+  // when a row does not end on a whole chunk, pieces past it are clamped to
+  // its last piece and meet zero activations.
+  const bool full = (rowbytes & 63) == 0;
+  const unsigned short* sbase = reinterpret_cast<const unsigned short*>(p.scales);
+  const int toff = FOLD ? 0 : t * E;
+
+  int s_tile = g0 / max(C, 1);
+  int s_c0 = g0 - s_tile * C;
+  int s_len = min(C - s_c0, g1 - g0);
+  const uint8_t *w0 = nullptr, *w1 = nullptr;
+  const unsigned short *sc0 = nullptr, *sc1 = nullptr;
+  auto seg_setup = [&]() {
+    const int r0 = min(s_tile * 16 + g, p.N - 1), r1 = min(s_tile * 16 + g + 8, p.N - 1);
+    w0 = p.w + (size_t)r0 * rowbytes;
+    w1 = p.w + (size_t)r1 * rowbytes;
+    if constexpr (SCALED) {
+      sc0 = sbase + (size_t)r0 * ngroups;
+      sc1 = sbase + (size_t)r1 * ngroups;
+    }
+  };
+
   uint4 qa0[U], qb0[U], qa1[U], qb1[U];
   uint32_t sa0[U], sb0[U], sa1[U], sb1[U];
-
-  // Rows past N are clamped to N-1 (computed, never stored); pieces past K are
-  // clamped to the last piece (they meet zero activations). No selects.
-  auto load = [&](int bt, int bc, int bn, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
-    const int r0 = min(bt * 16 + g, p.N - 1), r1 = min(bt * 16 + g + 8, p.N - 1);
-    const uint8_t* w0 = p.w + (size_t)r0 * rowbytes;
-    const uint8_t* w1 = p.w + (size_t)r1 * rowbytes;
-    const unsigned short* s0 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r0 * ngroups;
-    const unsigned short* s1 = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)r1 * ngroups;
+  // batch b of the current segment: chunks s_c0 + b*U + u for b*U + u < s_len
+  auto load = [&](int b, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (u < bn) {
-        const int pc = min((bc + u) * 4 + t, npieces - 1);
+      if (b * U + u < s_len) {
+        const int c = s_c0 + b * U + u;
+        int pc = c * 4 + t;
+        if (!full) pc = min(pc, npieces - 1);
         qa[u] = ldg_stream(w0 + (size_t)pc * 16);
         qb[u] = ldg_stream(w1 + (size_t)pc * 16);
         if constexpr (SCALED) {
-          const int grp = min(((bc + u) * KC + (FOLD ? 0 : t * E)) >> p.gshift, ngroups - 1);
-          const uint32_t h0 = __ldg(s0 + grp), h1 = __ldg(s1 + grp);
+          int grp = (c * KC + toff) >> p.gshift;
+          if (!full) grp = min(grp, ngroups - 1);
+          const uint32_t h0 = __ldg(sc0 + grp), h1 = __ldg(sc1 + grp);
           if constexpr (FOLD) {
             sa[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h0)));
             sb[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h1)));
@@ -418,29 +574,40 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
     }
   };
 
-  // Run cursors: loads, and an L2 prefetch kPrefetch batches ahead of them.
-  RunCursor ld{g0 / max(C, 1), g0 - (g0 / max(C, 1)) * C, g1 - g0};
-  RunCursor pf = ld;
-  // Each of the 32 lanes prefetches one 64-byte piece-pair line: rows g and
-  // g+8 of the batch, chunk t (lanes hold 16 rows x 2 chunks of U = 2).
-  auto prefetch_next = [&]() {
-    const int pt = pf.t, pc = pf.c;
-    const int n = pf.take(U, C);
-    if (n) {
-      const int row = min(pt * 16 + (lane & 15), p.N - 1);
-      const int ch = min(pc + (lane >> 4), pc + n - 1);
-      const size_t off = min((size_t)ch * 64, rowbytes - 16);
-      prefetch_l2_line(p.w + (size_t)row * rowbytes + off);
+  // L2 prefetch cursor over the whole run: each lane takes one 64-byte line of
+  // a batch (row lane % 16, chunk + lane / 16), crossing into the next tile.
+  int pf_t = s_tile, pf_c = s_c0, pf_left = g1 - g0;
+  auto pf_skip = [&]() {
+    pf_left -= U;
+    pf_c += U;
+    if (pf_c >= C) {
+      pf_c -= C;
+      ++pf_t;
     }
+  };
+  auto prefetch_next = [&]() {
+    if (pf_left <= 0) return;
+    int ch = pf_c + (lane >> 4), tl = pf_t;
+    if (ch >= C) {
+      ch -= C;
+      ++tl;
+    }
+    if ((lane >> 4) < pf_left) {
+      const int row = min(tl * 16 + (lane & 15), p.N - 1);
+      prefetch_l2_line(p.w + (size_t)row * rowbytes + min((size_t)ch * 64, rowbytes - 16));
+    }
+    pf_skip();
   };
 
   // Weights do not depend on the previous kernel: start streaming them first.
-  int tA = ld.t, cA = ld.c, nA = ld.take(U, C);
-  if (nA) load(tA, cA, nA, qa0, qb0, sa0, sb0);
-  int tB = ld.t, cB = ld.c, nB = ld.take(U, C);
-  if (nB) load(tB, cB, nB, qa1, qb1, sa1, sb1);
-  pf.take(U, C);
-  pf.take(U, C);
+  int nb = (s_len + U - 1) / U;
+  if (s_len > 0) {
+    seg_setup();
+    load(0, qa0, qb0, sa0, sb0);
+    if (nb > 1) load(1, qa1, qb1, sa1, sb1);
+  }
+  pf_skip();   // the two batches loaded directly
+  pf_skip();
 #pragma unroll 1
   for (int i = 0; i < kPrefetch; ++i) prefetch_next();
 
@@ -452,141 +619,21 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   if constexpr (kPeerEpi<EPI>) out_flag = exchange_flag(*p.out_step, p.out_tag, p.out_tags);
   WaitBudget wb;
 
-  // ---- stage the activation (M rows, K padded to the chunk) in lane order
-  {
-    const int groups8 = C * KC / 8;
-    if constexpr (PRO != PRO_PLAIN) {
-      if (tid < kMaxM) ssq[tid] = 0.f;
-      __syncthreads();
-    }
-    for (int m = 0; m < p.M; ++m) {
-      float sq = 0.f;
-      for (int i = tid; i < groups8; i += kStreamThreads) {
-        const int k = i * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (k < p.K) {
-          v = ldg_nc(p.act + (size_t)m * p.lda + k);
-          if constexpr (kResidPro<PRO>) {
-            // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
-            float ps[8];
-            if constexpr (PRO == PRO_RESID_NORM) {
-              const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
-              const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
-              ps[0] = a.x; ps[1] = a.y; ps[2] = a.z; ps[3] = a.w;
-              ps[4] = b.x; ps[5] = b.y; ps[6] = b.z; ps[7] = b.w;
-            } else {
-              // the all-reduce itself: the world partials, summed in rank order,
-              // each word read once it carries this step's flag
-#pragma unroll
-              for (int e = 0; e < 8; ++e) ps[e] = 0.f;
-              const size_t rstride = (size_t)p.M * p.K;
-              for (int r = 0; r < p.in_world; r += 2)
-                add_flagged8<2>(p.in_src + r * rstride + (size_t)m * p.K + k, rstride, min(2, p.in_world - r),
-                                in_flag, ps, wb, p.in_timeout_ns, p.in_error);
-            }
-            __half* hv = reinterpret_cast<__half*>(&v);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
-            if (blockIdx.x == 0) *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v;
-          }
-          if constexpr (PRO != PRO_PLAIN) {
-            const __half* hv = reinterpret_cast<const __half*>(&v);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float f = __half2float(hv[e]);
-              sq = fmaf(f, f, sq);
-            }
-          }
-        }
-        if constexpr (BITS == 4) v = perm_int4_pairs(v);
-        const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
-        sts128(act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8, v);
-      }
-      if constexpr (PRO != PRO_PLAIN) {
-        sq = warp_sum(sq);
-        if (lane == 0) atomicAdd(&ssq[m], sq);
-      }
-    }
-    if constexpr (PRO != PRO_PLAIN) {
-      __syncthreads();
-      // modeling_llama.py:65-68: h = weight * fp16(x * rsqrt(mean(x^2) + eps))
-      for (int m = 0; m < p.M; ++m) {
-        const float rstd = 1.0f / sqrtf(ssq[m] / (float)p.K + p.eps);
-        for (int i = tid; i < groups8; i += kStreamThreads) {
-          const int k = i * 8;
-          if (k >= p.K) continue;
-          const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
-          __half* dst = act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8;
-          uint4 v = lds128(dst);
-          uint4 gm = ldg_nc(p.gamma + k);
-          if constexpr (BITS == 4) gm = perm_int4_pairs(gm);
-          __half* hv = reinterpret_cast<__half*>(&v);
-          const __half* hg = reinterpret_cast<const __half*>(&gm);
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            hv[e] = __float2half_rn(__half2float(hg[e]) * r16(__half2float(hv[e]) * rstd));
-          sts128(dst, v);
-        }
-      }
-    }
-  }
-  __syncthreads();
+  stage_activation<BITS, PRO, kStreamThreads>(p, act_s, ssq, in_flag, wb);
 
-  // ---- stream the warp's run of (tile, chunk) work
   float acc[MT][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-  int seg_c0 = g0 - (g0 / max(C, 1)) * C;   // first chunk of the current tile segment
   const __half* arow[MT];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) arow[mt] = act_s + (size_t)min(g + 8 * mt, p.M - 1) * p.cp + t * 8;
 
-  auto flush = [&](int tile, int end_c) {
-    const bool whole = (seg_c0 == 0) && (end_c == C);
-    if (whole) {
-      finish_tile<MT, EPI>(p, tile, acc, lane, out_flag);
-    } else {
-      const int first = (tile * C) / p.per;
-      const int last = ((tile + 1) * C - 1) / p.per;
-      const int slot = wid - first, nslot = last - first + 1;
-      float* base = p.slots + (size_t)tile * p.max_slots * 32 * 4 * MT;
-      float4* mine = reinterpret_cast<float4*>(base + ((size_t)slot * 32 + lane) * 4 * MT);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) mine[mt] = make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
-      __threadfence();
-      int old = 0;
-      if (lane == 0) old = atomicAdd(p.counters + tile, 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == nslot - 1) {
-        __threadfence();
-        float sum[MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) sum[mt][0] = sum[mt][1] = sum[mt][2] = sum[mt][3] = 0.f;
-        for (int s = 0; s < nslot; ++s) {
-          const float4* src = reinterpret_cast<const float4*>(base + ((size_t)s * 32 + lane) * 4 * MT);
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            const float4 f = __ldcg(src + mt);
-            sum[mt][0] += f.x;
-            sum[mt][1] += f.y;
-            sum[mt][2] += f.z;
-            sum[mt][3] += f.w;
-          }
-        }
-        finish_tile<MT, EPI>(p, tile, sum, lane, out_flag);
-        if (lane == 0) p.counters[tile] = 0;
-      }
-    }
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-    seg_c0 = 0;
-  };
-
-  auto compute = [&](int bt, int bc, int bn, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
+  auto compute = [&](int b, const uint4(&qa)[U], const uint4(&qb)[U], const uint32_t(&sa)[U],
+                     const uint32_t(&sb)[U]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (u < bn) {
-        const int off = (bc + u) * KC;
+      if (b * U + u < s_len) {
+        const int off = (s_c0 + b * U + u) * KC;
         if constexpr (SCALED && FOLD) {
           float dc[MT][4];
 #pragma unroll
@@ -605,28 +652,42 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
         }
       }
     }
-    const int end_c = bc + bn;
-    if (end_c == C || bt * C + end_c == g1) flush(bt, end_c);
   };
 
-  while (nA) {
-    compute(tA, cA, nA, qa0, qb0, sa0, sb0);
-    tA = ld.t;
-    cA = ld.c;
-    nA = ld.take(U, C);
-    if (nA) {
-      load(tA, cA, nA, qa0, qb0, sa0, sb0);
+  int done = 0;   // chunks of the run finished in earlier segments
+  while (s_len > 0) {
+    for (int b = 0;; b += 2) {
+      compute(b, qa0, qb0, sa0, sb0);
+      if (b + 2 < nb) {
+        load(b + 2, qa0, qb0, sa0, sb0);
+        prefetch_next();
+      }
+      if (b + 1 >= nb) break;
+      compute(b + 1, qa1, qb1, sa1, sb1);
+      if (b + 3 < nb) {
+        load(b + 3, qa1, qb1, sa1, sb1);
+        prefetch_next();
+      }
+      if (b + 2 >= nb) break;
+    }
+    // the next segment (the next tile from its chunk 0) starts loading before
+    // this one's partial sums are written out
+    const int f_tile = s_tile, f_c0 = s_c0, f_end = s_c0 + s_len;
+    done += s_len;
+    ++s_tile;
+    s_c0 = 0;
+    s_len = min(C, (g1 - g0) - done);
+    nb = (s_len + U - 1) / U;
+    if (s_len > 0) {
+      seg_setup();
+      load(0, qa0, qb0, sa0, sb0);
+      if (nb > 1) load(1, qa1, qb1, sa1, sb1);
+      prefetch_next();
       prefetch_next();
     }
-    if (!nB) break;
-    compute(tB, cB, nB, qa1, qb1, sa1, sb1);
-    tB = ld.t;
-    cB = ld.c;
-    nB = ld.take(U, C);
-    if (nB) {
-      load(tB, cB, nB, qa1, qb1, sa1, sb1);
-      prefetch_next();
-    }
+    flush_tile<MT, EPI>(p, f_tile, f_c0, f_end, wid, acc, lane, out_flag);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
   }
   if constexpr (EPI == EPI_PEER_ARGMAX) {
     // The last CTA to finish (every CTA's atomicMax is then in the local keys)

@@ -1,9 +1,13 @@
 // Host-side planning and launch of the persistent stream-K GEMV kernel.
 #pragma once
 
+#include <stdlib.h>
+#include <string.h>
+
 #include <algorithm>
 
 #include "gemv_core.cuh"
+#include "gemv_tma.cuh"
 
 namespace lw {
 
@@ -27,7 +31,53 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct StreamPlan {
   int tiles, kchunks, cp, per, grid, max_slots, mt;
   size_t smem, ws_bytes;  // ws_bytes = 0 when no tile is split
+  int ring_slots;         // > 0: the bulk-copy kernel (gemv_tma_kernel) with this many slots per warp
 };
+
+// The bulk-copy GEMV (gemv_tma.cuh) serves M <= 8 with INT4 / INT8 weights
+// when the environment sets LW_B200_GEMV=bulk; by default every launch uses
+// the register-pipeline kernel, which measures faster on B200 (the per-lane
+// bulk copies are issued one lane at a time through uniform registers).
+inline bool tma_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LW_B200_GEMV");
+    return v && strcmp(v, "bulk") == 0;
+  }();
+  return on;
+}
+
+constexpr size_t kTmaSmemBudget = 232448 - 512;   // opt-in dynamic shared memory per CTA, less static
+
+// Plan of the bulk-copy kernel; false when its ring (>= 3 slots per warp) and
+// the staged activation do not fit in shared memory.
+template <int BITS>
+bool plan_tma(int M, int N, int K, bool allow_split, StreamPlan* pl) {
+  constexpr int KC = 4 * WT<BITS>::E;
+  if (BITS == 16 || M > 8) return false;
+  pl->mt = 1;
+  pl->tiles = (N + 15) / 16;
+  pl->kchunks = (K + KC - 1) / KC;
+  const int kpad = pl->kchunks * KC;
+  pl->cp = ((size_t)M * (kpad + 32) * 2 <= (size_t)kStageBudget) ? kpad + 32 : kpad;
+  const size_t act = align_up((size_t)M * pl->cp * 2, 128);
+  if (act + kTmaBarBytes >= kTmaSmemBudget) return false;
+  const int slots = (int)std::min<size_t>(kTmaMaxSlots, (kTmaSmemBudget - kTmaBarBytes - act) /
+                                                            ((size_t)kTmaWarps * kTmaSlotBytes));
+  if (slots < 3) return false;
+  pl->ring_slots = slots;
+  pl->smem = kTmaBarBytes + (size_t)kTmaWarps * slots * kTmaSlotBytes + act;
+  const long long warps_max = (long long)device_sm_count() * kTmaWarps;
+  const long long total = (long long)pl->tiles * pl->kchunks;
+  long long per = std::max<long long>(kTmaU, (total + warps_max - 1) / warps_max);
+  if (!allow_split || pl->tiles > kMaxSplitTiles) per = (per + pl->kchunks - 1) / pl->kchunks * pl->kchunks;
+  pl->per = (int)per;
+  const long long warps = (total + per - 1) / per;
+  pl->grid = (int)((warps + kTmaWarps - 1) / kTmaWarps);
+  const bool split = (per % pl->kchunks) != 0;
+  pl->max_slots = split ? (pl->kchunks - 1) / pl->per + 2 : 0;
+  pl->ws_bytes = split ? kCounterBytes + (size_t)pl->tiles * pl->max_slots * 32 * 4 * 4 : 0;
+  return true;
+}
 
 inline int mt_for(int M) { return M <= 8 ? 1 : (M <= 16 ? 2 : 4); }
 
@@ -86,7 +136,35 @@ cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   const bool split = (per % pl->kchunks) != 0;
   pl->max_slots = split ? (pl->kchunks - 1) / pl->per + 2 : 0;
   pl->ws_bytes = split ? kCounterBytes + (size_t)pl->tiles * pl->max_slots * 32 * 4 * MT * 4 : 0;
+  pl->ring_slots = 0;
   return cudaSuccess;
+}
+
+// Which plan a launch of these sizes uses: the bulk-copy kernel when it
+// applies (its tiles kept whole if the workspace is too small to split),
+// else the register-pipeline kernel.
+template <int BITS>
+bool choose_tma(int M, int N, int K, size_t ws_bytes, StreamPlan* pl) {
+  if (!tma_enabled() || !plan_tma<BITS>(M, N, K, true, pl)) return false;
+  if (pl->ws_bytes > ws_bytes) return plan_tma<BITS>(M, N, K, false, pl);
+  return true;
+}
+
+template <int BITS, int PRO, int EPI, bool FOLD>
+cudaError_t launch_tma(StreamParams p, const StreamPlan& pl, void* ws, cudaStream_t s, bool pdl) {
+  auto kern = gemv_tma_kernel<BITS, PRO, EPI, FOLD>;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  if (e != cudaSuccess) return e;
+  p.tiles = pl.tiles;
+  p.kchunks = pl.kchunks;
+  p.cp = pl.cp;
+  p.per = pl.per;
+  p.max_slots = pl.max_slots;
+  p.ring_slots = pl.ring_slots;
+  p.counters = pl.ws_bytes ? static_cast<int*>(ws) : nullptr;
+  p.slots = pl.ws_bytes ? reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes) : nullptr;
+  p.gshift = group_shift(p.K, p.G);
+  return lw_launch(kern, dim3(pl.grid), dim3(kTmaThreads), pl.smem, s, pdl, p);
 }
 
 // Launch one row block (M <= 32). The workspace (counters first, zeroed before
@@ -96,6 +174,12 @@ template <int BITS, int PRO, int EPI>
 cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl,
                                 bool allow_fold = false) {
   StreamPlan pl;
+  if constexpr (BITS != 16 && EPI != EPI_PEER_ARGMAX) {
+    if (choose_tma<BITS>(p.M, p.N, p.K, ws_bytes, &pl)) {
+      if (allow_fold && fold_scales<BITS>(p.K, p.G)) return launch_tma<BITS, PRO, EPI, true>(p, pl, ws, s, pdl);
+      return launch_tma<BITS, PRO, EPI, false>(p, pl, ws, s, pdl);
+    }
+  }
   cudaError_t e;
   const int mt = mt_for(p.M);
 #define LW_PLAN(MT_)                                                                    \
@@ -156,6 +240,10 @@ size_t stream_workspace(int M, int N, int K) {
   for (int m0 = 0; m0 < M; m0 += rows) {
     const int mb = std::min(rows, M - m0);
     StreamPlan pl;
+    if (BITS != 16 && EPI != EPI_PEER_ARGMAX && tma_enabled() && plan_tma<BITS>(mb, N, K, true, &pl)) {
+      need = std::max(need, pl.ws_bytes);
+      continue;
+    }
     cudaError_t e;
     const int mt = mt_for(mb);
     if (mt == 1)

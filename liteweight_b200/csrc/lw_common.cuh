@@ -147,6 +147,62 @@ LW_DEV void add_flagged8(const unsigned long long* src, size_t rank_stride, int 
   }
 }
 
+// ---------------------------------------------------------------- bulk copies
+
+LW_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+LW_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+// The initialised barriers become visible to the asynchronous (bulk copy) proxy.
+LW_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// Order this thread's earlier generic-proxy shared-memory accesses before its
+// later asynchronous-proxy ones (a bulk copy refilling a slot it has read).
+LW_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+LW_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+LW_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      " .reg .pred p;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Global -> shared bulk copy (16-byte aligned addresses, size a multiple of
+// 16), its bytes counted on the mbarrier at `bar`.
+LW_DEV void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Device error flag of this translation unit (each .cu file has its own copy:
+// the library is built without relocatable device code). Bounded waits that
+// give up record LW_ERR_TIMEOUT here; lw_take_device_error() reads them.
+static __device__ int lw_tu_error;
+
+LW_DEV void lw_record_error(int status) { atomicCAS(&lw_tu_error, 0, status); }
+
+// Wait for phase `parity` of the mbarrier at `bar`, bounded by the global
+// timer (timeout_ns) and an iteration cap; records LW_ERR_TIMEOUT on giving up.
+LW_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1; it < (1u << 24); ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u && (long long)(globaltimer_ns() - t0) > timeout_ns) break;
+  }
+  lw_record_error(LW_ERR_TIMEOUT);
+  return false;
+}
+
 // ---------------------------------------------------------------- tensor core
 
 // D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col).
@@ -245,6 +301,18 @@ LW_DEV float warp_max(float v) {
 LW_DEV float r16(float v) { return __half2float(__float2half_rn(v)); }
 
 }  // namespace lw
+
+// Host: read and clear this translation unit's device error flag on the
+// current device (synchronous). LW_OK when nothing was recorded.
+static inline int lw_tu_take_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, lw::lw_tu_error, sizeof(int)) != cudaSuccess) return LW_ERR_LAUNCH;
+  if (v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(lw::lw_tu_error, &z, sizeof(int)) != cudaSuccess) return LW_ERR_LAUNCH;
+  }
+  return v;
+}
 
 // Number of kernels this library has enqueued (lw_launch_count()).
 void lw_count_launch();
