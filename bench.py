@@ -370,10 +370,11 @@ class DecodeWorkload:
         torch.cuda.synchronize()
 
     def prefill(self):
-        """Load the prompt and run it through the step graph up to the first decode step."""
+        """Load the prompt and run it through the model in chunks (the engine's
+        prefill), up to the first decode step."""
         self.eng.start(self.prompt)
+        self.eng.prefill()
         self.eng.capture()
-        self.eng.step(self.P - 1)
 
     def step(self, it: int):
         self.eng.step(1)
@@ -710,7 +711,8 @@ def run_decode(args, dist: Dist):
     e2e_ms = dist.max(e["ms"], dev)
     e2e = {"value": round(e["tokens"] / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
            "h2d_bytes_per_step": e["h2d_bytes_per_step"], "d2h_bytes_per_step": e["d2h_bytes_per_step"],
-           "step": f"one call = prompt {wl.P} ids in, prefill + {wl.T} greedy tokens, ids out",
+           "step": f"one call = prompt {wl.P} ids in, chunked prefill ({wl.eng.prefill_rows} positions per "
+                   f"chunk) + {wl.T} greedy tokens, ids out",
            "ms_per_call": round(e2e_ms, 3)}
     clocks = clk.summary()
     launches = args.steps * wl.eng.kernels_per_step()

@@ -144,7 +144,8 @@ enum {
 /* What the fused GEMV does with each output. */
 enum {
   LW_EPI_PLAIN = 0,    /* out = fp16(y) (+bias) (+residual); residual may alias out */
-  LW_EPI_ROPE_KV = 1,  /* q|k|v rows (rope-pair order): RoPE q,k; q -> q_out, k,v -> cache at *pos */
+  LW_EPI_ROPE_KV = 1,  /* q|k|v rows (rope-pair order): RoPE q,k; q -> q_out, k,v -> cache at *pos
+                          (with prefill_seq: row m is position *pos + m of sequence *prefill_seq) */
   LW_EPI_SWIGLU = 2,   /* gate|up rows interleaved by 8: out[i] = silu(gate_i) * up_i */
   LW_EPI_F32 = 3,      /* out_f32 = y unrounded (tensor-parallel partial sum) */
   LW_EPI_ARGMAX = 4,   /* out = fp16 logits; argmax_keys[m] = max(key) (first max wins) */
@@ -179,7 +180,8 @@ enum {
 typedef struct {
   int world;            /* ranks taking part, 1..LW_MAX_RANKS */
   int rank;             /* this rank */
-  void* dst[LW_MAX_RANKS];  /* this rank's slot in rank d's receive buffer (mapped here) */
+  void* dst[LW_MAX_RANKS];  /* rank d's receive buffer (mapped here); this rank's words go at
+                               word offset rank * M * ldo (partials) or rank * M (keys) */
   const int* step;      /* device: decode steps completed; the same on every rank */
   int tag, tags_per_step;
   int* arrivals;        /* LW_EPI_PEER_ARGMAX: local int, zero before first use and left zero */
@@ -188,7 +190,7 @@ typedef struct {
 typedef struct {
   int world;
   int tag, tags_per_step;
-  const void* src;      /* local receive buffer: the world ranks' slots */
+  const void* src;      /* local receive buffer: rank r's words at r * M * K (partials) or r * M (keys) */
   const int* step;
   int* error;           /* device: set to LW_ERR_TIMEOUT when a wait gives up (may be NULL) */
   long long timeout_ns; /* wait limit */
@@ -228,6 +230,8 @@ typedef struct {
   size_t workspace_bytes;
   const lw_exchange_in* xin;    /* LW_PRO_PEER_RESID_NORM; read at the call */
   const lw_exchange_out* xout;  /* LW_EPI_PEER_*; read at the call */
+  const int* prefill_seq;       /* NULL: decode (row m = sequence m). Else a prompt chunk: the M
+                                   rows are positions *pos .. *pos + M - 1 of sequence *prefill_seq */
 } lw_fused_gemv_args;
 
 int lw_fused_gemv(const lw_fused_gemv_args* args, lw_stream_t stream);
@@ -246,6 +250,9 @@ typedef struct {
   void* out;
   const int* pos;
   int batch, n_q_heads, n_kv_heads, head_dim, max_seq, pdl;
+  const int* prefill_seq;  /* NULL: query row b is sequence b over positions 0..*pos. Else a prompt
+                              chunk of `batch` rows: row b is position *pos + b of sequence
+                              *prefill_seq, over positions 0..*pos + b (causal) */
 } lw_attention_args;
 
 int lw_attention_decode(const lw_attention_args* args, lw_stream_t stream);
@@ -270,6 +277,30 @@ int lw_embed_tokens(const int* tokens, const void* embed, void* x, const int* po
  * lm_head keys) is still cleared. */
 int lw_sample_tokens(int* tokens, unsigned long long* keys, const void* embed, void* x, int* pos, int* done,
                      int* step, const lw_exchange_in* xin, int batch, int hidden, int pdl, lw_stream_t stream);
+
+/* ---- chunked prefill: the prompt runs through the decode kernels M
+ * positions at a time (one sequence per chunk, rows = positions), so every
+ * weight is read once per chunk instead of once per prompt token. A chunk is
+ * lw_prefill_embed, the layers' kernels with prefill_seq set, then
+ * lw_prefill_advance (not the last chunk) or, for the last chunk, the
+ * lm_head GEMV and lw_prefill_sample. No counterpart in the reference, whose
+ * generate() runs the prompt through one HF forward call. */
+
+/* x[m] = embed[tokens[(*pos + m) * batch + *seq]] for m < rows. */
+int lw_prefill_embed(const int* tokens, const void* embed, void* x, const int* pos, const int* seq, int rows,
+                     int batch, int hidden, int pdl, lw_stream_t stream);
+
+/* *pos += rows and, when step != NULL, *step += 1 (after every earlier kernel of the stream). */
+int lw_prefill_advance(int* pos, int* step, int rows, int pdl, lw_stream_t stream);
+
+/* The token at position *pos + rows of sequence *seq: tokens[..] if >= 0,
+ * else the argmax decoded from keys[rows - 1] (or, with xin, the maximum of
+ * the world ranks' flagged keys of row rows - 1), then stored. Its embedding
+ * goes to x_out[*seq] (the decode step's residual stream); keys[0..rows) are
+ * cleared; *pos += rows; *step += 1 when step != NULL. */
+int lw_prefill_sample(int* tokens, unsigned long long* keys, const void* embed, void* x_out, int* pos, int* step,
+                      const int* seq, const lw_exchange_in* xin, int rows, int batch, int hidden, int pdl,
+                      lw_stream_t stream);
 
 /* ---- peer memory for the exchanges (setup calls: these allocate, map and
  * synchronise; they are not stream-ordered and must not be graph-captured) */

@@ -33,6 +33,7 @@ struct AttnParams {
   const __half* v;
   __half* out;         // [B][nq * hd]
   const int* pos;      // attend over positions 0..*pos
+  const int* seq;      // prompt chunk: row b is position *pos + b of sequence *seq (causal)
   int B, nq, nkv, S;
   float scale_log2;    // head_dim^-0.5 * log2(e)
 };
@@ -65,7 +66,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
-  const int len = *p.pos + 1;
+  pdl_launch_dependents();   // the next kernel's CTAs may start on the SMs this grid leaves idle
+  const int cs = p.seq ? *p.seq : b;                   // KV-cache sequence of this query row
+  const int len = *p.pos + 1 + (p.seq ? b : 0);
   const int per_round = kAttnCluster * W * kAttnPos;
   const int first = (rank * W + warp) * kAttnPos;
 
@@ -84,8 +87,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 #pragma unroll
     for (int d = 0; d < D; ++d) acc[h][d] = 0.f;
   }
-  const __half* kb = p.k + ((size_t)b * p.nkv + kvh) * p.S * HD + lane * D;
-  const __half* vb = p.v + ((size_t)b * p.nkv + kvh) * p.S * HD + lane * D;
+  const __half* kb = p.k + ((size_t)cs * p.nkv + kvh) * p.S * HD + lane * D;
+  const __half* vb = p.v + ((size_t)cs * p.nkv + kvh) * p.S * HD + lane * D;
   using VecT = typename std::conditional<D == 4, uint2, uint32_t>::type;
   VecT kr[2][kAttnPos], vr[2][kAttnPos];
   auto load_round = [&](int base, VecT (&kk)[kAttnPos], VecT (&vv)[kAttnPos]) {
@@ -147,7 +150,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     if (r + 2 < rounds) load_round((r + 2) * per_round, kr[0], vr[0]);
     process((r + 1) * per_round, kr[1], vr[1]);
   }
-  pdl_launch_dependents();
 
   // warps -> CTA
 #pragma unroll
@@ -207,6 +209,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
 __global__ void embed_kernel(const int* __restrict__ tokens, const __half* __restrict__ embed,
                              __half* __restrict__ x, const int* pos, int B, int H) {
   pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x;
   const int tok = tokens[(size_t)(*pos) * B + b];
   const uint4* src = reinterpret_cast<const uint4*>(embed + (size_t)tok * H);
@@ -239,6 +242,7 @@ struct SampleParams {
 
 __global__ void sample_kernel(const SampleParams p) {
   pdl_wait();
+  pdl_launch_dependents();
   __shared__ int s_tok;
   const int b = blockIdx.x;
   const int p_next = *p.pos + 1;
@@ -283,6 +287,90 @@ __global__ void sample_kernel(const SampleParams p) {
   }
 }
 
+// ------------------------------------------------------------- prefill chunks
+
+__global__ void prefill_embed_kernel(const int* __restrict__ tokens, const __half* __restrict__ embed,
+                                     __half* __restrict__ x, const int* pos, const int* seq, int B, int H) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int m = blockIdx.x;
+  const int tok = tokens[(size_t)(*pos + m) * B + *seq];
+  const uint4* src = reinterpret_cast<const uint4*>(embed + (size_t)tok * H);
+  uint4* dst = reinterpret_cast<uint4*>(x + (size_t)m * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+__global__ void prefill_advance_kernel(int* pos, int* step, int rows) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    *pos += rows;
+    if (step) *step += 1;
+  }
+}
+
+struct PrefillSampleParams {
+  int* tokens;
+  unsigned long long* keys;   // this rank's lm_head keys of the chunk rows
+  const __half* embed;
+  __half* x;                  // the decode step's residual stream [B][H]
+  int* pos;
+  int* step;                  // may be null
+  const int* seq;
+  int rows, B, H;
+  int in_world, in_tag, in_tags;   // in_world > 0: keys from the exchange (flagged words [in_world][rows])
+  const unsigned long long* in_src;
+  int* in_error;
+  long long in_timeout_ns;
+};
+
+// One block: the token after the chunk's last row (forced prompt token, or
+// the argmax of that row), its embedding as the decode residual of sequence
+// *seq, the chunk keys cleared, the position advanced past the chunk.
+__global__ void prefill_sample_kernel(const PrefillSampleParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int s_tok, s_seq, s_next;
+  if (threadIdx.x == 0) {
+    const int seq = *p.seq;
+    const int p_next = *p.pos + p.rows;
+    int tok = p.tokens[(size_t)p_next * p.B + seq];
+    if (tok < 0) {
+      unsigned long long key = 0;
+      const int r = p.rows - 1;
+      if (p.in_world) {
+        const unsigned long long f16 = exchange_flag16(exchange_flag(*p.step, p.in_tag, p.in_tags));
+        WaitBudget wb;
+        for (int k = 0; k < p.in_world; ++k) {
+          unsigned long long w;
+          do {
+            w = ld_volatile_u64(p.in_src + (size_t)k * p.rows + r);
+          } while ((w >> 48) != f16 && wb.keep_waiting(p.in_timeout_ns, p.in_error));
+          w &= 0xFFFFFFFFFFFFull;
+          key = w > key ? w : key;
+        }
+      } else {
+        key = __ldcg(p.keys + r);
+      }
+      tok = (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+      p.tokens[(size_t)p_next * p.B + seq] = tok;
+    }
+    s_tok = tok;
+    s_seq = seq;
+    s_next = p_next;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.rows; i += blockDim.x) p.keys[i] = 0ull;
+  const uint4* src = reinterpret_cast<const uint4*>(p.embed + (size_t)s_tok * p.H);
+  uint4* dst = reinterpret_cast<uint4*>(p.x + (size_t)s_seq * p.H);
+  for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = src[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *p.pos = s_next;
+    if (p.step) *p.step += 1;
+  }
+}
+
 }  // namespace lw
 
 // ======================================================================= host
@@ -316,12 +404,13 @@ int validate(const lw_fused_gemv_args* a) {
   if (a->M <= 0 || a->M > 32 || a->N <= 0 || a->K <= 0) return LW_ERR_BAD_SHAPE;
   if (a->bits != 16 && (!a->scales || a->group_size <= 0 || a->K % a->group_size)) return LW_ERR_BAD_GROUP;
   const int E = a->bits == 4 ? 32 : (a->bits == 8 ? 16 : 8);
-  if ((size_t)a->K * a->bits / 8 % 16 || a->K % 8 ||
+  if ((size_t)a->K * a->bits / 8 % 64 || a->K % 8 ||
       (a->bits != 16 && (a->group_size % E || lw::group_shift(a->K, a->group_size) < 0)))
     return LW_ERR_UNSUPPORTED;
   if (!al(a->act, 16) || !al(a->weight, 16) || a->lda % 8) return LW_ERR_ALIGNMENT;
   const int KC = 4 * E;
-  if ((size_t)a->M * ((a->K + KC - 1) / KC) * KC * 2 > (size_t)lw::kStageBudget) return LW_ERR_UNSUPPORTED;
+  if ((size_t)a->M * ((a->K + KC - 1) / KC) * KC * 2 + lw::gamma_bytes(a->prologue, a->K) > (size_t)lw::kStageBudget)
+    return LW_ERR_UNSUPPORTED;
   if (a->prologue != LW_PRO_PLAIN) {
     if (!a->gamma || !al(a->gamma, 16)) return LW_ERR_NULL_POINTER;
     if (a->prologue == LW_PRO_RESID_NORM && (!a->psum || !a->x_out || !al(a->psum, 16) || !al(a->x_out, 16)))
@@ -453,6 +542,7 @@ int lw_attention_decode(const lw_attention_args* a, lw_stream_t stream) {
   p.v = static_cast<const __half*>(a->v_cache);
   p.out = static_cast<__half*>(a->out);
   p.pos = a->pos;
+  p.seq = a->prefill_seq;
   p.B = a->batch;
   p.nq = a->n_q_heads;
   p.nkv = a->n_kv_heads;
@@ -527,6 +617,66 @@ int lw_sample_tokens(int* tokens, unsigned long long* keys, const void* embed, v
   }
   cudaGetLastError();
   cudaError_t e = lw_launch(lw::sample_kernel, dim3(batch), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                            pdl != 0, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+
+int lw_prefill_embed(const int* tokens, const void* embed, void* x, const int* pos, const int* seq, int rows,
+                     int batch, int hidden, int pdl, lw_stream_t stream) {
+  if (!tokens || !embed || !x || !pos || !seq) return LW_ERR_NULL_POINTER;
+  if (rows <= 0 || batch <= 0 || hidden <= 0 || hidden % 8) return LW_ERR_BAD_SHAPE;
+  if (!al(embed, 16) || !al(x, 16)) return LW_ERR_ALIGNMENT;
+  cudaGetLastError();
+  cudaError_t e = lw_launch(lw::prefill_embed_kernel, dim3(rows), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                            pdl != 0, tokens, static_cast<const __half*>(embed), static_cast<__half*>(x), pos, seq,
+                            batch, hidden);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+
+int lw_prefill_advance(int* pos, int* step, int rows, int pdl, lw_stream_t stream) {
+  if (!pos) return LW_ERR_NULL_POINTER;
+  if (rows <= 0) return LW_ERR_BAD_SHAPE;
+  cudaGetLastError();
+  cudaError_t e = lw_launch(lw::prefill_advance_kernel, dim3(1), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream),
+                            pdl != 0, pos, step, rows);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+
+int lw_prefill_sample(int* tokens, unsigned long long* keys, const void* embed, void* x_out, int* pos, int* step,
+                      const int* seq, const lw_exchange_in* xin, int rows, int batch, int hidden, int pdl,
+                      lw_stream_t stream) {
+  if (!tokens || !keys || !embed || !x_out || !pos || !seq) return LW_ERR_NULL_POINTER;
+  if (rows <= 0 || batch <= 0 || hidden <= 0 || hidden % 8) return LW_ERR_BAD_SHAPE;
+  if (!al(embed, 16) || !al(x_out, 16)) return LW_ERR_ALIGNMENT;
+  lw::PrefillSampleParams p = {};
+  p.tokens = tokens;
+  p.keys = keys;
+  p.embed = static_cast<const __half*>(embed);
+  p.x = static_cast<__half*>(x_out);
+  p.pos = pos;
+  p.step = step;
+  p.seq = seq;
+  p.rows = rows;
+  p.B = batch;
+  p.H = hidden;
+  if (xin) {
+    if (!xin->src || !step) return LW_ERR_NULL_POINTER;
+    if (xin->world < 1 || xin->world > LW_MAX_RANKS || xin->timeout_ns <= 0 || xin->tags_per_step <= 0 ||
+        xin->tag < 0 || xin->tag >= xin->tags_per_step)
+      return LW_ERR_BAD_SHAPE;
+    if (!al(xin->src, 8)) return LW_ERR_ALIGNMENT;
+    p.in_world = xin->world;
+    p.in_tag = xin->tag;
+    p.in_tags = xin->tags_per_step;
+    p.in_src = static_cast<const unsigned long long*>(xin->src);
+    p.in_error = xin->error;
+    p.in_timeout_ns = xin->timeout_ns;
+  }
+  cudaGetLastError();
+  cudaError_t e = lw_launch(lw::prefill_sample_kernel, dim3(1), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
                             pdl != 0, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;

@@ -37,6 +37,7 @@ inline StreamParams to_stream(const lw_fused_gemv_args* a) {
   p.out_f32 = a->out_f32;
   p.argmax_keys = a->argmax_keys;
   p.argmax_offset = a->argmax_offset;
+  p.seq = a->prefill_seq;
   if (a->prologue == LW_PRO_PEER_RESID_NORM && a->xin) {
     p.in_world = a->xin->world;
     p.in_tag = a->xin->tag;
@@ -48,6 +49,7 @@ inline StreamParams to_stream(const lw_fused_gemv_args* a) {
   }
   if ((a->epilogue == LW_EPI_PEER_F32 || a->epilogue == LW_EPI_PEER_ARGMAX) && a->xout) {
     p.out_world = a->xout->world;
+    p.out_rank = a->xout->rank;
     p.out_tag = a->xout->tag;
     p.out_tags = a->xout->tags_per_step;
     p.out_step = a->xout->step;

@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(512) gemm_f16_kn_kernel(const GemvParams p) {
   };
   load_batch(sb);
   pdl_wait();
+  pdl_launch_dependents();
   {
     const int kpad = ksteps * 16;
     const int groups8 = kpad / 8;
@@ -151,7 +152,6 @@ __global__ void __launch_bounds__(512) gemm_f16_kn_kernel(const GemvParams p) {
     }
     if (s0 + U < se) load_batch(s0 + U);
   }
-  pdl_launch_dependents();
 
   float* red = reinterpret_cast<float*>(smem + (size_t)p.M * p.cp * 2);
   const int CW = MT * 8;
@@ -224,7 +224,9 @@ template <int BITS>
 bool stream_ok(const void* act, const void* w, int K, int G) {
   constexpr int E = lw::WT<BITS>::E;
   const size_t rowbytes = (size_t)K * BITS / 8;
-  return (rowbytes % 16 == 0) && (K % 8 == 0) && aligned(w, 16) && aligned(act, 16) &&
+  // the stream kernel reads whole 64-byte chunks of a row (true for every
+  // group size liteweight uses: K is a multiple of the group)
+  return (rowbytes % 64 == 0) && (K % 8 == 0) && aligned(w, 16) && aligned(act, 16) &&
          (BITS == 16 || (G % E == 0 && lw::group_shift(K, G) >= 0));
 }
 

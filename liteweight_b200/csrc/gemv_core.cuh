@@ -109,6 +109,7 @@ struct StreamParams {
   int* counters;           // [tiles], zero before the first launch, left zero
   int max_slots;
   int ring_slots;          // gemv_tma_kernel: shared-memory slots per warp
+  const int* seq;          // prompt chunk (EPI_ROPE_KV): row m is position *pos + m of sequence *seq
   // tensor-parallel exchange, consumer (PRO_PEER_RESID_NORM): flagged words
   int in_world, in_tag, in_tags;
   const unsigned long long* in_src;    // local [in_world][M][K]
@@ -116,9 +117,9 @@ struct StreamParams {
   int* in_error;
   long long in_timeout_ns;
   // tensor-parallel exchange, producer (EPI_PEER_*)
-  int out_world, out_tag, out_tags;
+  int out_world, out_rank, out_tag, out_tags;
   const int* out_step;
-  unsigned long long* out_dst[kMaxRanks];  // this rank's slot on rank d: [M][ldo] or [M] words
+  unsigned long long* out_dst[kMaxRanks];  // rank d's receive buffer; this rank's words at out_rank * M * ldo (or * M)
   int* out_arrivals;                   // EPI_PEER_ARGMAX: local, zero, left zero
 };
 
@@ -257,9 +258,10 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
           } else if constexpr (EPI == EPI_PEER_F32) {
             // straight into every rank's receive buffer (peer stores over NVLink)
             const unsigned long long word = ((unsigned long long)flag << 32) | __float_as_uint(v[mt][i]);
+            const size_t at = ((size_t)p.out_rank * p.M + m) * p.ldo + n;
 #pragma unroll
             for (int d = 0; d < kMaxRanks; ++d)
-              if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + (size_t)m * p.ldo + n, word);
+              if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + at, word);
           } else {
             float y = r16(v[mt][i]);
             if (p.bias) y = r16(y + __half2float(p.bias[n]));
@@ -275,11 +277,8 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
     const int head = (tile * 16) / hd;
     const int jt = tile % (hd / 16);
     const int d_lo = 8 * jt + g, d_hi = d_lo + hd / 2;
-    const int pos = *p.pos;
-    const float c_lo = __half2float(p.rope_cos[(size_t)pos * hd + d_lo]);
-    const float c_hi = __half2float(p.rope_cos[(size_t)pos * hd + d_hi]);
-    const float s_lo = __half2float(p.rope_sin[(size_t)pos * hd + d_lo]);
-    const float s_hi = __half2float(p.rope_sin[(size_t)pos * hd + d_hi]);
+    const int pos0 = *p.pos;
+    const int seq = p.seq ? *p.seq : -1;   // prompt chunk: rows are positions of one sequence
     const int nq = p.n_q_heads, nkv = p.n_kv_heads;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -287,10 +286,16 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
       for (int c = 0; c < 2; ++c) {
         const int m = mt * 8 + 2 * t + c;
         if (m >= p.M || n_lo >= p.N) continue;
+        const int pos = seq >= 0 ? pos0 + m : pos0;
+        const int row = seq >= 0 ? seq : m;   // KV-cache sequence
         const float y_lo = r16(v[mt][c]), y_hi = r16(v[mt][2 + c]);
         float o_lo = y_lo, o_hi = y_hi;
         if (head < nq + nkv) {
           // modeling_llama.py:161-162: q*cos + rotate_half(q)*sin, fp16 after each op
+          const float c_lo = __half2float(p.rope_cos[(size_t)pos * hd + d_lo]);
+          const float c_hi = __half2float(p.rope_cos[(size_t)pos * hd + d_hi]);
+          const float s_lo = __half2float(p.rope_sin[(size_t)pos * hd + d_lo]);
+          const float s_hi = __half2float(p.rope_sin[(size_t)pos * hd + d_hi]);
           o_lo = r16(r16(y_lo * c_lo) + r16(-y_hi * s_lo));
           o_hi = r16(r16(y_hi * c_hi) + r16(y_lo * s_hi));
         }
@@ -298,9 +303,9 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
         if (head < nq) {
           dst = p.q_out + (size_t)m * nq * hd + (size_t)head * hd;
         } else if (head < nq + nkv) {
-          dst = p.k_cache + (((size_t)m * nkv + (head - nq)) * p.max_seq + pos) * hd;
+          dst = p.k_cache + (((size_t)row * nkv + (head - nq)) * p.max_seq + pos) * hd;
         } else {
-          dst = p.v_cache + (((size_t)m * nkv + (head - nq - nkv)) * p.max_seq + pos) * hd;
+          dst = p.v_cache + (((size_t)row * nkv + (head - nq - nkv)) * p.max_seq + pos) * hd;
         }
         dst[d_lo] = __float2half_rn(o_lo);
         dst[d_hi] = __float2half_rn(o_hi);
@@ -355,7 +360,8 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
 // the all-reduced partial sum to the residual (CTA 0 writes the new residual).
 // Called by all NT threads of the CTA; ends with a CTA barrier.
 template <int BITS, int PRO, int NT>
-LW_DEV void stage_activation(const StreamParams& p, __half* act_s, float* ssq, uint32_t in_flag, WaitBudget& wb) {
+LW_DEV void stage_activation(const StreamParams& p, __half* act_s, const __half* gam_s, float* ssq, uint32_t in_flag,
+                             WaitBudget& wb) {
   constexpr int E = WT<BITS>::E;
   constexpr int KC = 4 * E;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -424,7 +430,7 @@ LW_DEV void stage_activation(const StreamParams& p, __half* act_s, float* ssq, u
         const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
         __half* dst = act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8;
         uint4 v = lds128(dst);
-        uint4 gm = ldg_nc(p.gamma + k);
+        uint4 gm = lds128(gam_s + k);
         if constexpr (BITS == 4) gm = perm_int4_pairs(gm);
         __half* hv = reinterpret_cast<__half*>(&v);
         const __half* hg = reinterpret_cast<const __half*>(&gm);
@@ -436,6 +442,18 @@ LW_DEV void stage_activation(const StreamParams& p, __half* act_s, float* ssq, u
     }
   }
   __syncthreads();
+}
+
+// Copies the RMSNorm weight into shared memory (natural order). It does not
+// depend on the previous kernel, so this runs before griddepcontrol.wait and
+// its DRAM latency overlaps the previous kernel's tail. The copy is read after
+// the first barrier of stage_activation.
+template <int PRO, int NT>
+LW_DEV void stage_gamma(const StreamParams& p, __half* gam_s) {
+  if constexpr (PRO != PRO_PLAIN) {
+    const int groups8 = (p.K + 7) / 8;
+    for (int i = threadIdx.x; i < groups8; i += NT) sts128(gam_s + i * 8, ldg_nc(p.gamma + i * 8));
+  }
 }
 
 // A warp's tile segment [seg_c0, end_c) is done: a whole tile runs the
@@ -508,6 +526,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   constexpr bool SCALED = BITS < 16;
   extern __shared__ __align__(16) uint8_t smem[];
   __half* act_s = reinterpret_cast<__half*>(smem);
+  __half* gam_s = act_s + (size_t)p.M * p.cp;   // norm prologues: gamma [K], after the staged rows
   __shared__ float ssq[kMaxM];
 
   const int tid = threadIdx.x, lane = tid & 31;
@@ -517,29 +536,29 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   const int total = p.tiles * C;
   const int g0 = min(total, wid * p.per), g1 = min(total, g0 + p.per);
   const size_t rowbytes = (size_t)p.K * BITS / 8;
-  const int npieces = (int)(rowbytes / 16);
   const int ngroups = SCALED ? p.K / p.G : 1;
 
   // ---- the warp's run [g0, g1) of flattened (tile, chunk) work, cut into
-  // tile segments. A segment sets its row and scale pointers once and steps
-  // through batches of U chunks; loads run two batches ahead of the tensor
-  // cores (register double buffer) and L2 prefetches kPrefetch batches ahead
-  // of the loads. Rows past N are clamped to N-1 (computed, never stored);
-  // when a row does not end on a whole chunk, pieces past it are clamped to
-  // its last piece and meet zero activations.
-  const bool full = (rowbytes & 63) == 0;
+  // tile segments. A segment sets its row, scale and activation pointers once
+  // and steps through batches of U chunks; loads run two batches ahead of the
+  // tensor cores (register double buffer) and L2 prefetches kPrefetch batches
+  // ahead of the loads. Rows past N are clamped to N-1 (computed, never
+  // stored). Rows are whole 64-byte chunks (the host routes other shapes to
+  // the generic kernel), so no piece needs clamping; only a segment's last
+  // batch may hold fewer than U chunks.
   const unsigned short* sbase = reinterpret_cast<const unsigned short*>(p.scales);
   const int toff = FOLD ? 0 : t * E;
 
   int s_tile = g0 / max(C, 1);
   int s_c0 = g0 - s_tile * C;
   int s_len = min(C - s_c0, g1 - g0);
-  const uint8_t *w0 = nullptr, *w1 = nullptr;
-  const unsigned short *sc0 = nullptr, *sc1 = nullptr;
+  const uint8_t *w0 = nullptr, *w1 = nullptr;          // the lane's piece of chunk s_c0, rows g / g+8
+  const unsigned short *sc0 = nullptr, *sc1 = nullptr;  // scale rows g / g+8
   auto seg_setup = [&]() {
     const int r0 = min(s_tile * 16 + g, p.N - 1), r1 = min(s_tile * 16 + g + 8, p.N - 1);
-    w0 = p.w + (size_t)r0 * rowbytes;
-    w1 = p.w + (size_t)r1 * rowbytes;
+    const size_t piece = ((size_t)s_c0 * 4 + t) * 16;
+    w0 = p.w + (size_t)r0 * rowbytes + piece;
+    w1 = p.w + (size_t)r1 * rowbytes + piece;
     if constexpr (SCALED) {
       sc0 = sbase + (size_t)r0 * ngroups;
       sc1 = sbase + (size_t)r1 * ngroups;
@@ -548,19 +567,16 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
 
   uint4 qa0[U], qb0[U], qa1[U], qb1[U];
   uint32_t sa0[U], sb0[U], sa1[U], sb1[U];
-  // batch b of the current segment: chunks s_c0 + b*U + u for b*U + u < s_len
-  auto load = [&](int b, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
+  // batch b of the current segment: chunks s_c0 + b*U + u (u < n)
+  auto load = [&](int b, int n, uint4(&qa)[U], uint4(&qb)[U], uint32_t(&sa)[U], uint32_t(&sb)[U]) {
+    const size_t off = (size_t)b * (U * 64);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (b * U + u < s_len) {
-        const int c = s_c0 + b * U + u;
-        int pc = c * 4 + t;
-        if (!full) pc = min(pc, npieces - 1);
-        qa[u] = ldg_stream(w0 + (size_t)pc * 16);
-        qb[u] = ldg_stream(w1 + (size_t)pc * 16);
+      if (u < n) {
+        qa[u] = ldg_stream(w0 + off + u * 64);
+        qb[u] = ldg_stream(w1 + off + u * 64);
         if constexpr (SCALED) {
-          int grp = (c * KC + toff) >> p.gshift;
-          if (!full) grp = min(grp, ngroups - 1);
+          const int grp = ((s_c0 + b * U + u) * KC + toff) >> p.gshift;
           const uint32_t h0 = __ldg(sc0 + grp), h1 = __ldg(sc1 + grp);
           if constexpr (FOLD) {
             sa[u] = __float_as_uint(__half2float(__ushort_as_half((unsigned short)h0)));
@@ -594,7 +610,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
     }
     if ((lane >> 4) < pf_left) {
       const int row = min(tl * 16 + (lane & 15), p.N - 1);
-      prefetch_l2_line(p.w + (size_t)row * rowbytes + min((size_t)ch * 64, rowbytes - 16));
+      prefetch_l2_line(p.w + (size_t)row * rowbytes + (size_t)ch * 64);
     }
     pf_skip();
   };
@@ -603,15 +619,20 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   int nb = (s_len + U - 1) / U;
   if (s_len > 0) {
     seg_setup();
-    load(0, qa0, qb0, sa0, sb0);
-    if (nb > 1) load(1, qa1, qb1, sa1, sb1);
+    load(0, min(U, s_len), qa0, qb0, sa0, sb0);
+    if (nb > 1) load(1, min(U, s_len - U), qa1, qb1, sa1, sb1);
   }
   pf_skip();   // the two batches loaded directly
   pf_skip();
 #pragma unroll 1
   for (int i = 0; i < kPrefetch; ++i) prefetch_next();
 
+  stage_gamma<PRO, kStreamThreads>(p, gam_s);
   pdl_wait();
+  // Let the next kernel's CTAs launch as soon as this one's exit: they take
+  // the SM slots freed by CTAs that finish early and stream their weights
+  // (which do not depend on this kernel) while the last CTAs here finish.
+  pdl_launch_dependents();
 
   // the previous kernels are complete: the step number is final
   uint32_t in_flag = 0, out_flag = 0;
@@ -619,7 +640,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   if constexpr (kPeerEpi<EPI>) out_flag = exchange_flag(*p.out_step, p.out_tag, p.out_tags);
   WaitBudget wb;
 
-  stage_activation<BITS, PRO, kStreamThreads>(p, act_s, ssq, in_flag, wb);
+  stage_activation<BITS, PRO, kStreamThreads>(p, act_s, gam_s, ssq, in_flag, wb);
 
   float acc[MT][4];
 #pragma unroll
@@ -628,12 +649,14 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) arow[mt] = act_s + (size_t)min(g + 8 * mt, p.M - 1) * p.cp + t * 8;
 
-  auto compute = [&](int b, const uint4(&qa)[U], const uint4(&qb)[U], const uint32_t(&sa)[U],
+  // batch b of the segment, its first n chunks (a full batch has n == U)
+  auto compute = [&](int b, int n, const uint4(&qa)[U], const uint4(&qb)[U], const uint32_t(&sa)[U],
                      const uint32_t(&sb)[U]) {
+    const int off0 = (s_c0 + b * U) * KC;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (b * U + u < s_len) {
-        const int off = (s_c0 + b * U + u) * KC;
+      if (u < n) {
+        const int off = off0 + u * KC;
         if constexpr (SCALED && FOLD) {
           float dc[MT][4];
 #pragma unroll
@@ -656,16 +679,22 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
 
   int done = 0;   // chunks of the run finished in earlier segments
   while (s_len > 0) {
+    const int nfull = s_len / U;   // batches 0 .. nfull-1 hold U chunks; batch nfull the rest
+    const int last = s_len - nfull * U;
     for (int b = 0;; b += 2) {
-      compute(b, qa0, qb0, sa0, sb0);
+      if (b < nfull) compute(b, U, qa0, qb0, sa0, sb0);
+      else compute(b, last, qa0, qb0, sa0, sb0);
       if (b + 2 < nb) {
-        load(b + 2, qa0, qb0, sa0, sb0);
+        if (b + 2 < nfull) load(b + 2, U, qa0, qb0, sa0, sb0);
+        else load(b + 2, last, qa0, qb0, sa0, sb0);
         prefetch_next();
       }
       if (b + 1 >= nb) break;
-      compute(b + 1, qa1, qb1, sa1, sb1);
+      if (b + 1 < nfull) compute(b + 1, U, qa1, qb1, sa1, sb1);
+      else compute(b + 1, last, qa1, qb1, sa1, sb1);
       if (b + 3 < nb) {
-        load(b + 3, qa1, qb1, sa1, sb1);
+        if (b + 3 < nfull) load(b + 3, U, qa1, qb1, sa1, sb1);
+        else load(b + 3, last, qa1, qb1, sa1, sb1);
         prefetch_next();
       }
       if (b + 2 >= nb) break;
@@ -680,8 +709,8 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
     nb = (s_len + U - 1) / U;
     if (s_len > 0) {
       seg_setup();
-      load(0, qa0, qb0, sa0, sb0);
-      if (nb > 1) load(1, qa1, qb1, sa1, sb1);
+      load(0, min(U, s_len), qa0, qb0, sa0, sb0);
+      if (nb > 1) load(1, min(U, s_len - U), qa1, qb1, sa1, sb1);
       prefetch_next();
       prefetch_next();
     }
@@ -706,12 +735,11 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
         const unsigned long long word = (__ldcg(p.argmax_keys + m) & 0xFFFFFFFFFFFFull) | f16;
 #pragma unroll
         for (int d = 0; d < kMaxRanks; ++d)
-          if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + m, word);
+          if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + (size_t)p.out_rank * p.M + m, word);
       }
       if (tid == 0) *p.out_arrivals = 0;
     }
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace lw

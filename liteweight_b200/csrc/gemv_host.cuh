@@ -48,9 +48,12 @@ inline bool tma_enabled() {
 
 constexpr size_t kTmaSmemBudget = 232448 - 512;   // opt-in dynamic shared memory per CTA, less static
 
+// Shared memory for the RMSNorm weight of the norm prologues (K halves, whole 16-byte groups).
+inline size_t gamma_bytes(int pro, int K) { return pro == PRO_PLAIN ? 0 : (size_t)(K + 7) / 8 * 16; }
+
 // Plan of the bulk-copy kernel; false when its ring (>= 3 slots per warp) and
 // the staged activation do not fit in shared memory.
-template <int BITS>
+template <int BITS, int PRO>
 bool plan_tma(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   constexpr int KC = 4 * WT<BITS>::E;
   if (BITS == 16 || M > 8) return false;
@@ -59,7 +62,7 @@ bool plan_tma(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   pl->kchunks = (K + KC - 1) / KC;
   const int kpad = pl->kchunks * KC;
   pl->cp = ((size_t)M * (kpad + 32) * 2 <= (size_t)kStageBudget) ? kpad + 32 : kpad;
-  const size_t act = align_up((size_t)M * pl->cp * 2, 128);
+  const size_t act = align_up((size_t)M * pl->cp * 2 + gamma_bytes(PRO, K), 128);
   if (act + kTmaBarBytes >= kTmaSmemBudget) return false;
   const int slots = (int)std::min<size_t>(kTmaMaxSlots, (kTmaSmemBudget - kTmaBarBytes - act) /
                                                             ((size_t)kTmaWarps * kTmaSlotBytes));
@@ -116,8 +119,8 @@ cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   pl->tiles = (N + 15) / 16;
   pl->kchunks = (K + KC - 1) / KC;
   const int kpad = pl->kchunks * KC;
-  pl->cp = ((size_t)M * (kpad + 32) * 2 <= (size_t)kStageBudget) ? kpad + 32 : kpad;
-  pl->smem = (size_t)M * pl->cp * 2;
+  pl->cp = ((size_t)M * (kpad + 32) * 2 + gamma_bytes(PRO, K) <= (size_t)kStageBudget) ? kpad + 32 : kpad;
+  pl->smem = (size_t)M * pl->cp * 2 + gamma_bytes(PRO, K);
   auto kern = gemv_stream_kernel<BITS, MT, kBatch, PRO, EPI, BITS < 16>;
   cudaError_t e = cudaSuccess;
   if (pl->smem > 48 * 1024) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl->smem);
@@ -143,10 +146,10 @@ cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
 // Which plan a launch of these sizes uses: the bulk-copy kernel when it
 // applies (its tiles kept whole if the workspace is too small to split),
 // else the register-pipeline kernel.
-template <int BITS>
+template <int BITS, int PRO>
 bool choose_tma(int M, int N, int K, size_t ws_bytes, StreamPlan* pl) {
-  if (!tma_enabled() || !plan_tma<BITS>(M, N, K, true, pl)) return false;
-  if (pl->ws_bytes > ws_bytes) return plan_tma<BITS>(M, N, K, false, pl);
+  if (!tma_enabled() || !plan_tma<BITS, PRO>(M, N, K, true, pl)) return false;
+  if (pl->ws_bytes > ws_bytes) return plan_tma<BITS, PRO>(M, N, K, false, pl);
   return true;
 }
 
@@ -175,7 +178,7 @@ cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaS
                                 bool allow_fold = false) {
   StreamPlan pl;
   if constexpr (BITS != 16 && EPI != EPI_PEER_ARGMAX) {
-    if (choose_tma<BITS>(p.M, p.N, p.K, ws_bytes, &pl)) {
+    if (choose_tma<BITS, PRO>(p.M, p.N, p.K, ws_bytes, &pl)) {
       if (allow_fold && fold_scales<BITS>(p.K, p.G)) return launch_tma<BITS, PRO, EPI, true>(p, pl, ws, s, pdl);
       return launch_tma<BITS, PRO, EPI, false>(p, pl, ws, s, pdl);
     }
@@ -240,7 +243,7 @@ size_t stream_workspace(int M, int N, int K) {
   for (int m0 = 0; m0 < M; m0 += rows) {
     const int mb = std::min(rows, M - m0);
     StreamPlan pl;
-    if (BITS != 16 && EPI != EPI_PEER_ARGMAX && tma_enabled() && plan_tma<BITS>(mb, N, K, true, &pl)) {
+    if (BITS != 16 && EPI != EPI_PEER_ARGMAX && tma_enabled() && plan_tma<BITS, PRO>(mb, N, K, true, &pl)) {
       need = std::max(need, pl.ws_bytes);
       continue;
     }

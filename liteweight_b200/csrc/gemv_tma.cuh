@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const StreamPa
 
   uint8_t* ring = smem + kTmaBarBytes + (size_t)warp * S * kTmaSlotBytes;
   __half* act_s = reinterpret_cast<__half*>(smem + kTmaBarBytes + (size_t)kTmaWarps * S * kTmaSlotBytes);
+  __half* gam_s = act_s + (size_t)p.M * p.cp;
   const uint32_t bars = smem_u32(smem) + 8u * (uint32_t)(warp * S);
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(bars + 8u * s, 1);
@@ -113,13 +114,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const StreamPa
   int tA = cs.t, cA = cs.c, nA = cs.take(U, C);
   if (nA) load_scales(tA, cA, nA, saA, sbA);
 
+  stage_gamma<PRO, kTmaThreads>(p, gam_s);
   pdl_wait();
+  pdl_launch_dependents();   // the next kernel's CTAs may fill the SM slots freed here
 
   uint32_t in_flag = 0, out_flag = 0;
   if constexpr (PRO == PRO_PEER_RESID_NORM) in_flag = exchange_flag(*p.in_step, p.in_tag, p.in_tags);
   if constexpr (kPeerEpi<EPI>) out_flag = exchange_flag(*p.out_step, p.out_tag, p.out_tags);
   WaitBudget wb;
-  stage_activation<BITS, PRO, kTmaThreads>(p, act_s, ssq, in_flag, wb);
+  stage_activation<BITS, PRO, kTmaThreads>(p, act_s, gam_s, ssq, in_flag, wb);
 
   float acc[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
   int seg_c0 = g0 - (g0 / max(C, 1)) * C;
@@ -187,7 +190,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const StreamPa
       if ((pending >> s) & 1u) mbar_wait_bounded(bars + 8u * s, (phase >> s) & 1u, kTmaWaitNs);
   }
 
-  pdl_launch_dependents();
 }
 
 }  // namespace lw

@@ -74,7 +74,7 @@ class FusedGemvArgs(ctypes.Structure):
         ("q_out", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
         ("out_f32", c_void_p), ("argmax_keys", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
-        ("xin", c_void_p), ("xout", c_void_p),
+        ("xin", c_void_p), ("xout", c_void_p), ("prefill_seq", c_void_p),
     ]
 
 
@@ -83,7 +83,7 @@ class AttentionArgs(ctypes.Structure):
     _fields_ = [
         ("q", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p), ("out", c_void_p), ("pos", c_void_p),
         ("batch", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("max_seq", c_int),
-        ("pdl", c_int),
+        ("pdl", c_int), ("prefill_seq", c_void_p),
     ]
 
 
@@ -93,6 +93,9 @@ nat.register("lw_attention_decode", [ctypes.POINTER(AttentionArgs), c_void_p])
 nat.register("lw_embed_tokens", [c_void_p] * 4 + [c_int] * 3 + [c_void_p])
 nat.register("lw_sample_tokens", [c_void_p] * 8 + [c_int] * 3 + [c_void_p])
 nat.register("lw_struct_size", [c_int], c_size_t)
+nat.register("lw_prefill_embed", [c_void_p] * 5 + [c_int] * 4 + [c_void_p])
+nat.register("lw_prefill_advance", [c_void_p] * 2 + [c_int] * 2 + [c_void_p])
+nat.register("lw_prefill_sample", [c_void_p] * 8 + [c_int] * 4 + [c_void_p])
 nat.register("lw_peer_alloc", [c_size_t, ctypes.POINTER(c_void_p)])
 nat.register("lw_peer_free", [c_void_p])
 nat.register("lw_peer_handle_size", [], c_size_t)
@@ -239,6 +242,23 @@ def default_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
 
 # ------------------------------------------------------------------ engine
 
+def prefill_rows(spec: LlamaSpec, tp_size: int = 1, limit: int = 32) -> int:
+    """Positions per prompt chunk: the most rows every GEMV of the layer can
+    stage in shared memory (rows x K padded to whole chunks, fp16, plus the
+    RMSNorm weight for the norm prologues, within 220 KiB), at most `limit`."""
+    budget = 220 * 1024
+
+    def rows_for(K, bits, norm):
+        kc = {4: 128, 8: 64, 16: 32}[bits]
+        kpad = -(-K // kc) * kc
+        return (budget - (((K + 7) // 8) * 16 if norm else 0)) // (2 * kpad)
+
+    H, hd = spec.hidden, spec.head_dim
+    rows = min(rows_for(H, spec.bits, True), rows_for(spec.n_heads // tp_size * hd, spec.bits, False),
+               rows_for(spec.inter // tp_size, spec.bits, False), rows_for(H, 16, True))
+    return max(1, min(limit, rows))
+
+
 def _align(v: int, a: int) -> int:
     return (v + a - 1) // a * a
 
@@ -249,8 +269,9 @@ class PeerExchange:
     rank's mappings of their blocks.
 
     Values travel as flagged 8-byte words (include/liteweight_b200.h,
-    tensor-parallel exchange). Block layout (bytes): keys [world][batch] words
-    | two slot sets, each [world][batch][hidden] words. Partial-sum exchange e
+    tensor-parallel exchange). Block layout (bytes): keys [world][rows] words
+    | two slot sets, each [world][rows][hidden] words, for up to `batch` rows
+    (a launch of M rows uses the first world * M rows of a set). Partial-sum exchange e
     (o_proj of layer e // 2, or its down_proj) uses slot set e % 2: a rank can
     only be one exchange ahead of another (it cannot produce exchange e + 1
     before it has consumed e, which needs every rank's e), so a set is never
@@ -293,8 +314,7 @@ class PeerExchange:
             out = ExchangeOut(world=world, rank=rank, step=self.step.data_ptr(), tag=e, tags_per_step=self.tags,
                               arrivals=self.arrivals.data_ptr())
             for d in range(world):
-                own = self.part_bytes * rank if e < n_partial else 8 * batch * rank
-                out.dst[d] = self.peers[d] + self._recv_offset(e) + own
+                out.dst[d] = self.peers[d] + self._recv_offset(e)   # the kernel adds rank * rows
             self.outs.append(out)
             self.ins.append(ExchangeIn(world=world, tag=e, tags_per_step=self.tags,
                                        src=self.base + self._recv_offset(e), step=self.step.data_ptr(),
@@ -366,41 +386,65 @@ class DecodeEngine:
         f16 = dict(dtype=torch.float16, device=dev)
         self.k_cache = [torch.zeros(batch, self.nkv, max_seq, hd, **f16) for _ in layers]
         self.v_cache = [torch.zeros(batch, self.nkv, max_seq, hd, **f16) for _ in layers]
-        self.x = torch.zeros(batch, H, **f16)
-        self.x2 = torch.zeros(batch, H, **f16)
-        self.q = torch.zeros(batch, self.nq * hd, **f16)
-        self.attn = torch.zeros(batch, self.nq * hd, **f16)
-        self.act = torch.zeros(batch, self.inter, **f16)
-        self.logits = torch.zeros(batch, self.vshard, **f16)
-        self.psum = torch.zeros(batch, H, dtype=torch.float32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.done = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.keys = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.seq = torch.zeros(1, dtype=torch.int32, device=dev)   # sequence of the prompt chunk in flight
         self.tokens = torch.full((max_seq + 1, batch), -1, dtype=torch.int32, device=dev)
         self.step_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        # decode buffers (row = sequence) and prompt-chunk buffers (row = position)
+        self.prefill_rows = prefill_rows(spec, tp_size)
+        self.dec = self._buffers(batch)
+        self.pf = self._buffers(self.prefill_rows)
+        self.x, self.x2, self.q, self.attn = self.dec.x, self.dec.x2, self.dec.q, self.dec.attn
+        self.act, self.logits, self.psum, self.keys = self.dec.act, self.dec.logits, self.dec.psum, self.dec.keys
         self.exchange = None
         if tp_size > 1 and exchange == "peer":
-            self.exchange = PeerExchange(tp_group, tp_rank, tp_size, batch, H, 2 * len(layers), dev,
-                                         exchange_timeout_s)
+            self.exchange = PeerExchange(tp_group, tp_rank, tp_size, max(batch, self.prefill_rows), H,
+                                         2 * len(layers), dev, exchange_timeout_s)
             self.step_count = self.exchange.step
         self._build_calls()
         self.graph = None
+        self.prefill_graphs = {}
         self.host_pos = 0
 
+    def _buffers(self, rows: int):
+        """Activations of one launch shape (rows = sequences of a decode step or
+        positions of a prompt chunk)."""
+        dev, H, hd = self.device, self.spec.hidden, self.spec.head_dim
+        f16 = dict(dtype=torch.float16, device=dev)
+
+        class Bufs:
+            pass
+        b = Bufs()
+        b.rows = rows
+        b.x, b.x2 = torch.zeros(rows, H, **f16), torch.zeros(rows, H, **f16)
+        b.q = torch.zeros(rows, self.nq * hd, **f16)
+        b.attn = torch.zeros(rows, self.nq * hd, **f16)
+        b.act = torch.zeros(rows, self.inter, **f16)
+        b.logits = torch.zeros(rows, self.vshard, **f16)
+        b.psum = torch.zeros(rows, H, dtype=torch.float32, device=dev)
+        b.keys = torch.zeros(rows, dtype=torch.int64, device=dev)
+        return b
+
     # -------------------------------------------------------------- call table
-    def _gemv(self, **kw) -> FusedGemvArgs:
+    def _gemv(self, rows: int, **kw) -> FusedGemvArgs:
         a = FusedGemvArgs()
-        a.pdl, a.M, a.eps, a.fold_scales = self.pdl, self.B, self.spec.eps, self.fold
+        a.pdl, a.M, a.eps, a.fold_scales = self.pdl, rows, self.spec.eps, self.fold
         for k, v in kw.items():
             setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
         return a
 
-    def _build_calls(self):
-        sp, B, H, hd = self.spec, self.B, self.spec.hidden, self.spec.head_dim
+    def _make_calls(self, bufs, prefill: bool, final: bool = True):
+        """The kernels of one decode step (prefill=False: row b = sequence b at
+        *pos) or of one prompt chunk (prefill=True: row m = position *pos + m
+        of sequence *seq; `final` adds the lm_head and the pick of the next
+        token, else the chunk ends by advancing the position)."""
+        sp, H, hd, rows = self.spec, self.spec.hidden, self.spec.head_dim, bufs.rows
         tp = self.tp_size > 1
         ex = self.exchange
+        seq = self.seq.data_ptr() if prefill else None
         calls = []
-        xs = [self.x, self.x2]
+        xs = [bufs.x, bufs.x2]
         cur = 0           # index of the buffer holding the residual stream
         pending = None    # exchange whose all-reduced partial waits to be added to the residual
         gemv_args = []
@@ -408,7 +452,7 @@ class DecodeEngine:
         def norm_pro():
             nonlocal cur, pending
             if pending is not None:
-                d = dict(prologue=PRO_RESID_NORM, act=xs[cur], psum=self.psum, x_out=xs[1 - cur], lda=H)
+                d = dict(prologue=PRO_RESID_NORM, act=xs[cur], psum=bufs.psum, x_out=xs[1 - cur], lda=H)
                 if ex is not None:
                     d.update(prologue=PRO_PEER_RESID_NORM, xin=ex.in_ptr(pending))
                 cur = 1 - cur
@@ -422,65 +466,83 @@ class DecodeEngine:
                 return dict(epilogue=EPI_PLAIN, out=xs[cur], residual=xs[cur])
             if ex is not None:
                 return dict(epilogue=EPI_PEER_F32, xout=ex.out_ptr(e))
-            return dict(epilogue=EPI_F32, out_f32=self.psum)
+            return dict(epilogue=EPI_F32, out_f32=bufs.psum)
 
+        if prefill:
+            calls.append(("prefill_embed", bufs, "embed"))
         for li, L in enumerate(self.layers):
             pro = norm_pro()
-            a = self._gemv(bits=sp.bits, epilogue=EPI_ROPE_KV, N=(self.nq + 2 * self.nkv) * hd, K=H,
+            a = self._gemv(rows, bits=sp.bits, epilogue=EPI_ROPE_KV, N=(self.nq + 2 * self.nkv) * hd, K=H,
                            group_size=sp.group_size, weight=L.qkv_w, scales=L.qkv_s, gamma=L.in_norm,
                            head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv, max_seq=self.S,
-                           rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, q_out=self.q,
-                           k_cache=self.k_cache[li], v_cache=self.v_cache[li], **pro)
+                           rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, q_out=bufs.q,
+                           k_cache=self.k_cache[li], v_cache=self.v_cache[li], prefill_seq=seq, **pro)
             calls.append(("gemv", a, "qkv"))
             gemv_args.append(a)
-            at = AttentionArgs(q=self.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
-                               v_cache=self.v_cache[li].data_ptr(), out=self.attn.data_ptr(), pos=self.pos.data_ptr(),
-                               batch=B, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
-                               pdl=self.pdl)
+            at = AttentionArgs(q=bufs.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
+                               v_cache=self.v_cache[li].data_ptr(), out=bufs.attn.data_ptr(), pos=self.pos.data_ptr(),
+                               batch=rows, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
+                               pdl=self.pdl, prefill_seq=seq)
             calls.append(("attn", at, "attn"))
-            a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.nq * hd, group_size=sp.group_size,
-                           weight=L.o_w, scales=L.o_s, act=self.attn, lda=self.nq * hd, ldo=H,
+            a = self._gemv(rows, bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.nq * hd, group_size=sp.group_size,
+                           weight=L.o_w, scales=L.o_s, act=bufs.attn, lda=self.nq * hd, ldo=H,
                            **partial_epi(2 * li))
             calls.append(("gemv", a, "o"))
             gemv_args.append(a)
             if tp:
                 if ex is None:
-                    calls.append(("allreduce", self.psum, "allreduce"))
+                    calls.append(("allreduce", bufs.psum, "allreduce"))
                 pending = 2 * li
             pro = norm_pro()
-            a = self._gemv(bits=sp.bits, epilogue=EPI_SWIGLU, N=2 * self.inter, K=H, group_size=sp.group_size,
-                           weight=L.gu_w, scales=L.gu_s, gamma=L.post_norm, out=self.act, ldo=self.inter, **pro)
+            a = self._gemv(rows, bits=sp.bits, epilogue=EPI_SWIGLU, N=2 * self.inter, K=H, group_size=sp.group_size,
+                           weight=L.gu_w, scales=L.gu_s, gamma=L.post_norm, out=bufs.act, ldo=self.inter, **pro)
             calls.append(("gemv", a, "gu"))
             gemv_args.append(a)
-            a = self._gemv(bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
-                           weight=L.d_w, scales=L.d_s, act=self.act, lda=self.inter, ldo=H,
+            a = self._gemv(rows, bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
+                           weight=L.d_w, scales=L.d_s, act=bufs.act, lda=self.inter, ldo=H,
                            **partial_epi(2 * li + 1))
             calls.append(("gemv", a, "down"))
             gemv_args.append(a)
             if tp:
                 if ex is None:
-                    calls.append(("allreduce", self.psum, "allreduce"))
+                    calls.append(("allreduce", bufs.psum, "allreduce"))
                 pending = 2 * li + 1
+        if not final:
+            # the residual stream of the chunk is not needed further: only the KV cache
+            calls.append(("prefill_advance", rows, "advance"))
+            return calls, gemv_args
         pro = norm_pro()
-        head = dict(epilogue=EPI_ARGMAX, argmax_keys=self.keys)
+        head = dict(epilogue=EPI_ARGMAX, argmax_keys=bufs.keys)
         if ex is not None:
             head.update(epilogue=EPI_PEER_ARGMAX, xout=ex.out_ptr(2 * len(self.layers)))
-        a = self._gemv(bits=16, N=self.vshard, K=H, group_size=H, weight=self.lm_head, gamma=self.final_norm,
-                       out=self.logits, ldo=self.vshard, argmax_offset=self.tp_rank * self.vshard, **head, **pro)
+        a = self._gemv(rows, bits=16, N=self.vshard, K=H, group_size=H, weight=self.lm_head, gamma=self.final_norm,
+                       out=bufs.logits, ldo=self.vshard, argmax_offset=self.tp_rank * self.vshard, **head, **pro)
         calls.append(("gemv", a, "lm_head"))
         gemv_args.append(a)
         if tp and ex is None:
-            calls.append(("allreduce_max", self.keys, "allreduce"))
-        calls.append(("sample", None, "sample"))
-        # one workspace shared by the sequential GEMVs of a step
+            calls.append(("allreduce_max", bufs.keys, "allreduce"))
+        calls.append(("prefill_sample" if prefill else "sample", bufs, "sample"))
+        return calls, gemv_args
+
+    def _attach_workspace(self, gemv_args):
+        """One workspace shared by the sequential GEMVs of every call list."""
         need = max(int(nat.lib().lw_fused_gemv_workspace_size(ctypes.byref(a))) for a in gemv_args)
-        self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        if getattr(self, "workspace", None) is None or self.workspace.numel() < need:
+            self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+            for a in getattr(self, "_all_gemv_args", []):
+                a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        self._all_gemv_args = getattr(self, "_all_gemv_args", []) + list(gemv_args)
         for a in gemv_args:
             a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
-        self.calls = calls
+
+    def _build_calls(self):
+        self.workspace = None
+        self.calls, gemv_args = self._make_calls(self.dec, prefill=False)
+        self._attach_workspace(gemv_args)
         self.stat_args = {id(a): self._stat_variant(a) for a in gemv_args}
         self.x_in = self.x   # layer 0 reads the residual stream from self.x; sample writes it there
-        self.sample_xin = ex.in_ptr(2 * len(self.layers)) if ex is not None else None
+        self.sample_xin = self.exchange.in_ptr(2 * len(self.layers)) if self.exchange is not None else None
+        self.prefill_calls = {}
 
     def _stat_variant(self, a: FusedGemvArgs) -> FusedGemvArgs:
         """The same GEMV with its exchange replaced by local buffers, for timing
@@ -498,9 +560,12 @@ class DecodeEngine:
 
     # -------------------------------------------------------------- execution
     def _enqueue_step(self, sample: bool = True):
+        self._enqueue(self.calls, sample)
+
+    def _enqueue(self, calls, sample: bool = True):
         lib = nat.lib()
         s = torch.cuda.current_stream(self.device).cuda_stream
-        for kind, a, _name in self.calls:
+        for kind, a, _name in calls:
             if kind == "sample" and not sample:
                 continue
             if kind == "gemv":
@@ -513,6 +578,18 @@ class DecodeEngine:
                 torch.distributed.all_reduce(a, op=torch.distributed.ReduceOp.MAX, group=self.tp_group)
             elif kind == "sample":
                 self._sample(s)
+            elif kind == "prefill_embed":
+                nat.check("lw_prefill_embed", lib.lw_prefill_embed(
+                    self.tokens.data_ptr(), self.embed.data_ptr(), a.x.data_ptr(), self.pos.data_ptr(),
+                    self.seq.data_ptr(), a.rows, self.B, self.spec.hidden, self.pdl, s))
+            elif kind == "prefill_advance":
+                nat.check("lw_prefill_advance", lib.lw_prefill_advance(
+                    self.pos.data_ptr(), self.step_count.data_ptr(), a, self.pdl, s))
+            elif kind == "prefill_sample":
+                nat.check("lw_prefill_sample", lib.lw_prefill_sample(
+                    self.tokens.data_ptr(), a.keys.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
+                    self.pos.data_ptr(), self.step_count.data_ptr(), self.seq.data_ptr(), self.sample_xin, a.rows,
+                    self.B, self.spec.hidden, self.pdl, s))
 
     def _sample(self, s):
         nat.check("lw_sample_tokens", nat.lib().lw_sample_tokens(
@@ -538,14 +615,71 @@ class DecodeEngine:
 
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
         """Greedy continuation of input_ids [B, P] (host or device); returns the
-        new tokens [B, max_new_tokens] on the host. One graph replay per step,
-        one device->host copy at the end."""
+        new tokens [B, max_new_tokens] on the host. The prompt runs in chunks
+        (prefill), then one graph replay per new token, one device->host copy
+        at the end."""
         self.start(input_ids)
+        self.prefill()
         self.capture()
-        self.step(input_ids.shape[1] + max_new_tokens - 1)
+        self.step(max_new_tokens - 1)
         out = self.generated(max_new_tokens).to("cpu")
         self.check()
         return out
+
+    # -------------------------------------------------------------- prefill
+    def _prefill_calls(self, rows: int, final: bool):
+        key = (rows, final)
+        if key not in self.prefill_calls:
+            bufs = self.pf if rows == self.pf.rows else self._buffers(rows)
+            calls, gemv_args = self._make_calls(bufs, prefill=True, final=final)
+            self._attach_workspace(gemv_args)
+            self.prefill_calls[key] = calls
+        return self.prefill_calls[key]
+
+    def _capture_graph(self, calls):
+        """CUDA graph of a call list, after one eager run whose effects on the
+        decode state (tokens, position, residual stream, keys) are undone; the
+        exchange step count is not, so every rank stays in step."""
+        saved = (self.tokens.clone(), self.pos.clone(), self.x_in.clone(), self.keys.clone())
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._enqueue(calls)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            self._enqueue(calls)
+        torch.cuda.synchronize(self.device)
+        self.tokens.copy_(saved[0])
+        self.pos.copy_(saved[1])
+        self.x_in.copy_(saved[2])
+        self.keys.copy_(saved[3])
+        return g
+
+    def _prefill_graph(self, rows: int, final: bool):
+        key = (rows, final)
+        if key not in self.prefill_graphs:
+            self.prefill_graphs[key] = self._capture_graph(self._prefill_calls(rows, final))
+        return self.prefill_graphs[key]
+
+    def prefill(self, graph: bool = True):
+        """Run every sequence's prompt (loaded by start()) through the model in
+        chunks of up to prefill_rows positions: the KV cache holds positions
+        0..P-1, the first new token of each sequence is picked and embedded,
+        and the position is P. One chunk reads every weight once."""
+        P, R = self.prompt_len, self.prefill_rows
+        n = (P + R - 1) // R
+        last = P - (n - 1) * R
+        plan = [(R, False)] * (n - 1) + [(last, True)]
+        for b in range(self.B):
+            self.seq.fill_(b)
+            self.pos.zero_()
+            for rows, final in plan:
+                if graph:
+                    self._prefill_graph(rows, final).replay()
+                else:
+                    self._enqueue(self._prefill_calls(rows, final))
+        self.host_pos = P
 
     def check(self) -> None:
         """Raise if a tensor-parallel exchange wait gave up (reads a device flag: syncs)."""
@@ -556,6 +690,7 @@ class DecodeEngine:
         """Release the graph and, with a peer exchange, the shared block
         (collective over the tensor-parallel group)."""
         self.graph = None
+        self.prefill_graphs = {}
         if self.exchange is not None:
             self.exchange.close()
 
@@ -577,23 +712,8 @@ class DecodeEngine:
 
     def capture(self):
         """Capture one decode step as a CUDA graph (after one eager step to warm up)."""
-        if self.graph is not None:
-            return
-        saved = (self.tokens.clone(), self.pos.clone(), self.x_in.clone(), self.keys.clone())
-        side = torch.cuda.Stream(self.device)
-        side.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(side):
-            self._enqueue_step()
-        torch.cuda.synchronize(self.device)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=side):
-            self._enqueue_step()
-        torch.cuda.synchronize(self.device)
-        self.tokens.copy_(saved[0])
-        self.pos.copy_(saved[1])
-        self.x_in.copy_(saved[2])
-        self.keys.copy_(saved[3])
-        self.graph = g
+        if self.graph is None:
+            self.graph = self._capture_graph(self.calls)
 
     def step(self, n: int = 1, graph: bool = True):
         for _ in range(n):

@@ -13,7 +13,7 @@ from liteweight_b200 import build as lwbuild
 def test_struct_layout_matches_library():
     lwbuild.build()
     E.check_abi()
-    assert ctypes.sizeof(E.FusedGemvArgs) == 240 and ctypes.sizeof(E.AttentionArgs) == 64
+    assert ctypes.sizeof(E.FusedGemvArgs) == 248 and ctypes.sizeof(E.AttentionArgs) == 72
     assert ctypes.sizeof(E.ExchangeOut) == 96 and ctypes.sizeof(E.ExchangeIn) == 48
 
 
@@ -87,3 +87,11 @@ def test_exchange_flags():
     seen = {E.exchange_flag(s, t, tags) for s in range(3) for t in range(tags)}
     assert len(seen) == 3 * tags and 0 not in seen
     assert E.exchange_flag(0xFFFFFFFF // tags, tags - 1, tags) != 0
+
+
+def test_prefill_rows_fit_shared_memory():
+    """Prompt-chunk rows: the most every GEMV of a layer can stage (8B INT4
+    down_proj K=14336 -> 7 rows at TP1; the norm GEMVs with K=4096 -> 26)."""
+    s8 = E.LlamaSpec(**E.LLAMA_3_8B, bits=4)
+    assert [E.prefill_rows(s8, tp) for tp in (1, 2, 4, 8)] == [7, 15, 26, 26]
+    assert E.prefill_rows(E.LlamaSpec(**E.LLAMA_3_2_1B, bits=8)) == 13

@@ -67,8 +67,8 @@ def _exchanges(ranks, timeout_s=5.0):
         for e in range(TAGS):
             o = E.ExchangeOut(world=world, rank=r, step=R.step.data_ptr(), tag=e, tags_per_step=TAGS,
                               arrivals=R.arrivals.data_ptr())
-            for d, D in enumerate(ranks):
-                o.dst[d] = D.keys_in[r].data_ptr() if e == 2 else D.slots[e % 2, r].data_ptr()
+            for d, D in enumerate(ranks):   # receive buffers; the kernel adds rank * M (* ldo)
+                o.dst[d] = D.keys_in.data_ptr() if e == 2 else D.slots[e % 2].data_ptr()
             o_r.append(o)
             src = R.keys_in.data_ptr() if e == 2 else R.slots[e % 2].data_ptr()
             i_r.append(E.ExchangeIn(world=world, tag=e, tags_per_step=TAGS, src=src, step=R.step.data_ptr(),
