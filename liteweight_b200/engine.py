@@ -242,20 +242,31 @@ def default_inv_freq(head_dim: int, theta: float) -> torch.Tensor:
 
 # ------------------------------------------------------------------ engine
 
+def _stage_rows(K: int, bits: int, norm: bool) -> int:
+    """Activation rows one fused GEMV launch can stage in shared memory (rows x
+    K padded to whole chunks, fp16, plus the RMSNorm weight for the norm
+    prologues, within the 220 KiB the kernels budget)."""
+    kc = {4: 128, 8: 64, 16: 32}[bits]
+    kpad = -(-K // kc) * kc
+    return (220 * 1024 - (((K + 7) // 8) * 16 if norm else 0)) // (2 * kpad)
+
+
+def down_rows(spec: LlamaSpec, tp_size: int = 1) -> int:
+    """Rows one down_proj launch can stage (its K, the intermediate size, is the largest)."""
+    return max(1, _stage_rows(spec.inter // tp_size, spec.bits, False))
+
+
 def prefill_rows(spec: LlamaSpec, tp_size: int = 1, limit: int = 32) -> int:
-    """Positions per prompt chunk: the most rows every GEMV of the layer can
-    stage in shared memory (rows x K padded to whole chunks, fp16, plus the
-    RMSNorm weight for the norm prologues, within 220 KiB), at most `limit`."""
-    budget = 220 * 1024
-
-    def rows_for(K, bits, norm):
-        kc = {4: 128, 8: 64, 16: 32}[bits]
-        kpad = -(-K // kc) * kc
-        return (budget - (((K + 7) // 8) * 16 if norm else 0)) // (2 * kpad)
-
+    """Positions per prompt chunk: the most rows the q|k|v, o, gate|up and
+    lm_head launches can stage, at most `limit`. With one rank the down_proj
+    runs in row blocks of down_rows() (its weights are re-read per block); with
+    tensor parallelism the chunk also fits the down_proj, whose partial sums go
+    to the other ranks in one exchange per chunk."""
     H, hd = spec.hidden, spec.head_dim
-    rows = min(rows_for(H, spec.bits, True), rows_for(spec.n_heads // tp_size * hd, spec.bits, False),
-               rows_for(spec.inter // tp_size, spec.bits, False), rows_for(H, 16, True))
+    rows = min(_stage_rows(H, spec.bits, True), _stage_rows(spec.n_heads // tp_size * hd, spec.bits, False),
+               _stage_rows(H, 16, True))
+    if tp_size > 1:
+        rows = min(rows, down_rows(spec, tp_size))
     return max(1, min(limit, rows))
 
 
@@ -284,6 +295,7 @@ class PeerExchange:
         assert 1 <= world <= MAX_RANKS
         self.rank, self.world, self.group, self.device = rank, world, group, torch.device(device)
         self.n_partial = n_partial
+        self.rows = batch
         self.tags = n_partial + 1
         self.slot_off = _align(8 * world * batch, 256)
         self.set_bytes = _align(8 * world * batch * hidden, 256)
@@ -498,11 +510,17 @@ class DecodeEngine:
                            weight=L.gu_w, scales=L.gu_s, gamma=L.post_norm, out=bufs.act, ldo=self.inter, **pro)
             calls.append(("gemv", a, "gu"))
             gemv_args.append(a)
-            a = self._gemv(rows, bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
-                           weight=L.d_w, scales=L.d_s, act=bufs.act, lda=self.inter, ldo=H,
-                           **partial_epi(2 * li + 1))
-            calls.append(("gemv", a, "down"))
-            gemv_args.append(a)
+            blk = rows if tp else min(rows, down_rows(sp, 1))
+            for r0 in range(0, rows, blk):   # row blocks when the chunk exceeds what the down_proj can stage
+                nr = min(blk, rows - r0)
+                epi = partial_epi(2 * li + 1)
+                if not tp:
+                    epi.update(out=xs[cur].data_ptr() + 2 * r0 * H, residual=xs[cur].data_ptr() + 2 * r0 * H)
+                a = self._gemv(nr, bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
+                               weight=L.d_w, scales=L.d_s, act=bufs.act.data_ptr() + 2 * r0 * self.inter,
+                               lda=self.inter, ldo=H, **epi)
+                calls.append(("gemv", a, "down"))
+                gemv_args.append(a)
             if tp:
                 if ex is None:
                     calls.append(("allreduce", bufs.psum, "allreduce"))
@@ -629,6 +647,8 @@ class DecodeEngine:
     # -------------------------------------------------------------- prefill
     def _prefill_calls(self, rows: int, final: bool):
         key = (rows, final)
+        if self.exchange is not None:
+            assert rows <= self.exchange.rows, "prompt chunk larger than the exchange buffers"
         if key not in self.prefill_calls:
             bufs = self.pf if rows == self.pf.rows else self._buffers(rows)
             calls, gemv_args = self._make_calls(bufs, prefill=True, final=final)

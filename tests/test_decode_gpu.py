@@ -197,13 +197,17 @@ def test_generate_api_matches_hf_loop(bits):
     assert len(sampled.split()) == 6
 
 
-@pytest.mark.parametrize("bits,batch,P", [(4, 1, 20), (8, 2, 9), (4, 3, 1)])
-def test_chunked_prefill_matches_token_by_token(bits, batch, P):
+@pytest.mark.parametrize("bits,batch,P,down_block", [(4, 1, 20, 3), (8, 2, 9, 0), (4, 3, 1, 0)])
+def test_chunked_prefill_matches_token_by_token(bits, batch, P, down_block, monkeypatch):
     """generate() runs the prompt in chunks of prefill_rows positions (here
-    forced small so a prompt spans several chunks and a ragged last one): the
-    KV cache, the generated tokens and the decode logits equal those of the
-    token-by-token path, bit for bit (each row of a chunk runs the same
-    arithmetic as a decode step), and match the oracle."""
+    forced small so a prompt spans several chunks and a ragged last one; with
+    down_block the down_proj runs in row blocks inside a chunk): the KV cache
+    and the generated tokens equal those of the token-by-token path, bit for
+    bit (each row of a chunk runs the same arithmetic as a decode step), and
+    the oracle agrees with the picks."""
+    from liteweight_b200 import engine as E
+    if down_block:
+        monkeypatch.setattr(E, "down_rows", lambda spec, tp_size=1: down_block)
     w = random_model(512, 1024, 2, 8, 2, 64, 1000, bits, seed=7 + bits + batch)
     T = 6
     prompt = np.random.default_rng(P).integers(0, 1000, (batch, P))

@@ -90,8 +90,11 @@ def test_exchange_flags():
 
 
 def test_prefill_rows_fit_shared_memory():
-    """Prompt-chunk rows: the most every GEMV of a layer can stage (8B INT4
-    down_proj K=14336 -> 7 rows at TP1; the norm GEMVs with K=4096 -> 26)."""
+    """Prompt-chunk rows: the most the norm GEMVs (K=4096 -> 26) stage; the
+    down_proj (8B INT4 K=14336 -> 7 rows) runs in row blocks at TP1 and bounds
+    the chunk under tensor parallelism (K=7168 at TP2 -> 15)."""
     s8 = E.LlamaSpec(**E.LLAMA_3_8B, bits=4)
-    assert [E.prefill_rows(s8, tp) for tp in (1, 2, 4, 8)] == [7, 15, 26, 26]
-    assert E.prefill_rows(E.LlamaSpec(**E.LLAMA_3_2_1B, bits=8)) == 13
+    assert [E.prefill_rows(s8, tp) for tp in (1, 2, 4, 8)] == [26, 15, 26, 26]
+    assert [E.down_rows(s8, tp) for tp in (1, 2, 4)] == [7, 15, 31]
+    s1 = E.LlamaSpec(**E.LLAMA_3_2_1B, bits=8)
+    assert E.prefill_rows(s1) == 32 and E.down_rows(s1) == 13

@@ -224,8 +224,12 @@ def _nccl_worker(rank, world, port, out_path, exchange):
     gen = gen_t.cpu().numpy()
     gens = [torch.empty_like(gen_t) for _ in range(world)]
     dist.all_gather(gens, gen_t)
+    # generate(): the prompt in chunks through the same exchanges, then decode steps
+    eng.prefill_rows = 4
+    eng.pf = eng._buffers(4)
+    chunked = eng.generate(torch.from_numpy(prompt), T).numpy()
     if rank == 0:
-        np.savez(out_path, logits=np.stack(shards), tokens=gen, prompt=prompt,
+        np.savez(out_path, logits=np.stack(shards), tokens=gen, prompt=prompt, chunked=chunked,
                  same=all(bool(torch.equal(g, gens[0])) for g in gens))
     eng.close()                  # collective; releases the graph (NCCL calls in the "nccl" mode)
     del eng
@@ -255,6 +259,7 @@ def test_tp_decode_matches_oracle(world):
     peer, nccl = _run_tp("peer", world), _run_tp("nccl", world)
     for r in (peer, nccl):
         assert bool(r["same"]), "ranks picked different tokens"
+        assert np.array_equal(r["chunked"], r["tokens"]), "chunked prefill diverged from step-by-step"
     if world == 2:
         assert np.array_equal(peer["logits"], nccl["logits"])
         assert np.array_equal(peer["tokens"], nccl["tokens"])
