@@ -259,7 +259,8 @@ int lw_attention_decode(const lw_attention_args* args, lw_stream_t stream);
 
 /* sizeof(lw_fused_gemv_args) for which = 0, sizeof(lw_attention_args) for
  * which = 1, sizeof(lw_exchange_out) for 2, sizeof(lw_exchange_in) for 3,
- * else 0: lets a binding check its struct layouts at load time. */
+ * sizeof(lw_prefill_gemm_args) for 4, else 0: lets a binding check its
+ * struct layouts at load time. */
 size_t lw_struct_size(int which);
 
 /* x[b] = embed[tokens[*pos][b]] (tokens int32 [max_seq+1][batch]). */
@@ -301,6 +302,46 @@ int lw_prefill_advance(int* pos, int* step, int rows, int pdl, lw_stream_t strea
 int lw_prefill_sample(int* tokens, unsigned long long* keys, const void* embed, void* x_out, int* pos, int* step,
                       const int* seq, const lw_exchange_in* xin, int rows, int batch, int hidden, int pdl,
                       lw_stream_t stream);
+
+/* ---- prompt-chunk GEMM on the 5th-generation tensor cores ----------------
+ * out[m][n] for the M rows of a prompt chunk (M <= 256) and N weight rows
+ * (a multiple of 128): D = act[M][K] . dequant(W)[N][K]^T, fp32 sums in
+ * tensor memory (tcgen05.mma kind::f16, 128-row weight tiles, K in blocks of
+ * 64 through a 4-stage shared-memory pipeline), then one epilogue:
+ *   LW_TC_EPI_RESID:  out = fp16(fp16(y) + residual)   (residual may alias out)
+ *   LW_TC_EPI_SWIGLU: gate|up rows interleaved by 8, out[m][i] = silu(gate) * up
+ *   LW_TC_EPI_ROPE_KV: q|k|v rows in rope-pair order; RoPE q, k at position
+ *                      *pos + m; q -> q_out, k, v -> the cache of sequence *seq
+ * Weights dequantize exactly (fp16(code * scale)) as the GEMV does; the sums
+ * differ from it only in order. K a multiple of 64, INT4 or INT8, group size a
+ * power of two >= 32 dividing K. No counterpart in the reference (its prompt
+ * runs through one HF forward over QuantLinear's dequantize + matmul). */
+enum { LW_TC_EPI_RESID = 0, LW_TC_EPI_SWIGLU = 1, LW_TC_EPI_ROPE_KV = 2 };
+
+typedef struct {
+  int bits, epilogue, pdl;
+  int M, N, K, group_size;
+  int lda, ldo;
+  const void* act;       /* fp16 [M][lda] */
+  const void* weight;    /* [N][K * bits / 8] */
+  const void* scales;    /* fp16 [N][K / group_size] */
+  void* out;             /* fp16 [M][ldo] */
+  const void* residual;  /* fp16 [M][ldo] (LW_TC_EPI_RESID; may be NULL) */
+  int head_dim, n_q_heads, n_kv_heads, max_seq;
+  const void* rope_cos;  /* fp16 [max_seq][head_dim] */
+  const void* rope_sin;
+  const int* pos;
+  const int* seq;
+  void* q_out;           /* fp16 [M][n_q_heads * head_dim] */
+  void* k_cache;         /* fp16 [batch][n_kv_heads][max_seq][head_dim] */
+  void* v_cache;
+} lw_prefill_gemm_args;
+
+int lw_prefill_gemm(const lw_prefill_gemm_args* args, lw_stream_t stream);
+
+/* h[m] = RMSNorm(x[m]) * gamma for m < M (modeling_llama.py:63-68 rounding points). */
+int lw_rmsnorm_rows(const void* x, const void* gamma, void* h, int M, int K, float eps, int pdl,
+                    lw_stream_t stream);
 
 /* ---- peer memory for the exchanges (setup calls: these allocate, map and
  * synchronise; they are not stream-ordered and must not be graph-captured) */

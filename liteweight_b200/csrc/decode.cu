@@ -571,6 +571,7 @@ size_t lw_struct_size(int which) {
   if (which == 1) return sizeof(lw_attention_args);
   if (which == 2) return sizeof(lw_exchange_out);
   if (which == 3) return sizeof(lw_exchange_in);
+  if (which == 4) return sizeof(lw_prefill_gemm_args);
   return 0;
 }
 

@@ -325,6 +325,7 @@ cudaError_t launch_kn(GemvParams p, cudaStream_t s) {
 // Device error flags of the other translation units that launch kernels.
 int lw_decode_take_error();
 int lw_decode_tp_take_error();
+int lw_gemm_tc_take_error();
 
 extern "C" {
 
@@ -349,7 +350,8 @@ int lw_take_device_error(void) {
   const int mine = lw_tu_take_error();
   const int dec = lw_decode_take_error();
   const int tp = lw_decode_tp_take_error();
-  return mine ? mine : (dec ? dec : tp);
+  const int tc = lw_gemm_tc_take_error();
+  return mine ? mine : (dec ? dec : (tp ? tp : tc));
 }
 
 unsigned long long lw_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }

@@ -78,6 +78,22 @@ class FusedGemvArgs(ctypes.Structure):
     ]
 
 
+class PrefillGemmArgs(ctypes.Structure):
+    """Mirror of lw_prefill_gemm_args (include/liteweight_b200.h)."""
+    _fields_ = [
+        ("bits", c_int), ("epilogue", c_int), ("pdl", c_int), ("M", c_int), ("N", c_int), ("K", c_int),
+        ("group_size", c_int), ("lda", c_int), ("ldo", c_int),
+        ("act", c_void_p), ("weight", c_void_p), ("scales", c_void_p), ("out", c_void_p), ("residual", c_void_p),
+        ("head_dim", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("max_seq", c_int),
+        ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("pos", c_void_p), ("seq", c_void_p),
+        ("q_out", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
+    ]
+
+
+TC_EPI_RESID, TC_EPI_SWIGLU, TC_EPI_ROPE_KV = 0, 1, 2
+TC_ROWS = 128   # prompt-chunk rows on the tensor-core path
+
+
 class AttentionArgs(ctypes.Structure):
     """Mirror of lw_attention_args (include/liteweight_b200.h)."""
     _fields_ = [
@@ -96,6 +112,8 @@ nat.register("lw_struct_size", [c_int], c_size_t)
 nat.register("lw_prefill_embed", [c_void_p] * 5 + [c_int] * 4 + [c_void_p])
 nat.register("lw_prefill_advance", [c_void_p] * 2 + [c_int] * 2 + [c_void_p])
 nat.register("lw_prefill_sample", [c_void_p] * 8 + [c_int] * 4 + [c_void_p])
+nat.register("lw_prefill_gemm", [ctypes.POINTER(PrefillGemmArgs), c_void_p])
+nat.register("lw_rmsnorm_rows", [c_void_p] * 3 + [c_int] * 2 + [c_float, c_int, c_void_p])
 nat.register("lw_peer_alloc", [c_size_t, ctypes.POINTER(c_void_p)])
 nat.register("lw_peer_free", [c_void_p])
 nat.register("lw_peer_handle_size", [], c_size_t)
@@ -107,7 +125,8 @@ nat.register("lw_peer_close", [c_void_p])
 def check_abi() -> None:
     """The ctypes mirrors must have the library's struct sizes."""
     lib = nat.lib()
-    for which, cls in ((0, FusedGemvArgs), (1, AttentionArgs), (2, ExchangeOut), (3, ExchangeIn)):
+    for which, cls in ((0, FusedGemvArgs), (1, AttentionArgs), (2, ExchangeOut), (3, ExchangeIn),
+                       (4, PrefillGemmArgs)):
         got = int(lib.lw_struct_size(which))
         if got != ctypes.sizeof(cls):
             raise RuntimeError(f"{cls.__name__}: ctypes size {ctypes.sizeof(cls)} != library size {got}")
@@ -270,6 +289,16 @@ def prefill_rows(spec: LlamaSpec, tp_size: int = 1, limit: int = 32) -> int:
     return max(1, min(limit, rows))
 
 
+def tc_supported(spec: LlamaSpec) -> bool:
+    """The tensor-core prompt GEMM takes every linear of the layer: weight rows
+    in whole 128-row tiles, K in whole 64-element blocks."""
+    hd = spec.head_dim
+    ns = [(spec.n_heads + 2 * spec.n_kv_heads) * hd, spec.hidden, 2 * spec.inter]
+    ks = [spec.hidden, spec.n_heads * hd, spec.inter]
+    return (spec.bits in (4, 8) and spec.group_size >= 32 and all(n % 128 == 0 for n in ns)
+            and all(k % 64 == 0 for k in ks))
+
+
 def _align(v: int, a: int) -> int:
     return (v + a - 1) // a * a
 
@@ -403,8 +432,11 @@ class DecodeEngine:
         self.seq = torch.zeros(1, dtype=torch.int32, device=dev)   # sequence of the prompt chunk in flight
         self.tokens = torch.full((max_seq + 1, batch), -1, dtype=torch.int32, device=dev)
         self.step_count = torch.zeros(1, dtype=torch.int32, device=dev)
-        # decode buffers (row = sequence) and prompt-chunk buffers (row = position)
-        self.prefill_rows = prefill_rows(spec, tp_size)
+        # decode buffers (row = sequence) and prompt-chunk buffers (row = position). With one
+        # rank, prompt chunks of TC_ROWS positions run their linears on the tensor cores
+        # (lw_prefill_gemm); with tensor parallelism they run the fused GEMVs and exchanges.
+        self.use_tc = tp_size == 1 and tc_supported(spec)
+        self.prefill_rows = TC_ROWS if self.use_tc else prefill_rows(spec, tp_size)
         self.dec = self._buffers(batch)
         self.pf = self._buffers(self.prefill_rows)
         self.x, self.x2, self.q, self.attn = self.dec.x, self.dec.x2, self.dec.q, self.dec.attn
@@ -436,6 +468,7 @@ class DecodeEngine:
         b.logits = torch.zeros(rows, self.vshard, **f16)
         b.psum = torch.zeros(rows, H, dtype=torch.float32, device=dev)
         b.keys = torch.zeros(rows, dtype=torch.int64, device=dev)
+        b.h = torch.zeros(rows, H, **f16)   # RMSNorm output (tensor-core prompt chunks)
         return b
 
     # -------------------------------------------------------------- call table
@@ -542,9 +575,55 @@ class DecodeEngine:
         calls.append(("prefill_sample" if prefill else "sample", bufs, "sample"))
         return calls, gemv_args
 
+    def _make_tc_calls(self, bufs, final: bool):
+        """A prompt chunk on the tensor cores (one rank): per layer RMSNorm rows,
+        the q|k|v GEMM (RoPE + KV append), attention, the o GEMM (+ residual,
+        in place), RMSNorm, the gate|up GEMM (SwiGLU), the down GEMM (+ residual);
+        the last chunk then runs the lm_head GEMV on its last row only."""
+        sp, H, hd, rows = self.spec, self.spec.hidden, self.spec.head_dim, bufs.rows
+        seq = self.seq.data_ptr()
+        calls = [("prefill_embed", bufs, "embed")]
+
+        def tc(epi, N, K, w, s_, act, lda, out, ldo, **kw):
+            a = PrefillGemmArgs(bits=sp.bits, epilogue=epi, pdl=self.pdl, M=rows, N=N, K=K,
+                                group_size=sp.group_size, lda=lda, ldo=ldo, act=act.data_ptr(), weight=w.data_ptr(),
+                                scales=s_.data_ptr(), out=out.data_ptr() if out is not None else None)
+            for k, v in kw.items():
+                setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
+            return ("tcgemm", a, "tc")
+
+        for li, L in enumerate(self.layers):
+            calls.append(("rmsnorm", (bufs.x, L.in_norm, bufs.h, rows), "norm"))
+            calls.append(tc(TC_EPI_ROPE_KV, (self.nq + 2 * self.nkv) * hd, H, L.qkv_w, L.qkv_s, bufs.h, H, bufs.q,
+                            self.nq * hd, head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv, max_seq=self.S,
+                            rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, seq=seq, q_out=bufs.q,
+                            k_cache=self.k_cache[li], v_cache=self.v_cache[li]))
+            at = AttentionArgs(q=bufs.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
+                               v_cache=self.v_cache[li].data_ptr(), out=bufs.attn.data_ptr(), pos=self.pos.data_ptr(),
+                               batch=rows, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
+                               pdl=self.pdl, prefill_seq=seq)
+            calls.append(("attn", at, "attn"))
+            calls.append(tc(TC_EPI_RESID, H, self.nq * hd, L.o_w, L.o_s, bufs.attn, self.nq * hd, bufs.x, H,
+                            residual=bufs.x))
+            calls.append(("rmsnorm", (bufs.x, L.post_norm, bufs.h, rows), "norm"))
+            calls.append(tc(TC_EPI_SWIGLU, 2 * self.inter, H, L.gu_w, L.gu_s, bufs.h, H, bufs.act, self.inter))
+            calls.append(tc(TC_EPI_RESID, H, self.inter, L.d_w, L.d_s, bufs.act, self.inter, bufs.x, H,
+                            residual=bufs.x))
+        if not final:
+            calls.append(("prefill_advance", rows, "advance"))
+            return calls, []
+        last = bufs.x.data_ptr() + 2 * (rows - 1) * H
+        a = self._gemv(1, bits=16, prologue=PRO_NORM, epilogue=EPI_ARGMAX, N=self.vshard, K=H, group_size=H,
+                       weight=self.lm_head, gamma=self.final_norm, act=last, lda=H,
+                       out=bufs.logits.data_ptr() + 2 * (rows - 1) * self.vshard, ldo=self.vshard,
+                       argmax_keys=bufs.keys.data_ptr() + 8 * (rows - 1), argmax_offset=0)
+        calls.append(("gemv", a, "lm_head"))
+        calls.append(("prefill_sample", bufs, "sample"))
+        return calls, [a]
+
     def _attach_workspace(self, gemv_args):
         """One workspace shared by the sequential GEMVs of every call list."""
-        need = max(int(nat.lib().lw_fused_gemv_workspace_size(ctypes.byref(a))) for a in gemv_args)
+        need = max([int(nat.lib().lw_fused_gemv_workspace_size(ctypes.byref(a))) for a in gemv_args] + [256])
         if getattr(self, "workspace", None) is None or self.workspace.numel() < need:
             self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
             for a in getattr(self, "_all_gemv_args", []):
@@ -596,6 +675,12 @@ class DecodeEngine:
                 torch.distributed.all_reduce(a, op=torch.distributed.ReduceOp.MAX, group=self.tp_group)
             elif kind == "sample":
                 self._sample(s)
+            elif kind == "tcgemm":
+                nat.check("lw_prefill_gemm", lib.lw_prefill_gemm(ctypes.byref(a), s))
+            elif kind == "rmsnorm":
+                x, gamma, h, rows = a
+                nat.check("lw_rmsnorm_rows", lib.lw_rmsnorm_rows(x.data_ptr(), gamma.data_ptr(), h.data_ptr(), rows,
+                                                                 self.spec.hidden, self.spec.eps, self.pdl, s))
             elif kind == "prefill_embed":
                 nat.check("lw_prefill_embed", lib.lw_prefill_embed(
                     self.tokens.data_ptr(), self.embed.data_ptr(), a.x.data_ptr(), self.pos.data_ptr(),
@@ -651,7 +736,10 @@ class DecodeEngine:
             assert rows <= self.exchange.rows, "prompt chunk larger than the exchange buffers"
         if key not in self.prefill_calls:
             bufs = self.pf if rows == self.pf.rows else self._buffers(rows)
-            calls, gemv_args = self._make_calls(bufs, prefill=True, final=final)
+            if self.use_tc:
+                calls, gemv_args = self._make_tc_calls(bufs, final)
+            else:
+                calls, gemv_args = self._make_calls(bufs, prefill=True, final=final)
             self._attach_workspace(gemv_args)
             self.prefill_calls[key] = calls
         return self.prefill_calls[key]

@@ -197,14 +197,15 @@ def test_generate_api_matches_hf_loop(bits):
     assert len(sampled.split()) == 6
 
 
+@pytest.mark.parametrize("path", ["gemv", "tc"])
 @pytest.mark.parametrize("bits,batch,P,down_block", [(4, 1, 20, 3), (8, 2, 9, 0), (4, 3, 1, 0)])
-def test_chunked_prefill_matches_token_by_token(bits, batch, P, down_block, monkeypatch):
-    """generate() runs the prompt in chunks of prefill_rows positions (here
-    forced small so a prompt spans several chunks and a ragged last one; with
-    down_block the down_proj runs in row blocks inside a chunk): the KV cache
-    and the generated tokens equal those of the token-by-token path, bit for
-    bit (each row of a chunk runs the same arithmetic as a decode step), and
-    the oracle agrees with the picks."""
+def test_chunked_prefill(bits, batch, P, down_block, path, monkeypatch):
+    """generate() runs the prompt in chunks (here 4 positions, so a prompt
+    spans several chunks and a ragged last one). On the fused-GEMV path (with
+    down_block, the down_proj in row blocks) the KV cache and the generated
+    tokens equal those of the token-by-token path bit for bit; on the
+    tensor-core path (lw_prefill_gemm) the sums run in another order, so the
+    KV cache matches within the row tolerance and the picks match the oracle."""
     from liteweight_b200 import engine as E
     if down_block:
         monkeypatch.setattr(E, "down_rows", lambda spec, tp_size=1: down_block)
@@ -215,12 +216,19 @@ def test_chunked_prefill_matches_token_by_token(bits, batch, P, down_block, monk
     run_engine(a, prompt, P + T - 1)
     ref_tokens = a.generated(T).cpu().numpy()
     b = engine_from_oracle(w, bits, 128, batch=batch, max_seq=48)
+    assert b.use_tc   # every linear of this model tiles for the tensor-core GEMM
+    b.use_tc = path == "tc"
     b.prefill_rows = 4
     b.pf = b._buffers(4)
     got = b.generate(torch.from_numpy(prompt), T).numpy()
-    assert np.array_equal(got, ref_tokens)
-    for ka, kb in zip(a.k_cache + a.v_cache, b.k_cache + b.v_cache):
-        assert torch.equal(ka[:, :, :P + T - 1], kb[:, :, :P + T - 1])
-    # the first new token came from the last chunk's lm_head; the oracle agrees with every pick
+    if path == "gemv":
+        assert np.array_equal(got, ref_tokens)
+        for ka, kb in zip(a.k_cache + a.v_cache, b.k_cache + b.v_cache):
+            assert torch.equal(ka[:, :, :P + T - 1], kb[:, :, :P + T - 1])
+    else:
+        for ka, kb in zip(a.k_cache + a.v_cache, b.k_cache + b.v_cache):
+            r = ka[:, :, :P].float().reshape(-1, ka.shape[-1]).cpu().numpy()
+            g = kb[:, :, :P].float().reshape(-1, kb.shape[-1]).cpu().numpy()
+            assert np.all(np.abs(g - r) <= oq.row_tolerance(r) + 1e-3)
     oracle = ol.teacher_forced_logits(w, prompt, got)
     assert (oracle.argmax(-1) == got.T).mean() >= 0.9
