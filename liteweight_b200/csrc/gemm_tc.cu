@@ -179,49 +179,77 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcGemmPara
   const unsigned short* ssrc = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)wrow * ngroups;
   bool live = true;
 
-  for (int kb = 0; kb < p.kblocks; ++kb) {
-    const int s = kb % kTcStages, use = kb / kTcStages;
+  // Each thread's global loads of a k-block go to registers one block ahead of
+  // their use (dequantize / store), so the load latency overlaps a block of work.
+  constexpr int kBMax = kTcMaxM * 8 / kTcThreads;   // activation chunks per thread, at most
+  struct Regs {
+    uint4 w0, w1;
+    unsigned short sc;
+    uint4 b[kBMax];
+  };
+  auto load_block = [&](int kb, Regs& r) {
+    const int k0 = kb * kTcKBlock + ah * 32;
+    r.sc = __ldg(ssrc + min(k0 >> p.gshift, ngroups - 1));
+    if constexpr (BITS == 4) {
+      r.w0 = ldg_stream(wsrc + (size_t)k0 / 2);
+    } else {
+      r.w0 = ldg_stream(wsrc + (size_t)k0);
+      r.w1 = ldg_stream(wsrc + (size_t)k0 + 16);
+    }
+#pragma unroll
+    for (int j = 0; j < kBMax; ++j) {
+      const int i = tid + j * kTcThreads;
+      r.b[j] = make_uint4(0, 0, 0, 0);
+      const int m = i >> 3, c = i & 7;   // rows past M stay zero
+      if (i < p.Mpad * 8 && m < p.M) r.b[j] = ldg_nc(p.act + (size_t)m * p.lda + kb * kTcKBlock + c * 8);
+    }
+  };
+  auto store_block = [&](int s, const Regs& r) {
     const uint32_t sa = base + s * stage_bytes, sb = sa + a_bytes;
+    const uint32_t s2 = (uint32_t)r.sc | ((uint32_t)r.sc << 16);
+    if constexpr (BITS == 4) {
+      const uint32_t qw[4] = {r.w0.x, r.w0.y, r.w0.z, r.w0.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sts128(base_ptr + (sa - base) + swz(ar, ah * 4 + j), dequant8<4>(qw[j], 0u, s2));
+    } else {
+      const uint32_t qw[8] = {r.w0.x, r.w0.y, r.w0.z, r.w0.w, r.w1.x, r.w1.y, r.w1.z, r.w1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        sts128(base_ptr + (sa - base) + swz(ar, ah * 4 + j), dequant8<8>(qw[2 * j], qw[2 * j + 1], s2));
+    }
+#pragma unroll
+    for (int j = 0; j < kBMax; ++j) {
+      const int i = tid + j * kTcThreads;
+      if (i < p.Mpad * 8) sts128(base_ptr + (sb - base) + swz(i >> 3, i & 7), r.b[j]);
+    }
+  };
+  auto step = [&](int kb, const Regs& cur) {
+    const int s = kb % kTcStages, use = kb / kTcStages;
     if (use > 0 && live) live = mbar_wait_bounded(smem_u32(&bar_empty[s]), (use - 1) & 1, kTcWaitNs);
-    // A: this thread's 4 chunks of weight row ar
-    {
-      const int k0 = kb * kTcKBlock + ah * 32;
-      const unsigned short sc = __ldg(ssrc + min(k0 >> p.gshift, ngroups - 1));
-      const uint32_t s2 = (uint32_t)sc | ((uint32_t)sc << 16);
-      if constexpr (BITS == 4) {
-        const uint4 q = ldg_stream(wsrc + (size_t)k0 / 2);
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          sts128(base_ptr + (sa - base) + swz(ar, ah * 4 + j), dequant8<4>(qw[j], 0u, s2));
-      } else {
-        const uint4 q0 = ldg_stream(wsrc + (size_t)k0);
-        const uint4 q1 = ldg_stream(wsrc + (size_t)k0 + 16);
-        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          sts128(base_ptr + (sa - base) + swz(ar, ah * 4 + j), dequant8<8>(qw[2 * j], qw[2 * j + 1], s2));
-      }
-    }
-    // B: activation rows (zero past M)
-    for (int i = tid; i < p.Mpad * 8; i += kTcThreads) {
-      const int m = i >> 3, c = i & 7;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (m < p.M) v = ldg_nc(p.act + (size_t)m * p.lda + kb * kTcKBlock + c * 8);
-      sts128(base_ptr + (sb - base) + swz(m, c), v);
-    }
+    store_block(s, cur);
     fence_proxy_async_smem();   // the tensor core reads these through the async proxy
     mbar_arrive(smem_u32(&bar_full[s]));
     if (tid == 0) {
       if (live) live = mbar_wait_bounded(smem_u32(&bar_full[s]), use & 1, kTcWaitNs);
       tc_fence_after();
       if (live) {
+        const uint32_t sa = base + s * stage_bytes, sb = sa + a_bytes;
 #pragma unroll
         for (int j = 0; j < 4; ++j)   // K = 16 per instruction: 32 bytes further along each row
           tc_mma_f16(tmem, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), p.idesc, (kb | j) != 0);
       }
       tc_commit(smem_u32(&bar_empty[s]));
     }
+  };
+
+  Regs ra, rb;
+  load_block(0, ra);
+  for (int kb = 0; kb < p.kblocks; kb += 2) {
+    if (kb + 1 < p.kblocks) load_block(kb + 1, rb);
+    step(kb, ra);
+    if (kb + 1 >= p.kblocks) break;
+    if (kb + 2 < p.kblocks) load_block(kb + 2, ra);
+    step(kb + 1, rb);
   }
   if (tid == 0) tc_commit(smem_u32(&bar_done));
   mbar_wait_bounded(smem_u32(&bar_done), 0, kTcWaitNs);
