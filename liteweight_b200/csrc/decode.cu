@@ -203,6 +203,181 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   cluster.sync();   // keep this CTA's shared memory alive until every remote read is done
 }
 
+// ------------------------------------------------------------- prompt-chunk attention
+//
+// Rows of a prompt chunk are consecutive positions p0 .. p0 + R - 1 of one
+// sequence (causal: row r attends keys 0 .. p0 + r). One CTA per (16 query
+// positions, kv head) with one warp per query head of the GQA group, so each
+// K/V block is staged in shared memory once for the whole group. Per block of
+// 64 keys a warp computes S = Q K^T (16 x 64) with mma.sync m16n8k16 (K
+// fragments by ldmatrix), masks by position, updates an fp32 online softmax
+// (row max / sum, exp2 of log2e-scaled scores), and accumulates O += P V with
+// P taken straight from the score fragments (rounded to fp16, the precision
+// of the reference's softmax output) and V fragments by ldmatrix.trans.
+constexpr int kPfKeys = 64;
+constexpr int kPfRows = 16;
+
+LW_DEV void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+LW_DEV void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+LW_DEV uint32_t pack_h2(float lo, float hi) { return h2_as_u32(__floats2half2_rn(lo, hi)); }
+
+template <int HD, int GQ>
+__global__ void __launch_bounds__(GQ * 32) attn_prefill_kernel(const AttnParams p) {
+  constexpr int RS = HD + 8;   // padded row (halves): rows 16 bytes apart modulo 128
+  constexpr int NT = GQ * 32;
+  __shared__ __align__(16) __half ks[kPfKeys * RS];
+  __shared__ __align__(16) __half vs[kPfKeys * RS];
+  const int qb = blockIdx.x, kvh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int p0 = *p.pos, cs = *p.seq, R = p.B;
+  const int r0 = qb * kPfRows;
+  const int head = kvh * GQ + warp;
+  const int kv_len = p0 + min(R, r0 + kPfRows);   // keys any row of this block may see
+  const int qpos_lo = p0 + r0 + g, qpos_hi = qpos_lo + 8;
+
+  // Q fragments (A operand: 16 rows x HD), rows past R are zero
+  uint32_t qa[HD / 16][4];
+  {
+    const int rl = r0 + g, rh = r0 + g + 8;
+    const __half* ql = p.q + (size_t)rl * p.nq * HD + (size_t)head * HD + 2 * t;
+    const __half* qh = p.q + (size_t)rh * p.nq * HD + (size_t)head * HD + 2 * t;
+#pragma unroll
+    for (int kt = 0; kt < HD / 16; ++kt) {
+      qa[kt][0] = rl < R ? *reinterpret_cast<const uint32_t*>(ql + kt * 16) : 0u;
+      qa[kt][1] = rh < R ? *reinterpret_cast<const uint32_t*>(qh + kt * 16) : 0u;
+      qa[kt][2] = rl < R ? *reinterpret_cast<const uint32_t*>(ql + kt * 16 + 8) : 0u;
+      qa[kt][3] = rh < R ? *reinterpret_cast<const uint32_t*>(qh + kt * 16 + 8) : 0u;
+    }
+  }
+  float o[HD / 8][4];
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  const __half* kg = p.k + ((size_t)cs * p.nkv + kvh) * p.S * HD;
+  const __half* vg = p.v + ((size_t)cs * p.nkv + kvh) * p.S * HD;
+  const uint32_t ks_a = smem_u32(ks), vs_a = smem_u32(vs);
+
+  for (int k0 = 0; k0 < kv_len; k0 += kPfKeys) {
+    __syncthreads();   // the previous block is no longer read
+    for (int i = threadIdx.x; i < kPfKeys * HD / 8; i += NT) {
+      const int r = i / (HD / 8), c = (i % (HD / 8)) * 8;
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (k0 + r < kv_len) {
+        kv = *reinterpret_cast<const uint4*>(kg + (size_t)(k0 + r) * HD + c);
+        vv = *reinterpret_cast<const uint4*>(vg + (size_t)(k0 + r) * HD + c);
+      }
+      sts128(ks + r * RS + c, kv);
+      sts128(vs + r * RS + c, vv);
+    }
+    __syncthreads();
+
+    // S = Q K^T over this block's 64 keys (8 tiles of 8 keys)
+    float sc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+#pragma unroll
+    for (int kt = 0; kt < HD / 16; ++kt) {
+#pragma unroll
+      for (int n2 = 0; n2 < 4; ++n2) {
+        const int mi = lane >> 3;
+        const int key = n2 * 16 + (mi >> 1) * 8 + (lane & 7), dim = kt * 16 + (mi & 1) * 8;
+        uint32_t b[4];
+        ldsm_x4(ks_a + (uint32_t)(key * RS + dim) * 2u, b);
+        mma16816(sc[2 * n2], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], b[0], b[1]);
+        mma16816(sc[2 * n2 + 1], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], b[2], b[3]);
+      }
+    }
+    // scale, causal mask, online softmax (rows g and g + 8 of the lane)
+    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = k0 + nt * 8 + 2 * t + (e & 1);
+        const int qp = e < 2 ? qpos_lo : qpos_hi;
+        float v = sc[nt][e] * p.scale_log2;
+        if (key > qp || key >= kv_len) v = -INFINITY;
+        sc[nt][e] = v;
+        if (e < 2) mx_lo = fmaxf(mx_lo, v);
+        else mx_hi = fmaxf(mx_hi, v);
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+    }
+    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+    const float c_lo = mn_lo == -INFINITY ? 1.f : exp2f(m_lo - mn_lo);
+    const float c_hi = mn_hi == -INFINITY ? 1.f : exp2f(m_hi - mn_hi);
+    float s_lo = 0.f, s_hi = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sc[nt][0] = mn_lo == -INFINITY ? 0.f : exp2f(sc[nt][0] - mn_lo);
+      sc[nt][1] = mn_lo == -INFINITY ? 0.f : exp2f(sc[nt][1] - mn_lo);
+      sc[nt][2] = mn_hi == -INFINITY ? 0.f : exp2f(sc[nt][2] - mn_hi);
+      sc[nt][3] = mn_hi == -INFINITY ? 0.f : exp2f(sc[nt][3] - mn_hi);
+      s_lo += sc[nt][0] + sc[nt][1];
+      s_hi += sc[nt][2] + sc[nt][3];
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      s_lo += __shfl_xor_sync(0xffffffffu, s_lo, off);
+      s_hi += __shfl_xor_sync(0xffffffffu, s_hi, off);
+    }
+    l_lo = l_lo * c_lo + s_lo;
+    l_hi = l_hi * c_hi + s_hi;
+    m_lo = mn_lo;
+    m_hi = mn_hi;
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) {
+      o[i][0] *= c_lo;
+      o[i][1] *= c_lo;
+      o[i][2] *= c_hi;
+      o[i][3] *= c_hi;
+    }
+    // O += P V: the score fragments of key tiles 2kk, 2kk+1 are the A fragment of keys 16kk..16kk+15
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t a0 = pack_h2(sc[2 * kk][0], sc[2 * kk][1]);
+      const uint32_t a1 = pack_h2(sc[2 * kk][2], sc[2 * kk][3]);
+      const uint32_t a2 = pack_h2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+      const uint32_t a3 = pack_h2(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+      for (int d2 = 0; d2 < HD / 16; ++d2) {
+        const int mi = lane >> 3;
+        const int key = kk * 16 + (mi & 1) * 8 + (lane & 7), dim = d2 * 16 + (mi >> 1) * 8;
+        uint32_t b[4];
+        ldsm_x4_t(vs_a + (uint32_t)(key * RS + dim) * 2u, b);
+        mma16816(o[2 * d2], a0, a1, a2, a3, b[0], b[1]);
+        mma16816(o[2 * d2 + 1], a0, a1, a2, a3, b[2], b[3]);
+      }
+    }
+  }
+  // out rows r0 + g and r0 + g + 8
+  const int rl = r0 + g, rh = r0 + g + 8;
+  const float il = l_lo > 0.f ? 1.f / l_lo : 0.f, ih = l_hi > 0.f ? 1.f / l_hi : 0.f;
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) {
+    const int d = i * 8 + 2 * t;
+    if (rl < R)
+      *reinterpret_cast<uint32_t*>(p.out + (size_t)rl * p.nq * HD + (size_t)head * HD + d) =
+          pack_h2(o[i][0] * il, o[i][1] * il);
+    if (rh < R)
+      *reinterpret_cast<uint32_t*>(p.out + (size_t)rh * p.nq * HD + (size_t)head * HD + d) =
+          pack_h2(o[i][2] * ih, o[i][3] * ih);
+  }
+}
+
 // ------------------------------------------------------------- tokens
 
 // x[b] = embed[tokens[*pos][b]]
@@ -553,6 +728,18 @@ int lw_attention_decode(const lw_attention_args* a, lw_stream_t stream) {
   const bool pdl = a->pdl != 0;
   cudaGetLastError();
   cudaError_t e;
+  if (p.seq) {   // a prompt chunk: rows are positions of one sequence
+    dim3 grid((p.B + lw::kPfRows - 1) / lw::kPfRows, p.nkv);
+#define LW_PF(HD_, GQ_)                                                                                    \
+  if (a->head_dim == HD_ && gq == GQ_) {                                                                   \
+    e = lw_launch(lw::attn_prefill_kernel<HD_, GQ_>, grid, dim3(GQ_ * 32), 0, s, pdl, p);                  \
+    if (e == cudaSuccess) e = cudaGetLastError();                                                          \
+    return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;                                                       \
+  }
+    LW_PF(128, 1) LW_PF(128, 2) LW_PF(128, 4) LW_PF(128, 8) LW_PF(64, 1) LW_PF(64, 2) LW_PF(64, 4) LW_PF(64, 8)
+#undef LW_PF
+    return LW_ERR_UNSUPPORTED;
+  }
   if (a->head_dim == 128 && gq == 4) e = attn_launch<128, 4>(p, s, pdl);
   else if (a->head_dim == 128 && gq == 8) e = attn_launch<128, 8>(p, s, pdl);
   else if (a->head_dim == 128 && gq == 2) e = attn_launch<128, 2>(p, s, pdl);
