@@ -4,45 +4,77 @@
 // with W the liteweight-packed weight, dequantized exactly (fp16(code * scale),
 // liteweight/quantize.py:30-43, :102-128), and X the fp16 activation.
 //
-// One CTA per 128-row weight tile. The K dimension is cut into blocks of 64;
-// each block is one stage of a 4-stage shared-memory pipeline holding the
-// A operand (128 weight rows x 64, fp16) and the B operand (Mpad activation
-// rows x 64, fp16), both K-major in the 128-byte-swizzled layout the tensor
-// core reads (16-byte chunk c of row r stored at chunk c ^ (r & 7); rows 128
-// bytes apart, 8-row groups 1024 bytes apart). All 256 threads fill a stage
-// (weights: load, unpack, scale, reorder; activations: copy) and arrive on its
-// "full" mbarrier; one elected thread waits for it and issues four
-// tcgen05.mma (K = 16 each) accumulating into tensor memory (128 lanes = tile
-// rows, Mpad fp32 columns = activation rows), then tcgen05.commit to the
-// stage's "empty" mbarrier, which frees the stage for the producers. After the
-// last block a final commit signals the epilogue: every warp reads its 32
-// lanes x every other 32-column chunk with tcgen05.ld and applies the epilogue (residual
-// add / SwiGLU / RoPE + KV-cache append, the GEMV kernels' rounding points).
+// One CTA (or one cluster of `splits` CTAs, each a slice of K) per 128-row
+// weight tile. K is cut into blocks of 64; each block is one stage of an
+// S-stage ring (S <= 8, as many as fit) holding in shared memory
+//   B operand          Mpad activation rows x 64 fp16 (TMA, 128-byte swizzle:
+//                      16-byte chunk c of row r at chunk c ^ (r & 7), rows 128
+//                      bytes apart, 8-row groups 1024 bytes apart; K-major)
+//   raw weight codes   128 rows x 32 / 64 bytes (TMA, no swizzle)
+// and in tensor memory the A operand, 128 weight rows (lanes) x 64 fp16 (32
+// columns), written by the dequantizing threads with tcgen05.st: the MMA
+// reads A from tensor memory ("TS" form), so shared memory carries only the
+// copies in, the codes out and B into the tensor core (a 128 x 128 x 64
+// stage moves ~40 KB through it instead of ~72 KB with A staged there, which
+// bounded the stage rate at the shared-memory bandwidth). The CTA's eighteen
+// warps are specialised:
+//   warp 16  one lane issues the two TMA tile copies of each stage (weights
+//            first, before griddepcontrol.wait: they do not depend on the
+//            previous kernel) once the tensor core has released the stage;
+//   warps 0-15 unpack the stage's raw codes, scale them (fp16 hmul, the
+//            reference's rounding) and store the A operand to tensor memory:
+//            four groups of four warps (one weight row per thread, the warp's
+//            own 32 lanes) take the stages in turn;
+//   warp 17  owns the tensor memory; one lane issues four tcgen05.mma
+//            (K = 16 each) per stage into the fp32 accumulator (128 lanes =
+//            tile rows, columns [0, Mpad) = activation rows) and commits the
+//            stage back to the producer.
+// After the last stage, warps 0-15 read the accumulator with tcgen05.ld. With
+// one CTA per tile they apply the epilogue directly; with a cluster, every CTA
+// writes its partial tile to its own shared memory, and CTA c sums column
+// slice c of all partials over distributed shared memory in rank order (the
+// same sums on every run) and applies the epilogue to it. Epilogues: residual
+// add / SwiGLU / RoPE + KV-cache append, at the GEMV kernels' rounding points.
 //
 // Every mbarrier wait is bounded (global timer): on expiry the kernel records
-// LW_ERR_TIMEOUT, still drains, reads and releases its tensor memory, and
-// returns; results of that launch are then invalid.
+// LW_ERR_TIMEOUT, the other roles stop at their next wait, the producer waits
+// (bounded) for the copies it issued, and the tensor memory is released; the
+// results of that launch are then invalid.
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "gemv_host.cuh"
 
 namespace lw {
 
-constexpr int kTcThreads = 256;
-constexpr int kTcStages = 4;
-constexpr int kTcTileN = 128;     // weight rows per CTA (UMMA M)
-constexpr int kTcKBlock = 64;     // K per stage (one 128-byte swizzle row of fp16)
-constexpr int kTcMaxM = 256;      // activation rows (UMMA N)
+constexpr int kTcDeqWarps = 16;      // warps 0-15: dequantize, then the epilogue
+constexpr int kTcDeqThreads = kTcDeqWarps * 32;
+constexpr int kTcDeqGroups = kTcDeqWarps / 4;     // a group of 128 threads converts a whole block
+constexpr int kTcProducerWarp = kTcDeqWarps;       // TMA producer
+constexpr int kTcMmaWarp = kTcDeqWarps + 1;        // MMA issuer, tensor-memory owner
+constexpr int kTcThreads = kTcDeqThreads + 64;
+constexpr int kTcMaxStages = 8;
+constexpr int kTcTileN = 128;        // weight rows per CTA (UMMA M)
+constexpr int kTcKBlock = 64;        // K per stage (one 128-byte swizzle row of fp16)
+constexpr int kTcMaxM = 256;         // activation rows (UMMA N)
+constexpr int kTcMaxSplits = 4;
+constexpr size_t kTcSmemMax = 225 * 1024;
 constexpr long long kTcWaitNs = 500000000;
 
 struct TcGemmParams {
-  const uint8_t* w;
+  CUtensorMap tm_w;   // weights: [N rows][K * BITS / 8 bytes] u8, box {block bytes, 128}
+  CUtensorMap tm_x;   // activations: [M rows][K] fp16 (row stride lda), box {64, Mpad}, 128-byte swizzle
   const __half* scales;
-  const __half* act;
   __half* out;
   const __half* residual;
-  int lda, ldo;
+  int ldo;
   int M, Mpad, N, K, G, gshift, kblocks;
+  int splits, kb_per, stages;
+  uint32_t stage_bytes, b_bytes, w_bytes;
   uint32_t idesc;
   int tmem_cols;
+  int acc_cols;       // accumulator columns [0, acc_cols); A operand of ring slot s at acc_cols + 32 s
   // rope / kv
   const __half* rope_cos;
   const __half* rope_sin;
@@ -76,6 +108,29 @@ LW_DEV void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D (tensor memory) += A (tensor memory, 128 lanes x 16 fp16 in 8 columns) x B (shared memory).
+LW_DEV void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      " .reg .pred p;\n"
+      " setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 registers per thread -> 32 consecutive columns of this warp's 32 lanes.
+LW_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+LW_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 LW_DEV void tc_commit(uint32_t mbar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar) : "memory");
 }
@@ -108,7 +163,6 @@ LW_DEV uint64_t sw128_desc(uint32_t smem_addr) {
   return d;
 }
 
-LW_DEV uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
 
 // 8 codes of one 32-bit word -> 8 fp16 in natural k order, each fp16(code * scale).
 template <int BITS>
@@ -135,30 +189,103 @@ LW_DEV uint4 dequant8(uint32_t lo, uint32_t hi, uint32_t s2) {
   return o;
 }
 
+LW_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// One lane of the (fully active) warp returns true.
+LW_DEV bool elect_one_sync() {
+  uint32_t elected;
+  asm volatile(
+      "{\n"
+      " .reg .pred P;\n"
+      " elect.sync _|P, 0xffffffff;\n"
+      " selp.u32 %0, 1, 0, P;\n"
+      "}\n"
+      : "=r"(elected));
+  return elected != 0;
+}
+LW_DEV void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Epilogue of one accumulator value: tile row n (lane `lane` of its warp),
+// activation row m. Every lane of the warp calls it for the same m.
+template <int EPI>
+LW_DEV void tc_epilogue(const TcGemmParams& p, int n, int m, float y, int lane) {
+  if constexpr (EPI == LW_TC_EPI_RESID) {
+    if (m >= p.M || n >= p.N) return;
+    y = r16(y);
+    if (p.residual) y = r16(__half2float(p.residual[(size_t)m * p.ldo + n]) + y);
+    p.out[(size_t)m * p.ldo + n] = __float2half_rn(y);
+  } else {
+    // rows g and g + 8 of every 16-row tile are partners (gate/up, or the
+    // rotate_half pair): the lower lane of each pair finishes both
+    const float partner = __shfl_down_sync(0xffffffffu, y, 8);
+    const bool lower = (lane & 15) < 8;
+    if (!lower || m >= p.M || n >= p.N) return;
+    const int t16 = n >> 4, g = n & 7;
+    if constexpr (EPI == LW_TC_EPI_SWIGLU) {
+      const float gt = r16(y), up = r16(partner);
+      const float a = r16(silu_f32(gt));
+      p.out[(size_t)m * p.ldo + t16 * 8 + g] = __float2half_rn(a * up);
+    } else {
+      const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
+      const int head = (t16 * 16) / hd, jt = t16 % (hd / 16);
+      const int d_lo = 8 * jt + g, d_hi = d_lo + hd / 2;
+      const int pos = *p.pos + m, row = *p.seq;
+      const float y_lo = r16(y), y_hi = r16(partner);
+      float o_lo = y_lo, o_hi = y_hi;
+      if (head < nq + nkv) {
+        const float c_lo = __half2float(p.rope_cos[(size_t)pos * hd + d_lo]);
+        const float c_hi = __half2float(p.rope_cos[(size_t)pos * hd + d_hi]);
+        const float s_lo = __half2float(p.rope_sin[(size_t)pos * hd + d_lo]);
+        const float s_hi = __half2float(p.rope_sin[(size_t)pos * hd + d_hi]);
+        o_lo = r16(r16(y_lo * c_lo) + r16(-y_hi * s_lo));
+        o_hi = r16(r16(y_hi * c_hi) + r16(y_lo * s_hi));
+      }
+      __half* dst;
+      if (head < nq) dst = p.q_out + (size_t)m * nq * hd + (size_t)head * hd;
+      else if (head < nq + nkv) dst = p.k_cache + (((size_t)row * nkv + (head - nq)) * p.max_seq + pos) * hd;
+      else dst = p.v_cache + (((size_t)row * nkv + (head - nq - nkv)) * p.max_seq + pos) * hd;
+      dst[d_lo] = __float2half_rn(o_lo);
+      dst[d_hi] = __float2half_rn(o_hi);
+    }
+  }
+}
+
 template <int BITS, int EPI>
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcGemmParams p) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  __shared__ __align__(8) unsigned long long bar_full[kTcStages], bar_empty[kTcStages], bar_done;
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcGemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) unsigned long long bar_raw[kTcMaxStages], bar_a[kTcMaxStages], bar_empty[kTcMaxStages];
+  __shared__ __align__(8) unsigned long long bar_done;
   __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n0 = blockIdx.x * kTcTileN;
-  const uint32_t a_bytes = kTcTileN * 128;         // 16 KB
-  const uint32_t b_bytes = (uint32_t)p.Mpad * 128;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
-  // stages on 1024-byte boundaries (the swizzle pattern follows address bits 4-9)
+  const int split = (int)(blockIdx.x % (unsigned)p.splits), tile = (int)(blockIdx.x / (unsigned)p.splits);
+  const int n0 = tile * kTcTileN;
+  const int kb0 = split * p.kb_per, nkb = max(0, min(p.kblocks, kb0 + p.kb_per) - kb0);
+  const int S = p.stages;
+  // stages on 1024-byte boundaries (the swizzle pattern follows address bits 4-9):
+  // B operand at +0, raw weight codes after it
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - smem_u32(smem_raw));
 
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(smem_u32(&bar_full[s]), kTcThreads);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&bar_raw[s]), 1);
+      mbar_init(smem_u32(&bar_a[s]), kTcDeqThreads / kTcDeqGroups);
       mbar_init(smem_u32(&bar_empty[s]), 1);
     }
     mbar_init(smem_u32(&bar_done), 1);
+    abort_s = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == kTcMmaWarp) {
     tmem_alloc(smem_u32(&tmem_base_s), (uint32_t)p.tmem_cols);
     tmem_relinquish();
   }
@@ -167,159 +294,208 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const TcGemmPara
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
 
-  pdl_wait();
-  pdl_launch_dependents();
+  // Bounded wait shared by the roles: the first to give up makes the others
+  // stop at their next wait.
+  auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort_s) return false;
+    if (mbar_wait_bounded(bar, parity, kTcWaitNs)) return true;
+    abort_s = 1;
+    return false;
+  };
 
-  const size_t rowbytes = (size_t)p.K * BITS / 8;
-  const int ngroups = p.K / p.G;
-  // producer roles: weight row r = tid / 2, half h = tid & 1 (32 codes = 4 chunks)
-  const int ar = tid >> 1, ah = tid & 1;
-  const int wrow = min(n0 + ar, p.N - 1);
-  const uint8_t* wsrc = p.w + (size_t)wrow * rowbytes;
-  const unsigned short* ssrc = reinterpret_cast<const unsigned short*>(p.scales) + (size_t)wrow * ngroups;
-  bool live = true;
+  // The producer and MMA roles run as whole warps: their loop state and the
+  // operand descriptors stay warp-uniform (uniform registers), and one elected
+  // lane issues each TMA copy / tcgen05 instruction.
+  // Every lane of the warp polls (measured faster than one polling lane
+  // followed by a shuffle); lane 0's answer is the warp's.
+  auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    return __shfl_sync(0xffffffffu, wait(bar, parity) ? 1u : 0u, 0) != 0;
+  };
 
-  // Each thread's global loads of a k-block go to registers one block ahead of
-  // their use (dequantize / store), so the load latency overlaps a block of work.
-  constexpr int kBMax = kTcMaxM * 8 / kTcThreads;   // activation chunks per thread, at most
-  struct Regs {
-    uint4 w0, w1;
-    unsigned short sc;
-    uint4 b[kBMax];
-  };
-  auto load_block = [&](int kb, Regs& r) {
-    const int k0 = kb * kTcKBlock + ah * 32;
-    r.sc = __ldg(ssrc + min(k0 >> p.gshift, ngroups - 1));
-    if constexpr (BITS == 4) {
-      r.w0 = ldg_stream(wsrc + (size_t)k0 / 2);
-    } else {
-      r.w0 = ldg_stream(wsrc + (size_t)k0);
-      r.w1 = ldg_stream(wsrc + (size_t)k0 + 16);
+  if (warp == kTcProducerWarp) {
+    // ---- TMA producer
+    const bool leader = elect_one_sync();
+    if (leader) {
+      tma_prefetch_map(&p.tm_w);
+      tma_prefetch_map(&p.tm_x);
     }
-#pragma unroll
-    for (int j = 0; j < kBMax; ++j) {
-      const int i = tid + j * kTcThreads;
-      r.b[j] = make_uint4(0, 0, 0, 0);
-      const int m = i >> 3, c = i & 7;   // rows past M stay zero
-      if (i < p.Mpad * 8 && m < p.M) r.b[j] = ldg_nc(p.act + (size_t)m * p.lda + kb * kTcKBlock + c * 8);
+    const int first = min(S, nkb);
+    const int wx = BITS == 4 ? kTcKBlock / 2 : kTcKBlock;   // weight bytes per row per block
+    for (int i = 0; i < first; ++i) {
+      const uint32_t st = base + i * p.stage_bytes, bar = smem_u32(&bar_raw[i]);
+      if (leader) {
+        mbar_arrive_expect_tx(bar, p.w_bytes + p.b_bytes);
+        tma_load_2d(st + p.b_bytes, &p.tm_w, (kb0 + i) * wx, n0, bar);
+      }
     }
-  };
-  auto store_block = [&](int s, const Regs& r) {
-    const uint32_t sa = base + s * stage_bytes, sb = sa + a_bytes;
-    const uint32_t s2 = (uint32_t)r.sc | ((uint32_t)r.sc << 16);
-    if constexpr (BITS == 4) {
-      const uint32_t qw[4] = {r.w0.x, r.w0.y, r.w0.z, r.w0.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sts128(base_ptr + (sa - base) + swz(ar, ah * 4 + j), dequant8<4>(qw[j], 0u, s2));
-    } else {
-      const uint32_t qw[8] = {r.w0.x, r.w0.y, r.w0.z, r.w0.w, r.w1.x, r.w1.y, r.w1.z, r.w1.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        sts128(base_ptr + (sa - base) + swz(ar, ah * 4 + j), dequant8<8>(qw[2 * j], qw[2 * j + 1], s2));
+    pdl_wait();   // activations come from the previous kernel
+    pdl_launch_dependents();
+    for (int i = 0; i < first; ++i)
+      if (leader)
+        tma_load_2d(base + i * p.stage_bytes, &p.tm_x, (kb0 + i) * kTcKBlock, 0, smem_u32(&bar_raw[i]));
+    __syncwarp();
+    int issued = first;
+    uint32_t phase = 0;   // parity of the empty-barrier phase awaited in the current pass over the ring
+    for (int i = first, s = 0; i < nkb; ++i) {
+      if (!warp_wait(smem_u32(&bar_empty[s]), phase)) break;
+      const uint32_t st = base + s * p.stage_bytes, bar = smem_u32(&bar_raw[s]);
+      if (leader) {
+        mbar_arrive_expect_tx(bar, p.w_bytes + p.b_bytes);
+        tma_load_2d(st + p.b_bytes, &p.tm_w, (kb0 + i) * wx, n0, bar);
+        tma_load_2d(st, &p.tm_x, (kb0 + i) * kTcKBlock, 0, bar);
+      }
+      __syncwarp();
+      issued = i + 1;
+      if (++s == S) {
+        s = 0;
+        phase ^= 1u;
+      }
     }
-#pragma unroll
-    for (int j = 0; j < kBMax; ++j) {
-      const int i = tid + j * kTcThreads;
-      if (i < p.Mpad * 8) sts128(base_ptr + (sb - base) + swz(i >> 3, i & 7), r.b[j]);
+    // no copy may land after the CTA has exited: wait (bounded) for the last
+    // one issued into every stage (immediate unless a wait gave up)
+    if (leader) {
+      for (int s = 0; s < min(S, issued); ++s) {
+        const int last = (issued - 1 - s) / S;   // use index of stage s's last copy
+        mbar_wait_bounded(smem_u32(&bar_raw[s]), last & 1, kTcWaitNs);
+      }
     }
-  };
-  auto step = [&](int kb, const Regs& cur) {
-    const int s = kb % kTcStages, use = kb / kTcStages;
-    if (use > 0 && live) live = mbar_wait_bounded(smem_u32(&bar_empty[s]), (use - 1) & 1, kTcWaitNs);
-    store_block(s, cur);
-    fence_proxy_async_smem();   // the tensor core reads these through the async proxy
-    mbar_arrive(smem_u32(&bar_full[s]));
-    if (tid == 0) {
-      if (live) live = mbar_wait_bounded(smem_u32(&bar_full[s]), use & 1, kTcWaitNs);
+  } else if (warp == kTcMmaWarp) {
+    // ---- MMA issuer: B descriptor of stage 0, advanced by the stage offset and
+    // by 32 bytes (2 in 16-byte units) per K = 16 step; A in tensor memory,
+    // 8 columns per K = 16 step
+    const uint64_t db0 = sw128_desc(base);
+    uint32_t phase = 0;
+    for (int i = 0, s = 0; i < nkb; ++i) {
+      if (!warp_wait(smem_u32(&bar_a[s]), phase)) break;
       tc_fence_after();
-      if (live) {
-        const uint32_t sa = base + s * stage_bytes, sb = sa + a_bytes;
+      const uint64_t off = (uint64_t)(((uint32_t)s * p.stage_bytes) >> 4);
+      if (elect_one_sync()) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)   // K = 16 per instruction: 32 bytes further along each row
-          tc_mma_f16(tmem, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), p.idesc, (kb | j) != 0);
+        for (int j = 0; j < 4; ++j)
+          tc_mma_f16_ts(tmem, tmem + (uint32_t)(p.acc_cols + 32 * s + 8 * j), db0 + off + 2 * j, p.idesc,
+                        (i | j) != 0);
+        tc_commit(smem_u32(&bar_empty[s]));
       }
-      tc_commit(smem_u32(&bar_empty[s]));
+      __syncwarp();
+      if (++s == S) {
+        s = 0;
+        phase ^= 1u;
+      }
     }
-  };
-
-  Regs ra, rb;
-  load_block(0, ra);
-  for (int kb = 0; kb < p.kblocks; kb += 2) {
-    if (kb + 1 < p.kblocks) load_block(kb + 1, rb);
-    step(kb, ra);
-    if (kb + 1 >= p.kblocks) break;
-    if (kb + 2 < p.kblocks) load_block(kb + 2, ra);
-    step(kb + 1, rb);
+    if (elect_one_sync()) tc_commit(smem_u32(&bar_done));   // arrives once every MMA issued above has completed
+    __syncwarp();
+  } else {
+    // ---- dequantize: group dg (4 warps) converts blocks dg, dg + 4, ... of
+    // this CTA; thread ar of the group owns weight row ar (64 codes)
+    const int dg = tid >> 7, ar = tid & 127;
+    const int ngroups = p.K / p.G;
+    const unsigned short* ssrc =
+        reinterpret_cast<const unsigned short*>(p.scales) + (size_t)min(n0 + ar, p.N - 1) * ngroups;
+    auto scales_of = [&](int kb, unsigned short& s0, unsigned short& s1) {
+      s0 = __ldg(ssrc + min((kb * kTcKBlock) >> p.gshift, ngroups - 1));
+      s1 = __ldg(ssrc + min((kb * kTcKBlock + 32) >> p.gshift, ngroups - 1));
+    };
+    const uint32_t raw_off = p.b_bytes + (uint32_t)ar * (BITS == 4 ? 32u : 64u);
+    // this warp's 32 lanes of tensor memory (a warp reaches lanes 32 (warp % 4) ..)
+    const uint32_t a_taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)p.acc_cols;
+    int i = dg, s = dg;   // block index within this CTA's K slice, its ring slot (S >= kTcDeqGroups)
+    uint32_t phase = 0;
+    unsigned short n0s = 0, n1s = 0;
+    if (i < nkb) scales_of(kb0 + i, n0s, n1s);
+    for (; i < nkb; i += kTcDeqGroups) {
+      const uint32_t s2a = (uint32_t)n0s | ((uint32_t)n0s << 16), s2b = (uint32_t)n1s | ((uint32_t)n1s << 16);
+      if (i + kTcDeqGroups < nkb) scales_of(kb0 + i + kTcDeqGroups, n0s, n1s);
+      if (!warp_wait(smem_u32(&bar_raw[s]), phase)) break;
+      tc_fence_after();   // the MMAs that read this slot's A columns before have completed
+      uint8_t* st = base_ptr + (size_t)s * p.stage_bytes;
+      uint4 o[8];
+      if constexpr (BITS == 4) {
+        const uint4 q0 = lds128(st + raw_off), q1 = lds128(st + raw_off + 16);
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = dequant8<4>(qw[j], 0u, j < 4 ? s2a : s2b);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint4 q = lds128(st + raw_off + 16 * h);
+          o[2 * h] = dequant8<8>(q.x, q.y, h < 2 ? s2a : s2b);
+          o[2 * h + 1] = dequant8<8>(q.z, q.w, h < 2 ? s2a : s2b);
+        }
+      }
+      // row ar of the A operand: 64 fp16 (natural k order) in 32 columns of lane ar
+      uint32_t r[32];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        r[4 * j] = o[j].x;
+        r[4 * j + 1] = o[j].y;
+        r[4 * j + 2] = o[j].z;
+        r[4 * j + 3] = o[j].w;
+      }
+      tmem_st32(a_taddr + (uint32_t)(32 * s), r);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&bar_a[s]));
+      s += kTcDeqGroups;
+      if (s >= S) {
+        s -= S;
+        phase ^= 1u;
+      }
+    }
   }
-  if (tid == 0) tc_commit(smem_u32(&bar_done));
-  mbar_wait_bounded(smem_u32(&bar_done), 0, kTcWaitNs);
-  tc_fence_after();
+  __syncwarp();   // the producer and MMA warps reconverge with their single working lane
 
-  // ---- epilogue: warp w reads lanes 32*(w%4).. (tile rows) and every other
-  // 32-column chunk (starting at 32*(w/4)); a chunk starts below Mpad and the
-  // allocation is a power of two >= 32 and >= Mpad, so every read is inside it
+  // ---- epilogue (warps 0-15): warp w reads lanes 32*(w%4).. (tile rows) and
+  // every fourth 32-column chunk (starting at 32*(w/4)); a chunk starts below
+  // Mpad and the allocation is a power of two >= 32 and >= Mpad, so every read
+  // is inside it
+  constexpr int kChunkWarps = kTcDeqWarps / 4;
   const int lg = warp & 3, ch = warp >> 2;
-  const int r = lg * 32 + lane;            // tile row
+  const int r = lg * 32 + lane;   // tile row
   const int n = n0 + r;
-  for (int c0 = ch * 32; c0 < p.Mpad; c0 += 64) {
-    uint32_t v[32];
-    __syncwarp();                          // tcgen05.ld is warp-collective (.sync.aligned)
-    tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)c0, v);
-    tmem_wait_ld();
-    if constexpr (EPI == LW_TC_EPI_RESID) {
-      if (n < p.N) {
+  // partial-tile row stride (floats): whole 32-column chunks are stored, +1
+  // so that the 32 lanes (rows) of a warp hit distinct banks
+  const int RS = ((p.Mpad + 31) & ~31) + 1;
+  float* red = reinterpret_cast<float*>(base_ptr);
+  if (warp < kTcDeqWarps) {
+    pdl_wait();   // the residual input comes from a previous kernel
+    uint32_t done = 1;
+    if (lane == 0) done = mbar_wait_bounded(smem_u32(&bar_done), 0, kTcWaitNs) ? 1u : 0u;
+    const bool ok = __shfl_sync(0xffffffffu, done, 0) && !abort_s;
+    tc_fence_after();
+    if (ok) {
+      for (int c0 = ch * 32; c0 < p.Mpad; c0 += 32 * kChunkWarps) {
+        uint32_t v[32];
+        __syncwarp();   // tcgen05.ld is warp-collective (.sync.aligned)
+        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)c0, v);
+        tmem_wait_ld();
+        if (p.splits == 1) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int m = c0 + j;
-          if (m >= p.M) break;
-          float y = r16(__uint_as_float(v[j]));
-          if (p.residual) y = r16(__half2float(p.residual[(size_t)m * p.ldo + n]) + y);
-          p.out[(size_t)m * p.ldo + n] = __float2half_rn(y);
-        }
-      }
-    } else {
-      // rows g and g + 8 of every 16-row tile are partners (gate/up, or the
-      // rotate_half pair): the lower lane of each pair finishes both
-      const bool lower = (lane & 15) < 8;
-      const int t16 = n >> 4, g = n & 7;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float y = __uint_as_float(v[j]);
-        const float partner = __shfl_down_sync(0xffffffffu, y, 8);
-        const int m = c0 + j;
-        if (!lower || m >= p.M || n >= p.N) continue;
-        if constexpr (EPI == LW_TC_EPI_SWIGLU) {
-          const float gt = r16(y), up = r16(partner);
-          const float a = r16(silu_f32(gt));
-          p.out[(size_t)m * p.ldo + t16 * 8 + g] = __float2half_rn(a * up);
+          for (int j = 0; j < 32; ++j) tc_epilogue<EPI>(p, n, c0 + j, __uint_as_float(v[j]), lane);
         } else {
-          const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
-          const int head = (t16 * 16) / hd, jt = t16 % (hd / 16);
-          const int d_lo = 8 * jt + g, d_hi = d_lo + hd / 2;
-          const int pos = *p.pos + m, row = *p.seq;
-          const float y_lo = r16(y), y_hi = r16(partner);
-          float o_lo = y_lo, o_hi = y_hi;
-          if (head < nq + nkv) {
-            const float c_lo = __half2float(p.rope_cos[(size_t)pos * hd + d_lo]);
-            const float c_hi = __half2float(p.rope_cos[(size_t)pos * hd + d_hi]);
-            const float s_lo = __half2float(p.rope_sin[(size_t)pos * hd + d_lo]);
-            const float s_hi = __half2float(p.rope_sin[(size_t)pos * hd + d_hi]);
-            o_lo = r16(r16(y_lo * c_lo) + r16(-y_hi * s_lo));
-            o_hi = r16(r16(y_hi * c_hi) + r16(y_lo * s_hi));
-          }
-          __half* dst;
-          if (head < nq) dst = p.q_out + (size_t)m * nq * hd + (size_t)head * hd;
-          else if (head < nq + nkv) dst = p.k_cache + (((size_t)row * nkv + (head - nq)) * p.max_seq + pos) * hd;
-          else dst = p.v_cache + (((size_t)row * nkv + (head - nq - nkv)) * p.max_seq + pos) * hd;
-          dst[d_lo] = __float2half_rn(o_lo);
-          dst[d_hi] = __float2half_rn(o_hi);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) red[r * RS + c0 + j] = __uint_as_float(v[j]);
         }
       }
     }
+  }
+  if (p.splits > 1) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();   // every partial tile is in its CTA's shared memory
+    if (warp < kTcDeqWarps && !abort_s) {
+      const int cw = p.Mpad / p.splits, m0 = split * cw;
+      for (int j = ch; j < cw; j += kChunkWarps) {
+        float y = 0.f;
+        for (int q = 0; q < p.splits; ++q) y += cluster.map_shared_rank(red, q)[r * RS + m0 + j];
+        tc_epilogue<EPI>(p, n, m0 + j, y, lane);
+      }
+    }
+    cluster.sync();   // no CTA leaves while its partial tile is still being read
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+  if (warp == kTcMmaWarp) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
 }
 
 // h[m] = fp16(gamma * fp16(x * rstd)), rstd = 1 / sqrt(mean(x^2) + eps) in fp32.
@@ -378,12 +554,71 @@ uint32_t tc_idesc(int mpad) {
   return d;
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (the library links the static runtime only).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// 2-D tiled tensor map: `rows` rows of `cols` elements, row stride `stride`
+// bytes, box {box_cols, box_rows}; reads past the edges fill zeros.
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType type, const void* ptr, uint64_t cols, uint64_t rows,
+               uint64_t stride, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {stride};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return enc(m, type, 2, const_cast<void*>(ptr), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!counts[dev] && cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    counts[dev] = 148;
+  return counts[dev];
+}
+
 template <int BITS, int EPI>
 cudaError_t tc_launch(const lw::TcGemmParams& p, size_t smem, cudaStream_t s, bool pdl) {
   auto kern = lw::gemm_tc_kernel<BITS, EPI>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return lw_launch(kern, dim3(p.N / lw::kTcTileN), dim3(lw::kTcThreads), smem, s, pdl, p);
+  lw_count_launch();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.N / lw::kTcTileN) * p.splits);
+  cfg.blockDim = dim3(lw::kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.splits > 1) {   // the CTAs of one tile (its K slices) form a cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)p.splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 }  // namespace
@@ -416,12 +651,9 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
       return LW_ERR_UNSUPPORTED;
   }
   lw::TcGemmParams p = {};
-  p.w = static_cast<const uint8_t*>(a->weight);
   p.scales = static_cast<const __half*>(a->scales);
-  p.act = static_cast<const __half*>(a->act);
   p.out = static_cast<__half*>(a->out);
   p.residual = static_cast<const __half*>(a->residual);
-  p.lda = a->lda;
   p.ldo = a->ldo;
   p.M = a->M;
   p.Mpad = (a->M + 15) / 16 * 16;
@@ -431,9 +663,9 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
   p.gshift = lw::group_shift(a->K, a->group_size);
   p.kblocks = a->K / lw::kTcKBlock;
   p.idesc = tc_idesc(p.Mpad);
-  int cols = 32;
-  while (cols < p.Mpad) cols <<= 1;
-  p.tmem_cols = cols;
+  int acc = 32;
+  while (acc < p.Mpad) acc <<= 1;
+  p.acc_cols = acc;
   p.rope_cos = static_cast<const __half*>(a->rope_cos);
   p.rope_sin = static_cast<const __half*>(a->rope_sin);
   p.pos = a->pos;
@@ -445,7 +677,34 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
   p.q_out = static_cast<__half*>(a->q_out);
   p.k_cache = static_cast<__half*>(a->k_cache);
   p.v_cache = static_cast<__half*>(a->v_cache);
-  const size_t smem = 1024 + (size_t)lw::kTcStages * (lw::kTcTileN * 128 + (size_t)p.Mpad * 128);
+
+  // K slices per tile: while the tiles alone leave at least half the SMs idle
+  // and every slice keeps >= 8 blocks of 64
+  const int tiles = p.N / lw::kTcTileN;
+  int splits = 1;
+  while (splits < lw::kTcMaxSplits && tiles * splits * 2 <= sm_count() && p.kblocks >= splits * 2 * 8) splits *= 2;
+  p.splits = splits;
+  p.kb_per = (p.kblocks + splits - 1) / splits;
+
+  const uint32_t wx = a->bits == 4 ? lw::kTcKBlock / 2 : lw::kTcKBlock;   // weight bytes per row per block
+  p.w_bytes = wx * lw::kTcTileN;
+  p.b_bytes = (uint32_t)p.Mpad * 128;
+  p.stage_bytes = p.b_bytes + p.w_bytes;
+  p.stages = (int)std::min<size_t>({(size_t)lw::kTcMaxStages, (lw::kTcSmemMax - 1024) / p.stage_bytes,
+                                    (size_t)(512 - acc) / 32});
+  int cols = 32;
+  while (cols < acc + 32 * p.stages) cols <<= 1;
+  p.tmem_cols = cols;
+  const size_t red_bytes = (size_t)lw::kTcTileN * (((p.Mpad + 31) & ~31) + 1) * 4;
+  if (p.stages < lw::kTcDeqGroups || (splits > 1 && red_bytes > (size_t)p.stages * p.stage_bytes)) return LW_ERR_BAD_SHAPE;
+  const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes;
+
+  const size_t rowbytes = (size_t)a->K * a->bits / 8;
+  if (!encode_2d(&p.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->weight, rowbytes, (uint64_t)a->N, rowbytes, wx,
+                 lw::kTcTileN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->act, (uint64_t)a->K, (uint64_t)a->M,
+                 (uint64_t)a->lda * 2, lw::kTcKBlock, (uint32_t)p.Mpad, CU_TENSOR_MAP_SWIZZLE_128B))
+    return LW_ERR_LAUNCH;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool pdl = a->pdl != 0;
   cudaGetLastError();

@@ -3,8 +3,9 @@
 Checked against a torch fp32 reference of the same arithmetic (dequantize
 exactly to fp16, fp32 sums, the epilogue's fp16 rounding points), within the
 row-scaled tolerance, for INT4 and INT8, M from 1 to 256 (ragged, padded to
-16 inside), several group sizes, and each epilogue (residual add, SwiGLU,
-RoPE + KV-cache append). lw_rmsnorm_rows against the oracle's RMSNorm.
+16 inside), several group sizes, K in one CTA per tile or sliced over a
+cluster of 2 / 4 CTAs (summed over distributed shared memory), and each
+epilogue (residual add, SwiGLU, RoPE + KV-cache append). lw_rmsnorm_rows against the oracle's RMSNorm.
 """
 
 import ctypes
@@ -61,7 +62,9 @@ def _close(got, ref):
 
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("M,N,K,G", [(1, 128, 64, 64), (5, 256, 256, 128), (16, 128, 512, 32), (37, 384, 192, 64),
-                                     (128, 256, 1024, 128), (256, 128, 256, 256)])
+                                     (128, 256, 1024, 128), (256, 128, 256, 256),
+                                     # K sliced over a cluster (2 or 4 CTAs per tile), ragged slices
+                                     (64, 512, 4096, 128), (200, 128, 2048, 64), (33, 256, 1088, 64)])
 @pytest.mark.parametrize("residual", [False, True])
 def test_gemm_residual(bits, M, N, K, G, residual):
     q, s, deq = _weights(bits, N, K, G, seed=M + N + K)
@@ -78,9 +81,10 @@ def test_gemm_residual(bits, M, N, K, G, residual):
 
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("M", [3, 64, 200])
-def test_gemm_swiglu(bits, M):
+@pytest.mark.parametrize("K", [512, 2048])
+def test_gemm_swiglu(bits, M, K):
     from liteweight_b200 import engine as E
-    I, K = 256, 512
+    I = 256
     q, s, deq = _weights(bits, 2 * I, K, 128, seed=M)
     gen = torch.Generator(device=DEV).manual_seed(M)
     act = torch.randn(M, K, generator=gen, device=DEV).half()
@@ -95,13 +99,13 @@ def test_gemm_swiglu(bits, M):
     assert E.TC_EPI_SWIGLU == 1
 
 
-@pytest.mark.parametrize("M,pos0", [(7, 0), (128, 40)])
-def test_gemm_rope_kv(M, pos0):
+@pytest.mark.parametrize("M,pos0,K", [(7, 0, 256), (128, 40, 256), (50, 3, 2048)])
+def test_gemm_rope_kv(M, pos0, K):
     """The q|k|v epilogue: rows stored in rope-pair order; RoPE (fp16 after
     each op, modeling_llama.py:161-162) at positions pos0 + m; q to q_out,
     k and v to the cache of sequence 1 only."""
     from liteweight_b200 import engine as E
-    hd, nq, nkv, K, S = 64, 4, 2, 256, 256
+    hd, nq, nkv, S = 64, 4, 2, 256
     N = (nq + 2 * nkv) * hd
     q, s, deq = _weights(4, N, K, 128, seed=3)
     gen = torch.Generator(device=DEV).manual_seed(9)
