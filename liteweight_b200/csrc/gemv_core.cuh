@@ -358,72 +358,109 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
 // element order the unpack produces (lane order), applying the prologue:
 // RMSNorm (modeling_llama.py:65-68 rounding points), optionally after adding
 // the all-reduced partial sum to the residual (CTA 0 writes the new residual).
-// Called by all NT threads of the CTA; ends with a CTA barrier.
+// A thread issues the loads of up to kStageBatch of its 16-byte groups before
+// storing any (each load is one L2 round trip after griddepcontrol.wait). The
+// sum of squares is reduced per warp, then over the warps in warp order (the
+// same fp32 sums on every run). ssq holds kMaxM * (NT / 32) floats. Called by
+// all NT threads of the CTA; ends with a CTA barrier.
+constexpr int kStageBatch = 8;
+
 template <int BITS, int PRO, int NT>
 LW_DEV void stage_activation(const StreamParams& p, __half* act_s, const __half* gam_s, float* ssq, uint32_t in_flag,
                              WaitBudget& wb) {
   constexpr int E = WT<BITS>::E;
   constexpr int KC = 4 * E;
-  const int tid = threadIdx.x, lane = tid & 31;
+  constexpr int NW = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int C = p.kchunks;
   const int groups8 = C * KC / 8;
-  if constexpr (PRO != PRO_PLAIN) {
-    if (tid < kMaxM) ssq[tid] = 0.f;
-    __syncthreads();
-  }
+  auto store = [&](int m, int k, uint4 v) {
+    if constexpr (BITS == 4) v = perm_int4_pairs(v);
+    const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
+    sts128(act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8, v);
+  };
+  auto square_sum = [&](const uint4& v, float& sq) {
+    const __half* hv = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = __half2float(hv[e]);
+      sq = fmaf(f, f, sq);
+    }
+  };
   for (int m = 0; m < p.M; ++m) {
     float sq = 0.f;
-    for (int i = tid; i < groups8; i += NT) {
-      const int k = i * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (k < p.K) {
-        v = ldg_nc(p.act + (size_t)m * p.lda + k);
-        if constexpr (kResidPro<PRO>) {
-          // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
+    if constexpr (PRO == PRO_PEER_RESID_NORM) {
+      for (int i = tid; i < groups8; i += NT) {
+        const int k = i * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (k < p.K) {
+          v = ldg_nc(p.act + (size_t)m * p.lda + k);
+          // the all-reduce itself: the world partials, summed in rank order,
+          // each word read once it carries this step's flag; then
+          // x_new = fp16(x + fp16(sum))
           float ps[8];
-          if constexpr (PRO == PRO_RESID_NORM) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
-            ps[0] = a.x; ps[1] = a.y; ps[2] = a.z; ps[3] = a.w;
-            ps[4] = b.x; ps[5] = b.y; ps[6] = b.z; ps[7] = b.w;
-          } else {
-            // the all-reduce itself: the world partials, summed in rank order,
-            // each word read once it carries this step's flag
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ps[e] = 0.f;
-            const size_t rstride = (size_t)p.M * p.K;
-            for (int r = 0; r < p.in_world; r += 2)
-              add_flagged8<2>(p.in_src + r * rstride + (size_t)m * p.K + k, rstride, min(2, p.in_world - r),
-                              in_flag, ps, wb, p.in_timeout_ns, p.in_error);
-          }
+          for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+          const size_t rstride = (size_t)p.M * p.K;
+          for (int r = 0; r < p.in_world; r += 2)
+            add_flagged8<2>(p.in_src + r * rstride + (size_t)m * p.K + k, rstride, min(2, p.in_world - r), in_flag,
+                            ps, wb, p.in_timeout_ns, p.in_error);
           __half* hv = reinterpret_cast<__half*>(&v);
 #pragma unroll
           for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
           if (blockIdx.x == 0) *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v;
+          square_sum(v, sq);
         }
-        if constexpr (PRO != PRO_PLAIN) {
-          const __half* hv = reinterpret_cast<const __half*>(&v);
+        store(m, k, v);
+      }
+    } else {
+      for (int i0 = tid; i0 < groups8; i0 += NT * kStageBatch) {
+        uint4 v[kStageBatch];
+        float4 pa[kStageBatch], pb[kStageBatch];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float f = __half2float(hv[e]);
-            sq = fmaf(f, f, sq);
+        for (int b = 0; b < kStageBatch; ++b) {
+          const int k = (i0 + b * NT) * 8;
+          v[b] = make_uint4(0, 0, 0, 0);
+          if (k < p.K) {
+            v[b] = ldg_nc(p.act + (size_t)m * p.lda + k);
+            if constexpr (PRO == PRO_RESID_NORM) {
+              pa[b] = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k));
+              pb[b] = __ldg(reinterpret_cast<const float4*>(p.psum + (size_t)m * p.K + k + 4));
+            }
           }
         }
+#pragma unroll
+        for (int b = 0; b < kStageBatch; ++b) {
+          const int i = i0 + b * NT, k = i * 8;
+          if (i >= groups8) break;
+          if (k < p.K) {
+            if constexpr (PRO == PRO_RESID_NORM) {
+              // x_new = fp16(x + fp16(psum)) (residual add of the all-reduced partial)
+              const float ps[8] = {pa[b].x, pa[b].y, pa[b].z, pa[b].w, pb[b].x, pb[b].y, pb[b].z, pb[b].w};
+              __half* hv = reinterpret_cast<__half*>(&v[b]);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
+              if (blockIdx.x == 0) *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v[b];
+            }
+            if constexpr (PRO != PRO_PLAIN) square_sum(v[b], sq);
+          }
+          store(m, k, v[b]);
+        }
       }
-      if constexpr (BITS == 4) v = perm_int4_pairs(v);
-      const int c = k / KC, r = k - c * KC, tt = r / E, j = (r - tt * E) / 8;
-      sts128(act_s + (size_t)m * p.cp + c * KC + (j * 4 + tt) * 8, v);
     }
     if constexpr (PRO != PRO_PLAIN) {
       sq = warp_sum(sq);
-      if (lane == 0) atomicAdd(&ssq[m], sq);
+      if (lane == 0) ssq[m * NW + warp] = sq;
     }
   }
   if constexpr (PRO != PRO_PLAIN) {
     __syncthreads();
     // modeling_llama.py:65-68: h = weight * fp16(x * rsqrt(mean(x^2) + eps))
     for (int m = 0; m < p.M; ++m) {
-      const float rstd = 1.0f / sqrtf(ssq[m] / (float)p.K + p.eps);
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) tot += ssq[m * NW + w];
+      const float rstd = 1.0f / sqrtf(tot / (float)p.K + p.eps);
       for (int i = tid; i < groups8; i += NT) {
         const int k = i * 8;
         if (k >= p.K) continue;
@@ -527,7 +564,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamMinBlocks) gemv_stream_
   extern __shared__ __align__(16) uint8_t smem[];
   __half* act_s = reinterpret_cast<__half*>(smem);
   __half* gam_s = act_s + (size_t)p.M * p.cp;   // norm prologues: gamma [K], after the staged rows
-  __shared__ float ssq[kMaxM];
+  __shared__ float ssq[kMaxM * (kStreamThreads / 32)];
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;

@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const StreamPa
   constexpr int E = WT<BITS>::E;
   constexpr int KC = 4 * E;
   extern __shared__ __align__(16) uint8_t smem[];   // bulk-copy destinations need 16 B, mbarriers 8 B
-  __shared__ float ssq[kMaxM];
+  __shared__ float ssq[kMaxM * (kTmaThreads / 32)];
 
   const int S = p.ring_slots;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
