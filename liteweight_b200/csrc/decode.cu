@@ -41,22 +41,38 @@ struct AttnParams {
 // Cluster attention: one thread-block cluster of kAttnCluster CTAs per
 // (sequence, kv head); CTA r of the cluster and warp w of the CTA own
 // positions [base + (r * W + w) * P, ... + P) of every round of
-// kAttnCluster * W * P positions. A warp issues the K/V loads of a whole
-// round (P positions, D halves each per lane) before using any, and those of
-// the next round before computing this one. Lanes split the head dimension;
-// per position the q.k dots of the GQA group are warp-reduced, then an online
-// softmax per query head updates (m, l, acc). Warps merge through shared
-// memory, then the cluster's CTAs merge through distributed shared memory
-// after a cluster barrier - no global round trips, no counters.
+// kAttnCluster * W * P positions (P = 8). Per round a warp computes, on the
+// tensor cores, S = Q K^T for the GQA group's query heads (MMA rows; rows
+// past GQ are zero) against its 8 positions (one m16n8k16 per 16 head dims),
+// an online softmax per head (rows: max / sum over the 4 lanes of a row), and
+// O += P V with m16n8k8 (P straight from the score fragments). Head dims are
+// permuted the same way in q and K so that each lane's fragments are whole
+// 16-byte loads: lane (g, t) holds K row g, 16-byte chunks 4q + t; V dims are
+// assigned to output columns so that lane (g, t) holds rows 2t, 2t+1, dims
+// [g HD/8, (g+1) HD/8) and pairs them with one byte permute per fragment.
+// Warps merge through shared memory, then the cluster's CTAs merge through
+// distributed shared memory after a cluster barrier - no global round trips,
+// no counters. The first two rounds of positions before *pos are loaded before
+// griddepcontrol.wait (they do not depend on the previous kernel).
 constexpr int kAttnWarps = 8;
 constexpr int kAttnCluster = 8;
 constexpr int kAttnPos = 8;   // positions per warp per round
 
+LW_DEV void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
 template <int HD, int GQ>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnParams p) {
+  static_assert(GQ <= 8 && (HD == 64 || HD == 128), "GQA group of at most 8 heads, head_dim 64 or 128");
   namespace cg = cooperative_groups;
-  constexpr int D = HD / 32;
   constexpr int W = kAttnWarps;
+  constexpr int KQ = HD / 32;    // 16-byte K chunks per lane per position (2 k-steps each)
+  constexpr int DPL = HD / 8;    // V dims per lane group g
+  constexpr int NV = DPL / 8;    // 16-byte V chunks per lane per position
   __shared__ float sm_m[W][GQ], sm_l[W][GQ];
   __shared__ float sm_acc[W][GQ][HD];
   __shared__ float cta_m[GQ], cta_l[GQ];
@@ -64,104 +80,144 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int kvh = blockIdx.y, b = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int per_round = kAttnCluster * W * kAttnPos;
+  const int first = (rank * W + warp) * kAttnPos;
+  // Positions before *pos were written by earlier steps, not by the kernel
+  // this one waits for: the first two rounds of them are loaded before
+  // griddepcontrol.wait, so their DRAM latency overlaps the previous kernel.
+  // (*pos itself is final before this grid launches: the kernel that advances
+  // it completed before the previous kernel passed its own wait.)
+  const int cs_pre = p.seq ? -1 : b;
+  const int len_pre = p.seq ? 0 : *p.pos;              // prefetchable positions [0, len_pre)
+
+  uint4 kr[2][KQ], vr[2][2][NV];   // per round: K row g; V rows 2t, 2t+1
+  const __half* kb = nullptr;
+  const __half* vb = nullptr;
+  int len = 0;
+  auto load_k = [&](int base, uint4 (&kk)[KQ]) {
+    const int s = min(base + first + g, len - 1);   // clamped: positions past len are masked below
+#pragma unroll
+    for (int q = 0; q < KQ; ++q) kk[q] = *reinterpret_cast<const uint4*>(kb + (size_t)s * HD + (4 * q + t) * 8);
+  };
+  auto load_v = [&](int base, uint4 (&vv)[2][NV]) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int s = min(base + first + 2 * t + e, len - 1);
+#pragma unroll
+      for (int c = 0; c < NV; ++c)
+        vv[e][c] = *reinterpret_cast<const uint4*>(vb + (size_t)s * HD + g * DPL + c * 8);
+    }
+  };
+  auto load_round = [&](int base, int r) {
+    load_k(base, kr[r]);
+    load_v(base, vr[r]);
+  };
+  if (len_pre > 0) {
+    kb = p.k + ((size_t)cs_pre * p.nkv + kvh) * p.S * HD;
+    vb = p.v + ((size_t)cs_pre * p.nkv + kvh) * p.S * HD;
+    len = len_pre;
+    load_round(0, 0);
+    load_round(per_round, 1);
+  }
   pdl_wait();
   pdl_launch_dependents();   // the next kernel's CTAs may start on the SMs this grid leaves idle
   const int cs = p.seq ? *p.seq : b;                   // KV-cache sequence of this query row
-  const int len = *p.pos + 1 + (p.seq ? b : 0);
-  const int per_round = kAttnCluster * W * kAttnPos;
-  const int first = (rank * W + warp) * kAttnPos;
-
-  float qf[GQ][D];
+  len = *p.pos + 1 + (p.seq ? b : 0);
+  kb = p.k + ((size_t)cs * p.nkv + kvh) * p.S * HD;
+  vb = p.v + ((size_t)cs * p.nkv + kvh) * p.S * HD;
+  if (len_pre == 0 || len != len_pre + 1) {
+    load_round(0, 0);   // nothing (or not the expected positions) prefetched
+    load_round(per_round, 1);
+  } else {
+    // only position len - 1 (this step's, written by the previous kernel) is new
 #pragma unroll
-  for (int h = 0; h < GQ; ++h) {
-    const __half* qp = p.q + (size_t)b * p.nq * HD + (size_t)(kvh * GQ + h) * HD + lane * D;
-#pragma unroll
-    for (int d = 0; d < D; ++d) qf[h][d] = __half2float(qp[d]) * p.scale_log2;
-  }
-  float m[GQ], l[GQ], acc[GQ][D];
-#pragma unroll
-  for (int h = 0; h < GQ; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
-#pragma unroll
-    for (int d = 0; d < D; ++d) acc[h][d] = 0.f;
-  }
-  const __half* kb = p.k + ((size_t)cs * p.nkv + kvh) * p.S * HD + lane * D;
-  const __half* vb = p.v + ((size_t)cs * p.nkv + kvh) * p.S * HD + lane * D;
-  using VecT = typename std::conditional<D == 4, uint2, uint32_t>::type;
-  VecT kr[2][kAttnPos], vr[2][kAttnPos];
-  auto load_round = [&](int base, VecT (&kk)[kAttnPos], VecT (&vv)[kAttnPos]) {
-#pragma unroll
-    for (int j = 0; j < kAttnPos; ++j) {
-      const int s = min(base + first + j, len - 1);   // clamped: positions past len are skipped below
-      kk[j] = *reinterpret_cast<const VecT*>(kb + (size_t)s * HD);
-      vv[j] = *reinterpret_cast<const VecT*>(vb + (size_t)s * HD);
+    for (int rr = 0; rr < 2; ++rr) {
+      if (rr * per_round + first + g == len - 1) load_k(rr * per_round, kr[rr]);
+      if (rr * per_round + first + 2 * t == len - 1 || rr * per_round + first + 2 * t + 1 == len - 1)
+        load_v(rr * per_round, vr[rr]);
     }
-  };
-  auto process = [&](int base, const VecT (&kk)[kAttnPos], const VecT (&vv)[kAttnPos]) {
+  }
+  // the queries come from the previous kernel: read after the wait. A
+  // fragments: row g = query head kvh * GQ + g (zero past GQ), the same dim
+  // permutation as K; rows g + 8 are zero.
+  uint32_t qa[KQ][4];
+  {
+    const __half* qp = p.q + (size_t)b * p.nq * HD + (size_t)(kvh * GQ + min(g, GQ - 1)) * HD;
+#pragma unroll
+    for (int q = 0; q < KQ; ++q) {
+      uint4 v = *reinterpret_cast<const uint4*>(qp + (4 * q + t) * 8);
+      if (g >= GQ) v = make_uint4(0, 0, 0, 0);
+      qa[q][0] = v.x;   // k-step 2q:   dims +0,1 / +2,3
+      qa[q][1] = v.y;
+      qa[q][2] = v.z;   // k-step 2q+1: dims +4,5 / +6,7
+      qa[q][3] = v.w;
+    }
+  }
+  float m_r = -INFINITY, l_r = 0.f;   // softmax state of head g (replicated over the row's 4 lanes)
+  float o[DPL][4];
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+
+  auto process = [&](int base, const uint4 (&kk)[KQ], const uint4 (&vv)[2][NV]) {
     const int n = min(kAttnPos, len - (base + first));
     if (n <= 0) return;
-    float dot[kAttnPos][GQ];
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < kAttnPos; ++j) {
-      const __half* kh = reinterpret_cast<const __half*>(&kk[j]);
-#pragma unroll
-      for (int h = 0; h < GQ; ++h) {
-        float a = 0.f;
-#pragma unroll
-        for (int d = 0; d < D; ++d) a = fmaf(qf[h][d], __half2float(kh[d]), a);
-        dot[j][h] = a;
-      }
+    for (int q = 0; q < KQ; ++q) {
+      mma16816(sc, qa[q][0], 0u, qa[q][1], 0u, kk[q].x, kk[q].y);
+      mma16816(sc, qa[q][2], 0u, qa[q][3], 0u, kk[q].z, kk[q].w);
     }
+    // scores of head g at positions 2t, 2t + 1 of the round (log2 domain)
+    float s0 = 2 * t < n ? sc[0] * p.scale_log2 : -INFINITY;
+    float s1 = 2 * t + 1 < n ? sc[1] * p.scale_log2 : -INFINITY;
+    float mx = fmaxf(s0, s1);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m_r, mx);   // finite: position base + first < len
+    const float corr = exp2f(m_r - mn);
+    const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
+    float sum = p0 + p1;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    l_r = l_r * corr + sum;
+    m_r = mn;
+    const uint32_t pa = h2_as_u32(__floats2half2_rn(p0, p1));
+    const uint32_t* v0 = reinterpret_cast<const uint32_t*>(&vv[0][0]);
+    const uint32_t* v1 = reinterpret_cast<const uint32_t*>(&vv[1][0]);
 #pragma unroll
-    for (int j = 0; j < kAttnPos; ++j)
-#pragma unroll
-      for (int h = 0; h < GQ; ++h) dot[j][h] = warp_sum(dot[j][h]);
-#pragma unroll
-    for (int h = 0; h < GQ; ++h) {
-      float mr = m[h];
-#pragma unroll
-      for (int j = 0; j < kAttnPos; ++j)
-        if (j < n) mr = fmaxf(mr, dot[j][h]);
-      const float corr = exp2f(m[h] - mr);
-      l[h] *= corr;
-#pragma unroll
-      for (int d = 0; d < D; ++d) acc[h][d] *= corr;
-#pragma unroll
-      for (int j = 0; j < kAttnPos; ++j) {
-        if (j < n) {
-          const float e = exp2f(dot[j][h] - mr);
-          l[h] += e;
-          const __half* vh = reinterpret_cast<const __half*>(&vv[j]);
-#pragma unroll
-          for (int d = 0; d < D; ++d) acc[h][d] = fmaf(e, __half2float(vh[d]), acc[h][d]);
-        }
-      }
-      m[h] = mr;
+    for (int j = 0; j < DPL; ++j) {
+      o[j][0] *= corr;
+      o[j][1] *= corr;
+      // B[k = position 2t, 2t+1][n = g] for output columns j: dim g * DPL + j of the two rows
+      const uint32_t bv = __byte_perm(v0[j >> 1], v1[j >> 1], (j & 1) ? 0x7632 : 0x5410);
+      mma1688(o[j], pa, 0u, bv);
     }
   };
+  // rounds 0 and 1 are in registers; later rounds load two ahead of use
   const int rounds = (len + per_round - 1) / per_round;
-  load_round(0, kr[0], vr[0]);
   for (int r = 0; r < rounds; r += 2) {
-    if (r + 1 < rounds) load_round((r + 1) * per_round, kr[1], vr[1]);
     process(r * per_round, kr[0], vr[0]);
+    if (r + 2 < rounds) load_round((r + 2) * per_round, 0);
     if (r + 1 >= rounds) break;
-    if (r + 2 < rounds) load_round((r + 2) * per_round, kr[0], vr[0]);
     process((r + 1) * per_round, kr[1], vr[1]);
+    if (r + 3 < rounds) load_round((r + 3) * per_round, 1);
   }
-
-  // warps -> CTA
-#pragma unroll
-  for (int h = 0; h < GQ; ++h) {
-    if (lane == 0) {
-      sm_m[warp][h] = m[h];
-      sm_l[warp][h] = l[h];
+  // per-warp state to shared memory: o[j][0] / o[j][1] = head g, dims
+  // (2t) DPL + j / (2t + 1) DPL + j
+  if (g < GQ) {
+    if (t == 0) {
+      sm_m[warp][g] = m_r;
+      sm_l[warp][g] = l_r;
     }
 #pragma unroll
-    for (int d = 0; d < D; ++d) sm_acc[warp][h][lane * D + d] = acc[h][d];
+    for (int j = 0; j < DPL; ++j) {
+      sm_acc[warp][g][(2 * t) * DPL + j] = o[j][0];
+      sm_acc[warp][g][(2 * t + 1) * DPL + j] = o[j][1];
+    }
   }
   __syncthreads();
+  // warps -> CTA
   for (int i = threadIdx.x; i < GQ * HD; i += W * 32) {
     const int h = i / HD, d = i - h * HD;
     float M = -INFINITY;
@@ -186,17 +242,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   cluster.sync();
   for (int i = rank * (W * 32) + threadIdx.x; i < GQ * HD; i += kAttnCluster * W * 32) {
     const int h = i / HD, d = i - h * HD;
+    // all remote reads issued together (independent distributed-shared-memory loads)
+    float mc[kAttnCluster], lc[kAttnCluster], ac[kAttnCluster];
+#pragma unroll
+    for (int c = 0; c < kAttnCluster; ++c) {
+      mc[c] = *cluster.map_shared_rank(&cta_m[h], c);
+      lc[c] = *cluster.map_shared_rank(&cta_l[h], c);
+      ac[c] = *cluster.map_shared_rank(&cta_acc[h][d], c);
+    }
     float M = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < kAttnCluster; ++c) M = fmaxf(M, *cluster.map_shared_rank(&cta_m[h], c));
+    for (int c = 0; c < kAttnCluster; ++c) M = fmaxf(M, mc[c]);
     float L = 0.f, A = 0.f;
 #pragma unroll
     for (int c = 0; c < kAttnCluster; ++c) {
-      const float mc = *cluster.map_shared_rank(&cta_m[h], c);
-      if (mc == -INFINITY) continue;
-      const float w = exp2f(mc - M);
-      L = fmaf(*cluster.map_shared_rank(&cta_l[h], c), w, L);
-      A = fmaf(*cluster.map_shared_rank(&cta_acc[h][d], c), w, A);
+      const float w = mc[c] == -INFINITY ? 0.f : exp2f(mc[c] - M);   // a CTA with no positions adds nothing
+      L = fmaf(lc[c], w, L);
+      A = fmaf(ac[c], w, A);
     }
     p.out[(size_t)b * p.nq * HD + (size_t)(kvh * GQ + h) * HD + d] = __float2half_rn(A / L);
   }
