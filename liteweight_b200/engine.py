@@ -91,7 +91,7 @@ class PrefillGemmArgs(ctypes.Structure):
 
 
 TC_EPI_RESID, TC_EPI_SWIGLU, TC_EPI_ROPE_KV = 0, 1, 2
-TC_ROWS = 128   # prompt-chunk rows on the tensor-core path
+TC_ROWS = 256   # prompt-chunk rows on the tensor-core path (the GEMM's largest M)
 
 
 class AttentionArgs(ctypes.Structure):
