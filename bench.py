@@ -72,11 +72,8 @@ class ClockSampler:
 
     def __enter__(self):
         try:
-            self.out = open(ROOT / "gpurun_out" / f".clocks_{os.getpid()}.csv", "w") \
-                if (ROOT / "gpurun_out").exists() else None
-            if self.out is None:
-                import tempfile
-                self.out = tempfile.NamedTemporaryFile("w", suffix=".csv", delete=False)
+            import tempfile
+            self.out = tempfile.NamedTemporaryFile("w", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
