@@ -307,16 +307,18 @@ int lw_prefill_sample(int* tokens, unsigned long long* keys, const void* embed, 
  * out[m][n] for the M rows of a prompt chunk (M <= 256) and N weight rows
  * (a multiple of 128): D = act[M][K] . dequant(W)[N][K]^T, fp32 sums in
  * tensor memory (tcgen05.mma kind::f16, 128-row weight tiles, K in blocks of
- * 64 through a 4-stage shared-memory pipeline), then one epilogue:
+ * 64 through a shared-memory ring fed by TMA), then one epilogue:
  *   LW_TC_EPI_RESID:  out = fp16(fp16(y) + residual)   (residual may alias out)
  *   LW_TC_EPI_SWIGLU: gate|up rows interleaved by 8, out[m][i] = silu(gate) * up
  *   LW_TC_EPI_ROPE_KV: q|k|v rows in rope-pair order; RoPE q, k at position
  *                      *pos + m; q -> q_out, k, v -> the cache of sequence *seq
+ *   LW_TC_EPI_F32:    out is fp32 [M][ldo], out = y (a tensor-parallel rank's
+ *                      partial sum of a row-split linear, to be all-reduced)
  * Weights dequantize exactly (fp16(code * scale)) as the GEMV does; the sums
  * differ from it only in order. K a multiple of 64, INT4 or INT8, group size a
  * power of two >= 32 dividing K. No counterpart in the reference (its prompt
  * runs through one HF forward over QuantLinear's dequantize + matmul). */
-enum { LW_TC_EPI_RESID = 0, LW_TC_EPI_SWIGLU = 1, LW_TC_EPI_ROPE_KV = 2 };
+enum { LW_TC_EPI_RESID = 0, LW_TC_EPI_SWIGLU = 1, LW_TC_EPI_ROPE_KV = 2, LW_TC_EPI_F32 = 3 };
 
 typedef struct {
   int bits, epilogue, pdl;
@@ -325,7 +327,7 @@ typedef struct {
   const void* act;       /* fp16 [M][lda] */
   const void* weight;    /* [N][K * bits / 8] */
   const void* scales;    /* fp16 [N][K / group_size] */
-  void* out;             /* fp16 [M][ldo] */
+  void* out;             /* fp16 [M][ldo] (fp32 for LW_TC_EPI_F32) */
   const void* residual;  /* fp16 [M][ldo] (LW_TC_EPI_RESID; may be NULL) */
   int head_dim, n_q_heads, n_kv_heads, max_seq;
   const void* rope_cos;  /* fp16 [max_seq][head_dim] */
@@ -342,6 +344,14 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* args, lw_stream_t stream);
 /* h[m] = RMSNorm(x[m]) * gamma for m < M (modeling_llama.py:63-68 rounding points). */
 int lw_rmsnorm_rows(const void* x, const void* gamma, void* h, int M, int K, float eps, int pdl,
                     lw_stream_t stream);
+
+/* x[m] = fp16(x[m] + fp16(psum[m])) in place (psum fp32 [M][K], the all-reduced
+ * partial sums of a row-split linear), then h[m] = RMSNorm(x[m]) * gamma: the
+ * residual add and norm between the linears of a tensor-parallel prompt chunk,
+ * at the rounding points of the GEMV prologue LW_PRO_RESID_NORM
+ * (modeling_llama.py:63-68 and the residual add of :290-335). */
+int lw_resid_rmsnorm_rows(void* x, const float* psum, const void* gamma, void* h, int M, int K, float eps, int pdl,
+                          lw_stream_t stream);
 
 /* ---- peer memory for the exchanges (setup calls: these allocate, map and
  * synchronise; they are not stream-ordered and must not be graph-captured) */

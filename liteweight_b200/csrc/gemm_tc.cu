@@ -216,7 +216,9 @@ LW_DEV void tma_prefetch_map(const CUtensorMap* map) {
 // activation row m. Every lane of the warp calls it for the same m.
 template <int EPI>
 LW_DEV void tc_epilogue(const TcGemmParams& p, int n, int m, float y, int lane) {
-  if constexpr (EPI == LW_TC_EPI_RESID) {
+  if constexpr (EPI == LW_TC_EPI_F32) {
+    if (m < p.M && n < p.N) reinterpret_cast<float*>(p.out)[(size_t)m * p.ldo + n] = y;
+  } else if constexpr (EPI == LW_TC_EPI_RESID) {
     if (m >= p.M || n >= p.N) return;
     y = r16(y);
     if (p.residual) y = r16(__half2float(p.residual[(size_t)m * p.ldo + n]) + y);
@@ -499,16 +501,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 }
 
 // h[m] = fp16(gamma * fp16(x * rstd)), rstd = 1 / sqrt(mean(x^2) + eps) in fp32.
-__global__ void rmsnorm_rows_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma,
+// With psum, x[m] first becomes fp16(x + fp16(psum)) (written back; the
+// second pass reads the new values, which this block wrote before its barrier).
+__global__ void rmsnorm_rows_kernel(__half* x, const float* __restrict__ psum, const __half* __restrict__ gamma,
                                     __half* __restrict__ h, int K, float eps) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float part[32];
   const int m = blockIdx.x;
-  const __half* xr = x + (size_t)m * K;
+  __half* xr = x + (size_t)m * K;
   float sq = 0.f;
   for (int i = threadIdx.x * 8; i < K; i += blockDim.x * 8) {
-    const uint4 v = ldg_nc(xr + i);
+    uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+    if (psum) {
+      const float4 a = *reinterpret_cast<const float4*>(psum + (size_t)m * K + i);
+      const float4 b = *reinterpret_cast<const float4*>(psum + (size_t)m * K + i + 4);
+      const float ps[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      __half* hv = reinterpret_cast<__half*>(&v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
+      *reinterpret_cast<uint4*>(xr + i) = v;
+    }
     const __half* hv = reinterpret_cast<const __half*>(&v);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -527,7 +540,7 @@ __global__ void rmsnorm_rows_kernel(const __half* __restrict__ x, const __half* 
   __syncthreads();
   const float rstd = 1.0f / sqrtf(part[0] / (float)K + eps);
   for (int i = threadIdx.x * 8; i < K; i += blockDim.x * 8) {
-    uint4 v = ldg_nc(xr + i);
+    uint4 v = *reinterpret_cast<const uint4*>(xr + i);
     const uint4 gm = ldg_nc(gamma + i);
     __half* hv = reinterpret_cast<__half*>(&v);
     const __half* hg = reinterpret_cast<const __half*>(&gm);
@@ -642,6 +655,9 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
     case LW_TC_EPI_SWIGLU:
       if (a->ldo < a->N / 2) return LW_ERR_BAD_SHAPE;
       break;
+    case LW_TC_EPI_F32:
+      if (a->ldo < a->N || !al(a->out, 16)) return LW_ERR_BAD_SHAPE;
+      break;
     case LW_TC_EPI_ROPE_KV:
       if (!a->q_out || !a->k_cache || !a->v_cache || !a->rope_cos || !a->rope_sin || !a->pos || !a->seq)
         return LW_ERR_NULL_POINTER;
@@ -717,22 +733,38 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
   LW_TC(8, LW_TC_EPI_RESID)
   LW_TC(8, LW_TC_EPI_SWIGLU)
   LW_TC(8, LW_TC_EPI_ROPE_KV)
+  LW_TC(4, LW_TC_EPI_F32)
+  LW_TC(8, LW_TC_EPI_F32)
 #undef LW_TC
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
 }
 
-int lw_rmsnorm_rows(const void* x, const void* gamma, void* h, int M, int K, float eps, int pdl,
-                    lw_stream_t stream) {
+namespace {
+int rmsnorm_rows_launch(void* x, const float* psum, const void* gamma, void* h, int M, int K, float eps, int pdl,
+                        lw_stream_t stream) {
   if (!x || !gamma || !h) return LW_ERR_NULL_POINTER;
   if (M <= 0 || K <= 0 || K % 8) return LW_ERR_BAD_SHAPE;
-  if (!al(x, 16) || !al(gamma, 16) || !al(h, 16)) return LW_ERR_ALIGNMENT;
+  if (!al(x, 16) || !al(gamma, 16) || !al(h, 16) || (psum && !al(psum, 16))) return LW_ERR_ALIGNMENT;
   cudaGetLastError();
   cudaError_t e = lw_launch(lw::rmsnorm_rows_kernel, dim3(M), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
-                            pdl != 0, static_cast<const __half*>(x), static_cast<const __half*>(gamma),
+                            pdl != 0, static_cast<__half*>(x), psum, static_cast<const __half*>(gamma),
                             static_cast<__half*>(h), K, eps);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
+}
+}  // namespace
+
+int lw_rmsnorm_rows(const void* x, const void* gamma, void* h, int M, int K, float eps, int pdl,
+                    lw_stream_t stream) {
+  // x is only read when psum is NULL
+  return rmsnorm_rows_launch(const_cast<void*>(x), nullptr, gamma, h, M, K, eps, pdl, stream);
+}
+
+int lw_resid_rmsnorm_rows(void* x, const float* psum, const void* gamma, void* h, int M, int K, float eps, int pdl,
+                          lw_stream_t stream) {
+  if (!psum) return LW_ERR_NULL_POINTER;
+  return rmsnorm_rows_launch(x, psum, gamma, h, M, K, eps, pdl, stream);
 }
 
 }  // extern "C"

@@ -344,7 +344,7 @@ const char* lw_status_string(int status) {
   }
 }
 
-int lw_abi_version(void) { return 110; }
+int lw_abi_version(void) { return 111; }
 
 int lw_take_device_error(void) {
   const int mine = lw_tu_take_error();

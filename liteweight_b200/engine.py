@@ -90,7 +90,7 @@ class PrefillGemmArgs(ctypes.Structure):
     ]
 
 
-TC_EPI_RESID, TC_EPI_SWIGLU, TC_EPI_ROPE_KV = 0, 1, 2
+TC_EPI_RESID, TC_EPI_SWIGLU, TC_EPI_ROPE_KV, TC_EPI_F32 = 0, 1, 2, 3
 TC_ROWS = 256   # prompt-chunk rows on the tensor-core path (the GEMM's largest M)
 
 
@@ -114,6 +114,7 @@ nat.register("lw_prefill_advance", [c_void_p] * 2 + [c_int] * 2 + [c_void_p])
 nat.register("lw_prefill_sample", [c_void_p] * 8 + [c_int] * 4 + [c_void_p])
 nat.register("lw_prefill_gemm", [ctypes.POINTER(PrefillGemmArgs), c_void_p])
 nat.register("lw_rmsnorm_rows", [c_void_p] * 3 + [c_int] * 2 + [c_float, c_int, c_void_p])
+nat.register("lw_resid_rmsnorm_rows", [c_void_p] * 4 + [c_int] * 2 + [c_float, c_int, c_void_p])
 nat.register("lw_peer_alloc", [c_size_t, ctypes.POINTER(c_void_p)])
 nat.register("lw_peer_free", [c_void_p])
 nat.register("lw_peer_handle_size", [], c_size_t)
@@ -289,12 +290,12 @@ def prefill_rows(spec: LlamaSpec, tp_size: int = 1, limit: int = 32) -> int:
     return max(1, min(limit, rows))
 
 
-def tc_supported(spec: LlamaSpec) -> bool:
-    """The tensor-core prompt GEMM takes every linear of the layer: weight rows
-    in whole 128-row tiles, K in whole 64-element blocks."""
-    hd = spec.head_dim
-    ns = [(spec.n_heads + 2 * spec.n_kv_heads) * hd, spec.hidden, 2 * spec.inter]
-    ks = [spec.hidden, spec.n_heads * hd, spec.inter]
+def tc_supported(spec: LlamaSpec, tp_size: int = 1) -> bool:
+    """The tensor-core prompt GEMM takes every linear of a rank's layer shard:
+    weight rows in whole 128-row tiles, K in whole 64-element blocks."""
+    hd, nq, nkv, inter = spec.head_dim, spec.n_heads // tp_size, spec.n_kv_heads // tp_size, spec.inter // tp_size
+    ns = [(nq + 2 * nkv) * hd, spec.hidden, 2 * inter]
+    ks = [spec.hidden, nq * hd, inter]
     return (spec.bits in (4, 8) and spec.group_size >= 32 and all(n % 128 == 0 for n in ns)
             and all(k % 64 == 0 for k in ks))
 
@@ -432,10 +433,11 @@ class DecodeEngine:
         self.seq = torch.zeros(1, dtype=torch.int32, device=dev)   # sequence of the prompt chunk in flight
         self.tokens = torch.full((max_seq + 1, batch), -1, dtype=torch.int32, device=dev)
         self.step_count = torch.zeros(1, dtype=torch.int32, device=dev)
-        # decode buffers (row = sequence) and prompt-chunk buffers (row = position). With one
-        # rank, prompt chunks of TC_ROWS positions run their linears on the tensor cores
-        # (lw_prefill_gemm); with tensor parallelism they run the fused GEMVs and exchanges.
-        self.use_tc = tp_size == 1 and tc_supported(spec)
+        # decode buffers (row = sequence) and prompt-chunk buffers (row = position). Prompt
+        # chunks of TC_ROWS positions run their linears on the tensor cores (lw_prefill_gemm;
+        # with tensor parallelism the row-split linears' fp32 partials are all-reduced by NCCL
+        # between the GEMMs); shapes the GEMM does not tile run the fused GEMVs and exchanges.
+        self.use_tc = tc_supported(spec, tp_size)
         self.prefill_rows = TC_ROWS if self.use_tc else prefill_rows(spec, tp_size)
         self.dec = self._buffers(batch)
         self.pf = self._buffers(self.prefill_rows)
@@ -443,7 +445,8 @@ class DecodeEngine:
         self.act, self.logits, self.psum, self.keys = self.dec.act, self.dec.logits, self.dec.psum, self.dec.keys
         self.exchange = None
         if tp_size > 1 and exchange == "peer":
-            self.exchange = PeerExchange(tp_group, tp_rank, tp_size, max(batch, self.prefill_rows), H,
+            self.exchange = PeerExchange(tp_group, tp_rank, tp_size,
+                                         max(batch, prefill_rows(spec, tp_size) if self.use_tc else self.prefill_rows), H,
                                          2 * len(layers), dev, exchange_timeout_s)
             self.step_count = self.exchange.step
         self._build_calls()
@@ -576,12 +579,18 @@ class DecodeEngine:
         return calls, gemv_args
 
     def _make_tc_calls(self, bufs, final: bool):
-        """A prompt chunk on the tensor cores (one rank): per layer RMSNorm rows,
-        the q|k|v GEMM (RoPE + KV append), attention, the o GEMM (+ residual,
-        in place), RMSNorm, the gate|up GEMM (SwiGLU), the down GEMM (+ residual);
-        the last chunk then runs the lm_head GEMV on its last row only."""
+        """A prompt chunk on the tensor cores: per layer RMSNorm rows, the q|k|v
+        GEMM (RoPE + KV append), attention, the o GEMM (+ residual, in place),
+        RMSNorm, the gate|up GEMM (SwiGLU), the down GEMM (+ residual); the last
+        chunk then runs the lm_head GEMV on its last row only. With tensor
+        parallelism the o and down GEMMs write this rank's fp32 partial sums,
+        NCCL all-reduces them, and lw_resid_rmsnorm_rows adds them to the
+        residual before the next norm; the lm_head's vocabulary-shard argmax keys
+        are max-reduced the same way, so prefill_sample reads local keys."""
         sp, H, hd, rows = self.spec, self.spec.hidden, self.spec.head_dim, bufs.rows
         seq = self.seq.data_ptr()
+        tp = self.tp_size > 1
+        bufs.sample_xin = None
         calls = [("prefill_embed", bufs, "embed")]
 
         def tc(epi, N, K, w, s_, act, lda, out, ldo, **kw):
@@ -592,8 +601,18 @@ class DecodeEngine:
                 setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
             return ("tcgemm", a, "tc")
 
+        def norm(gamma, pending):
+            if pending:
+                return ("resid_rmsnorm", (bufs.x, bufs.psum, gamma, bufs.h, rows), "norm")
+            return ("rmsnorm", (bufs.x, gamma, bufs.h, rows), "norm")
+
+        def row_split(w, s_, act, K):
+            if not tp:
+                return [tc(TC_EPI_RESID, H, K, w, s_, act, K, bufs.x, H, residual=bufs.x)]
+            return [tc(TC_EPI_F32, H, K, w, s_, act, K, bufs.psum, H), ("allreduce", bufs.psum, "allreduce")]
+
         for li, L in enumerate(self.layers):
-            calls.append(("rmsnorm", (bufs.x, L.in_norm, bufs.h, rows), "norm"))
+            calls.append(norm(L.in_norm, tp and li > 0))
             calls.append(tc(TC_EPI_ROPE_KV, (self.nq + 2 * self.nkv) * hd, H, L.qkv_w, L.qkv_s, bufs.h, H, bufs.q,
                             self.nq * hd, head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv, max_seq=self.S,
                             rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, seq=seq, q_out=bufs.q,
@@ -603,21 +622,23 @@ class DecodeEngine:
                                batch=rows, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
                                pdl=self.pdl, prefill_seq=seq)
             calls.append(("attn", at, "attn"))
-            calls.append(tc(TC_EPI_RESID, H, self.nq * hd, L.o_w, L.o_s, bufs.attn, self.nq * hd, bufs.x, H,
-                            residual=bufs.x))
-            calls.append(("rmsnorm", (bufs.x, L.post_norm, bufs.h, rows), "norm"))
+            calls += row_split(L.o_w, L.o_s, bufs.attn, self.nq * hd)
+            calls.append(norm(L.post_norm, tp))
             calls.append(tc(TC_EPI_SWIGLU, 2 * self.inter, H, L.gu_w, L.gu_s, bufs.h, H, bufs.act, self.inter))
-            calls.append(tc(TC_EPI_RESID, H, self.inter, L.d_w, L.d_s, bufs.act, self.inter, bufs.x, H,
-                            residual=bufs.x))
+            calls += row_split(L.d_w, L.d_s, bufs.act, self.inter)
         if not final:
             calls.append(("prefill_advance", rows, "advance"))
             return calls, []
+        if tp:   # the last down partial joins the residual stream (h is not used)
+            calls.append(norm(self.final_norm, True))
         last = bufs.x.data_ptr() + 2 * (rows - 1) * H
         a = self._gemv(1, bits=16, prologue=PRO_NORM, epilogue=EPI_ARGMAX, N=self.vshard, K=H, group_size=H,
                        weight=self.lm_head, gamma=self.final_norm, act=last, lda=H,
                        out=bufs.logits.data_ptr() + 2 * (rows - 1) * self.vshard, ldo=self.vshard,
-                       argmax_keys=bufs.keys.data_ptr() + 8 * (rows - 1), argmax_offset=0)
+                       argmax_keys=bufs.keys.data_ptr() + 8 * (rows - 1), argmax_offset=self.tp_rank * self.vshard)
         calls.append(("gemv", a, "lm_head"))
+        if tp:
+            calls.append(("allreduce_max", bufs.keys, "allreduce"))
         calls.append(("prefill_sample", bufs, "sample"))
         return calls, [a]
 
@@ -681,6 +702,11 @@ class DecodeEngine:
                 x, gamma, h, rows = a
                 nat.check("lw_rmsnorm_rows", lib.lw_rmsnorm_rows(x.data_ptr(), gamma.data_ptr(), h.data_ptr(), rows,
                                                                  self.spec.hidden, self.spec.eps, self.pdl, s))
+            elif kind == "resid_rmsnorm":
+                x, psum, gamma, h, rows = a
+                nat.check("lw_resid_rmsnorm_rows", lib.lw_resid_rmsnorm_rows(
+                    x.data_ptr(), psum.data_ptr(), gamma.data_ptr(), h.data_ptr(), rows, self.spec.hidden,
+                    self.spec.eps, self.pdl, s))
             elif kind == "prefill_embed":
                 nat.check("lw_prefill_embed", lib.lw_prefill_embed(
                     self.tokens.data_ptr(), self.embed.data_ptr(), a.x.data_ptr(), self.pos.data_ptr(),
@@ -691,7 +717,8 @@ class DecodeEngine:
             elif kind == "prefill_sample":
                 nat.check("lw_prefill_sample", lib.lw_prefill_sample(
                     self.tokens.data_ptr(), a.keys.data_ptr(), self.embed.data_ptr(), self.x_in.data_ptr(),
-                    self.pos.data_ptr(), self.step_count.data_ptr(), self.seq.data_ptr(), self.sample_xin, a.rows,
+                    self.pos.data_ptr(), self.step_count.data_ptr(), self.seq.data_ptr(),
+                    getattr(a, "sample_xin", self.sample_xin), a.rows,
                     self.B, self.spec.hidden, self.pdl, s))
 
     def _sample(self, s):
@@ -732,7 +759,7 @@ class DecodeEngine:
     # -------------------------------------------------------------- prefill
     def _prefill_calls(self, rows: int, final: bool):
         key = (rows, final)
-        if self.exchange is not None:
+        if self.exchange is not None and not self.use_tc:
             assert rows <= self.exchange.rows, "prompt chunk larger than the exchange buffers"
         if key not in self.prefill_calls:
             bufs = self.pf if rows == self.pf.rows else self._buffers(rows)

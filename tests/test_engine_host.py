@@ -98,3 +98,13 @@ def test_prefill_rows_fit_shared_memory():
     assert [E.down_rows(s8, tp) for tp in (1, 2, 4)] == [7, 15, 31]
     s1 = E.LlamaSpec(**E.LLAMA_3_2_1B, bits=8)
     assert E.prefill_rows(s1) == 32 and E.down_rows(s1) == 13
+
+
+def test_tc_supported_per_rank_shards():
+    """The tensor-core prompt path takes a rank's shard when every shard's
+    linear tiles (128-row weight tiles, K in 64-element blocks)."""
+    from liteweight_b200 import engine as E
+    spec = E.LlamaSpec(**E.LLAMA_3_8B, bits=4, group_size=128)
+    assert all(E.tc_supported(spec, tp) for tp in (1, 2, 4, 8))
+    odd = E.LlamaSpec(**{**E.LLAMA_3_8B, "inter": 14336 + 32}, bits=4, group_size=128)
+    assert not E.tc_supported(odd, 1)

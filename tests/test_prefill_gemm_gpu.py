@@ -151,3 +151,40 @@ def test_rmsnorm_rows():
     ref = ol.rmsnorm(x, gamma, 1e-5).astype(np.float32)
     got = h.float().cpu().numpy()
     assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max()
+
+
+def test_resid_rmsnorm_rows():
+    """x = fp16(x + fp16(psum)) in place, then RMSNorm of the new x (the
+    tensor-parallel prompt chunk's residual add and norm)."""
+    from liteweight_b200 import _native as nat
+    M, K = 7, 4096
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    psum = rng.standard_normal((M, K)).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    xt, pt, gt = (torch.from_numpy(a).to(DEV) for a in (x, psum, gamma))
+    h = torch.zeros(M, K, device=DEV).half()
+    nat.check("norm", nat.lib().lw_resid_rmsnorm_rows(xt.data_ptr(), pt.data_ptr(), gt.data_ptr(), h.data_ptr(),
+                                                      M, K, 1e-5, 1, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    x_new = (x.astype(np.float32) + psum.astype(np.float16).astype(np.float32)).astype(np.float16)
+    assert np.array_equal(xt.cpu().numpy(), x_new)
+    ref = ol.rmsnorm(x_new, gamma, 1e-5).astype(np.float32)
+    got = h.float().cpu().numpy()
+    assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M,K", [(5, 256), (128, 2048)])
+def test_gemm_f32_partial(bits, M, K):
+    """LW_TC_EPI_F32: the fp32 sums of a row-split linear (a tensor-parallel
+    rank's partial), before any fp16 rounding."""
+    N = 256
+    q, s, deq = _weights(bits, N, K, 128, seed=11 + M)
+    gen = torch.Generator(device=DEV).manual_seed(M)
+    act = torch.randn(M, K, generator=gen, device=DEV).half()
+    out = torch.full((M, N), float("nan"), device=DEV)
+    _run(bits=bits, epilogue=3, M=M, N=N, K=K, group_size=128, lda=K, ldo=N, act=act, weight=q, scales=s, out=out)
+    ref = act.float() @ deq.float().T
+    err = (out - ref).abs().max().item()
+    assert err <= 1e-3 * ref.abs().max().item(), err
