@@ -73,14 +73,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   constexpr int KQ = HD / 32;    // 16-byte K chunks per lane per position (2 k-steps each)
   constexpr int DPL = HD / 8;    // V dims per lane group g
   constexpr int NV = DPL / 8;    // 16-byte V chunks per lane per position
+  // per-warp partial outputs: head h, dim d at h * SAS + d + d / 32, so the
+  // fragment stores (lanes = heads x 32-dim strides) fall in distinct banks
+  constexpr int SAS = HD + HD / 32 + 4;
   __shared__ float sm_m[W][GQ], sm_l[W][GQ];
-  __shared__ float sm_acc[W][GQ][HD];
+  __shared__ float sm_acc[W][GQ * SAS];
   __shared__ float cta_m[GQ], cta_l[GQ];
   __shared__ float cta_acc[GQ][HD];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  auto acc_at = [](int h, int d) { return h * SAS + d + (d >> 5); };
   const int per_round = kAttnCluster * W * kAttnPos;
   const int first = (rank * W + warp) * kAttnPos;
   // Positions before *pos were written by earlier steps, not by the kernel
@@ -212,8 +216,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
     }
 #pragma unroll
     for (int j = 0; j < DPL; ++j) {
-      sm_acc[warp][g][(2 * t) * DPL + j] = o[j][0];
-      sm_acc[warp][g][(2 * t + 1) * DPL + j] = o[j][1];
+      sm_acc[warp][acc_at(g, (2 * t) * DPL + j)] = o[j][0];
+      sm_acc[warp][acc_at(g, (2 * t + 1) * DPL + j)] = o[j][1];
     }
   }
   __syncthreads();
@@ -229,7 +233,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
       for (int w = 0; w < W; ++w) {
         const float c = exp2f(sm_m[w][h] - M);
         L = fmaf(sm_l[w][h], c, L);
-        A = fmaf(sm_acc[w][h][d], c, A);
+        A = fmaf(sm_acc[w][acc_at(h, d)], c, A);
       }
     }
     cta_acc[h][d] = A;
