@@ -94,7 +94,8 @@ int lw_gemm_w4a16(const void* act, const void* qweight, const void* scales, cons
  * scratch is a fixed 4 MiB array inside the library, held on every GPU that
  * loads it until exit; problems needing more (lw_gemm_workspace_size) return
  * LW_ERR_WORKSPACE. The first call on a device looks the array up, so make
- * it before any stream capture. All calls share the array: calls that
+ * it before any stream capture; the address is cached for the process, so do
+ * not call it after cudaDeviceReset. All calls share the array: calls that
  * overlap on the GPU race. */
 int lw_gemm_w4a16_noalloc(const void* act, const void* qweight, const void* scales, const void* bias,
                           void* out, int M, int N, int K, int group_size, lw_stream_t stream);

@@ -103,17 +103,38 @@ def launch_count() -> int:
 
 
 _workspaces: dict = {}
+_retired: list = []
+_unzeroed: set = set()   # workspaces allocated under stream capture, not yet zeroed
 
 
 def workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     """Zero-initialised scratch for the matmul entry points, one per (device,
     stream) so concurrent streams never share it; grown on demand. The kernels
-    leave it zeroed after every call."""
+    leave it zeroed after every call.
+
+    A workspace that is replaced by a larger one is never freed: a CUDA graph
+    captured earlier holds its address (split-tile counters and partial-sum
+    slots) and keeps writing there on every replay, so the memory must not go
+    back to torch's allocator for another tensor to own. Growth is geometric,
+    so the retired blocks add up to less than the live one."""
     key = (device.index, stream)
     ws = _workspaces.get(key)
+    capturing = torch.cuda.is_current_stream_capturing()
     if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        size = max(nbytes, 1 << 20, 2 * ws.numel() if ws is not None else 0)
+        if ws is not None:
+            _retired.append(ws)
+        # Under stream capture the zero fill is recorded into the graph, not
+        # run: the block is zeroed again by the first eager call after it.
+        ws = torch.zeros(size, dtype=torch.uint8, device=device)
         _workspaces[key] = ws
+        if capturing:
+            _unzeroed.add(key)
+        else:
+            _unzeroed.discard(key)
+    elif key in _unzeroed and not capturing:
+        ws.zero_()
+        _unzeroed.discard(key)
     return ws
 
 

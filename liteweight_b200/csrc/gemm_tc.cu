@@ -462,7 +462,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   if (warp < kTcDeqWarps) {
     pdl_wait();   // the residual input comes from a previous kernel
     uint32_t done = 1;
-    if (lane == 0) done = mbar_wait_bounded(smem_u32(&bar_done), 0, kTcWaitNs) ? 1u : 0u;
+    if (lane == 0) {
+      done = mbar_wait_bounded(smem_u32(&bar_done), 0, kTcWaitNs) ? 1u : 0u;
+      if (!done) abort_s = 1;   // this CTA's partial tile will be missing: the cluster must know
+    }
     const bool ok = __shfl_sync(0xffffffffu, done, 0) && !abort_s;
     tc_fence_after();
     if (ok) {
@@ -484,8 +487,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   if (p.splits > 1) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();   // every partial tile is in its CTA's shared memory
-    if (warp < kTcDeqWarps && !abort_s) {
+    cluster.sync();   // every partial tile (and every CTA's abort flag) is in its CTA's shared memory
+    // A CTA that gave up on a wait left its partial tile unwritten: if any
+    // did, no CTA combines (the error flag is set; the outputs keep their
+    // previous contents instead of sums built from stale shared memory).
+    bool any_abort = false;
+    for (int q = 0; q < p.splits; ++q)
+      any_abort |= *static_cast<volatile int*>(cluster.map_shared_rank(const_cast<int*>(&abort_s), q)) != 0;
+    if (warp < kTcDeqWarps && !any_abort) {
       const int cw = p.Mpad / p.splits, m0 = split * cw;
       for (int j = ch; j < cw; j += kChunkWarps) {
         float y = 0.f;

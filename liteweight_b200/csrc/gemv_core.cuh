@@ -513,6 +513,7 @@ LW_DEV void flush_tile(const StreamParams& p, int tile, int seg_c0, int end_c, i
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) mine[mt] = make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
   __threadfence();
+  __syncwarp();   // every lane's slot is stored and fenced before lane 0 counts the warp in
   int old = 0;
   if (lane == 0) old = atomicAdd(p.counters + tile, 1);
   old = __shfl_sync(0xffffffffu, old, 0);

@@ -7,11 +7,16 @@
 // outputs. For them, lw_gemm_w4a16_noalloc runs the same kernel with its
 // scratch in a fixed array that lives inside this library.
 //
-// The array is kNoallocScratchBytes (4 MiB) per GPU, created when the library
-// is loaded and held by every GPU that loads it until the process exits.
-// Problems whose scratch need exceeds it are rejected with LW_ERR_WORKSPACE.
+// The array is kNoallocScratchBytes (4 MiB) per GPU. It comes into existence
+// on a device when the library's device code is first loaded there (with
+// lazy module loading, at the first kernel launch or symbol lookup) and is
+// held by that GPU until the process exits. Problems whose scratch need
+// exceeds it are rejected with LW_ERR_WORKSPACE, before anything is enqueued.
 // The first call on a device looks the array's device address up
 // (cudaGetSymbolAddress), so make that first call before any stream capture.
+// The address is cached per device for the life of the process: do not use
+// this entry point after cudaDeviceReset (or anything else that destroys the
+// device's primary context) in the same process.
 // Every call clears the array's counter region on the stream before the
 // kernel runs; all calls share the array, so calls that overlap on the GPU
 // (different streams, or different host threads) race and must not be issued.
@@ -50,8 +55,14 @@ int noalloc_scratch(void** out) {
 
 extern "C" int lw_gemm_w4a16_noalloc(const void* act, const void* qweight, const void* scales, const void* bias,
                                      void* out, int M, int N, int K, int group_size, lw_stream_t stream) {
+  // Validate everything lw_gemm_w4a16 would reject before the counter clear
+  // below is enqueued, so a rejected call leaves the stream untouched.
   if (!act || !qweight || !scales || !out) return LW_ERR_NULL_POINTER;
   if (M <= 0 || N <= 0 || K <= 0 || K % 2) return LW_ERR_BAD_SHAPE;
+  if (group_size <= 0 || K % group_size) return LW_ERR_BAD_GROUP;
+  if (reinterpret_cast<uintptr_t>(act) % 2 || reinterpret_cast<uintptr_t>(out) % 2 ||
+      reinterpret_cast<uintptr_t>(scales) % 2 || (bias && reinterpret_cast<uintptr_t>(bias) % 2))
+    return LW_ERR_ALIGNMENT;
   void* ws = nullptr;
   const int st = noalloc_scratch(&ws);
   if (st) return st;

@@ -646,6 +646,9 @@ class DecodeEngine:
         """One workspace shared by the sequential GEMVs of every call list."""
         need = max([int(nat.lib().lw_fused_gemv_workspace_size(ctypes.byref(a))) for a in gemv_args] + [256])
         if getattr(self, "workspace", None) is None or self.workspace.numel() < need:
+            if getattr(self, "workspace", None) is not None:
+                # a graph captured before may still write there: never hand it back
+                self._retired_workspaces = getattr(self, "_retired_workspaces", []) + [self.workspace]
             self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
             for a in getattr(self, "_all_gemv_args", []):
                 a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()

@@ -1,8 +1,9 @@
 """Generate the golden fixtures in this folder from the reference itself.
 
-Run in a container where the liteweight sources are present:
+Run where the liteweight sources are present, giving their root directory
+(the one holding ``liteweight/``):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference-root>
 
 It imports the reference's ``liteweight.quantize`` and ``liteweight.serialize``
 and the installed ``transformers`` (5.5.0) ``LlamaForCausalLM``, and writes:
@@ -182,4 +183,6 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference-root>")
+    main(sys.argv[1])

@@ -336,3 +336,47 @@ def test_workspace_reuse_across_shapes():
         act = rng.standard_normal((M, K)).astype(np.float16)
         got = run_quant(act, q, s, 128, bits)
         check_rows(got, oq.packed_matmul(act, q, s, 128, bits), f"reuse int{bits} {M}x{K}x{N}")
+
+
+def test_graph_survives_workspace_growth():
+    """A graph captured with a small shape keeps its workspace after a larger
+    shape grows the stream's workspace: replaying it afterwards still matches
+    the oracle, and the larger call's output is right too."""
+    from liteweight_b200 import _native as nat
+    k = kern()
+    rng = np.random.default_rng(23)
+    s_ = torch.cuda.Stream()
+    with torch.cuda.stream(s_):
+        key = (torch.device(DEV).index or 0, s_.cuda_stream)
+        old = nat._workspaces.pop(key, None)   # start this stream from a small workspace
+        if old is not None:
+            nat._retired.append(old)
+        q1, sc1 = quantized(512, 4096, 128, 4, seed=31)     # M=1, K=4096: a split-tile plan
+        act1 = rng.standard_normal((1, 4096)).astype(np.float16)
+        a1 = torch.from_numpy(act1).to(DEV)
+        qt1, st1 = torch.from_numpy(q1).to(DEV), torch.from_numpy(sc1).to(DEV)
+        need1 = int(nat.lib().lw_gemm_workspace_size(4, 1, 512, 4096))
+        assert need1 > 0
+        k.matmul_int4(a1, qt1, st1)
+        torch.cuda.synchronize()
+        small_ws = nat._workspaces[key].data_ptr()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s_):
+            out1 = k.matmul_int4(a1, qt1, st1)
+        # a much larger split-tile problem grows (replaces) the stream's workspace
+        q2, sc2 = quantized(28672, 4096, 128, 4, seed=32)
+        act2 = rng.standard_normal((1, 4096)).astype(np.float16)
+        big = k.matmul_int4(torch.from_numpy(act2).to(DEV), torch.from_numpy(q2).to(DEV),
+                            torch.from_numpy(sc2).to(DEV))
+        torch.cuda.synchronize()
+        assert nat._workspaces[key].data_ptr() != small_ws, "the larger call did not grow the workspace"
+        # fill freshly allocated memory with garbage: if the retired block had
+        # been handed back, these tensors could own it
+        junk = [torch.full((1 << 20,), 255, dtype=torch.uint8, device=DEV) for _ in range(8)]
+        for _ in range(3):
+            out1.fill_(0)
+            g.replay()
+        torch.cuda.synchronize()
+        del junk
+    check_rows(out1, oq.packed_matmul(act1, q1, sc1, 128, 4), "graph replay after workspace growth")
+    check_rows(big, oq.packed_matmul(act2, q2, sc2, 128, 4), "the call that grew the workspace")

@@ -7,9 +7,12 @@ the scratch it uses to combine weight tiles split between warps. The
 no-allocation entry point keeps that scratch in a fixed array inside the
 library. This test calls it through the C ABI twice in a row, on a shape whose
 tiles are split (so the array is used), and checks each result against the
-regular entry point given a torch-allocated workspace, within the row-scaled
-tolerance of the other kernel tests. It also checks that a problem needing
-more scratch than the array holds is rejected.
+regular entry point given a torch-allocated workspace: both run the same plan
+and kernel, so the outputs must be bit-identical; one comparison against the
+oracle (dequantize, fp32 matmul) within the row-scaled tolerance of the other
+kernel tests guards both. It also checks that a problem needing more scratch
+than the array holds is rejected, and that a bad group size is rejected
+before anything is enqueued.
 
 The file is named to be collected last, so a run that stops at the first
 failure has run every other test before this one.
@@ -59,10 +62,11 @@ def test_noalloc_matches_regular_entry_point_twice(lib):
         lib.call("lw_gemm_w4a16", act.data_ptr(), qt.data_ptr(), st.data_ptr(), None, ref.data_ptr(),
                  M, N, K, 128, ws.data_ptr(), need, stream)
         torch.cuda.synchronize()
-        g, r = got.float().cpu().numpy(), ref.float().cpu().numpy()
+        g = got.float().cpu().numpy()
         assert np.isfinite(g).all(), call
-        tol = oq.row_tolerance(r)
-        assert np.all(np.abs(g - r) <= tol), (call, float(np.abs(g - r).max()))
+        assert torch.equal(got, ref), (call, float((got.float() - ref.float()).abs().max()))
+        o = oq.packed_matmul(act.cpu().numpy(), q, s, 128, 4).astype(np.float32)
+        assert np.all(np.abs(g - o) <= oq.row_tolerance(o)), (call, float(np.abs(g - o).max()))
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(lib):
@@ -75,3 +79,10 @@ def test_noalloc_rejects_problems_beyond_its_scratch(lib):
             assert status == 7, status            # LW_ERR_WORKSPACE
             return
     pytest.skip("no candidate shape needs more scratch than the array on this device")
+
+
+def test_noalloc_rejects_bad_group_before_enqueueing(lib):
+    # K % group_size != 0: rejected with LW_ERR_BAD_GROUP; pointers are never touched
+    status = lib.lib().lw_gemm_w4a16_noalloc(0x1000, 0x1000, 0x1000, None, 0x1000, 1, 512, 8192, 96,
+                                             torch.cuda.current_stream().cuda_stream)
+    assert status == 3, status                    # LW_ERR_BAD_GROUP
