@@ -22,9 +22,16 @@ Prints ONE JSON line (rank 0). Workloads:
   fp16 scales + activation + output over time). Multi-GPU: independent
   replicas (``scaling: weak``). A per-M sweep (M = 1..256) is reported beside it.
 
+The default decode line also carries (one GPU) a ``gemv`` object with the
+same M = 1 figures, the single-QuantLinear W8A16 case (K = 2048, N = 8192,
+per-output-channel scales, M = 1 and 16), the 8B gate|up shape and the
+GB/s-vs-M sweep, and a ``parity`` object: the greedy ids of the timed
+configuration and the first decode steps' logits checked against a
+teacher-forced fp32 torch restatement of the same packed weights.
+
 ``--impl reference`` times the reference's CPU path for the same workload
-(dequantize the packed weights, fp32 matmul, fp16 result - restated by the
-numpy oracle) on the host cores, rank 0 only, on a bounded sample.
+(dequantize the packed weights, fp32 matmul, fp16 result - restated with
+torch tensor ops by oracle/torch_cpu.py) on the host cores, rank 0 only.
 """
 
 from __future__ import annotations
@@ -46,6 +53,8 @@ sys.path.insert(0, str(ROOT))
 
 GEMV_SHAPES = [(2048, 2048), (2048, 512), (2048, 8192), (8192, 2048)]   # (K, N)
 GROUP = 128
+CONFIG1 = (8, 2048, 8192, 2048)   # bits, K, N, G: one W8A16 QuantLinear with per-output-channel scales
+GATE_UP_8B = (4, 4096, 28672, 128)
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -136,7 +145,7 @@ class Dist:
         if self.world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=300))
             self.pg = dist
 
     def barrier(self, device=None):
@@ -169,9 +178,9 @@ class Dist:
 
 # ----------------------------------------------------------------- GEMV workload
 
-def gemv_bytes(M: int, K: int, N: int, bits: int) -> int:
+def gemv_bytes(M: int, K: int, N: int, bits: int, group: int = GROUP) -> int:
     from liteweight_b200.perf import quant_matmul_workload
-    return quant_matmul_workload(M, K, N, bits, GROUP).bytes_moved
+    return quant_matmul_workload(M, K, N, bits, group).bytes_moved
 
 
 def capture_graph(fn):
@@ -208,69 +217,105 @@ class GemvWorkload:
     metric = "dequant-GEMV HBM GB/s (M=1, Llama-3.2-1B linear shapes, INT4+INT8 G128)"
     unit = "GB/s"
 
-    def __init__(self, device, seed: int = 0):
+    def __init__(self, device, seed: int = 0, extras: bool = True):
         import torch
         from liteweight_b200 import _native as nat
         self.torch, self.nat, self.dev = torch, nat, device
         self.M = 1
         gen = torch.Generator(device=device).manual_seed(seed)
-        self.items = [(bits, K, N) for bits in (4, 8) for K, N in GEMV_SHAPES]   # (bits, K, N)
-        step_w = sum(N * K * b // 8 for b, K, N in self.items)
-        # weight copies: one rotation is more than twice the L2
+        # (bits, K, N, G): the step's 8 GEMVs, then the extra cases timed beside it
+        self.items = [(bits, K, N, GROUP) for bits in (4, 8) for K, N in GEMV_SHAPES]
+        self.n_step = len(self.items)
+        if extras:
+            self.items += [CONFIG1, GATE_UP_8B]
+        step_w = sum(N * K * b // 8 for b, K, N, _ in self.items[:self.n_step])
+        # weight copies of the step's GEMVs: one rotation is more than twice the L2
         self.R = max(3, -(-2 * L2_BYTES // step_w))
-        self.weights = []   # [copy][item] -> (q, s)
-        for _ in range(self.R):
+        self.weights = []   # [item][copy] -> (q, s)
+        for i, (bits, K, N, G) in enumerate(self.items):
             per = []
-            for bits, K, N in self.items:
+            for r in range(self.copies_for(i)):
                 if bits == 4:
                     q = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=device, generator=gen)
                 else:
                     q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=device, generator=gen)
-                s = (torch.rand(N, K // GROUP, device=device, generator=gen) * 2e-3 + 1e-4).half()
+                s = (torch.rand(N, K // G, device=device, generator=gen) * 2e-3 + 1e-4).half()
                 per.append((q, s))
             self.weights.append(per)
         self.acts = {K: torch.randn(256, K, dtype=torch.float16, device=device, generator=gen)
-                     for K in {K for _, K, _ in self.items}}
+                     for K in {it[1] for it in self.items}}
         self.outs = {N: torch.empty(256, N, dtype=torch.float16, device=device)
-                     for N in {N for _, _, N in self.items}}
-        self.bytes_per_step = sum(gemv_bytes(self.M, K, N, b) for b, K, N in self.items)
+                     for N in {it[2] for it in self.items}}
+        self.bytes_per_step = sum(gemv_bytes(self.M, K, N, b, G) for b, K, N, G in self.items[:self.n_step])
         n0 = nat.launch_count()
         self.step_graphs = [capture_graph(lambda r=r: self._step(r)) for r in range(self.R)]
         # capture_graph runs fn twice (eager warm-up + capture): launches of one step
         self.launches_per_step = (nat.launch_count() - n0) // (2 * self.R)
 
+    def copies_for(self, i: int) -> int:
+        """Weight copies of item i: the step's GEMVs rotate together (R copies,
+        more than twice the L2 per rotation); an extra case alone needs more
+        than twice the L2 of its own copies."""
+        if i < self.n_step:
+            return self.R
+        bits, K, N, _ = self.items[i]
+        return max(2, -(-2 * L2_BYTES // (N * K * bits // 8)))
+
     def _call(self, i: int, copy: int, M: int):
-        bits, K, N = self.items[i]
-        q, s = self.weights[copy][i]
+        bits, K, N, G = self.items[i]
+        q, s = self.weights[i][copy]
         act, out = self.acts[K], self.outs[N]
         stream = self.torch.cuda.current_stream().cuda_stream
         ws, ws_bytes = self.nat.matmul_workspace(bits, M, N, K, self.dev, stream)
         fn = "lw_gemm_w4a16" if bits == 4 else "lw_gemm_w8a16"
-        self.nat.call(fn, act.data_ptr(), q.data_ptr(), s.data_ptr(), None, out.data_ptr(), M, N, K, GROUP,
+        self.nat.call(fn, act.data_ptr(), q.data_ptr(), s.data_ptr(), None, out.data_ptr(), M, N, K, G,
                       ws, ws_bytes, stream)
 
     def _step(self, copy: int):
-        for i in range(len(self.items)):
+        for i in range(self.n_step):
             self._call(i, copy, self.M)
 
     def step(self, it: int):
         self.step_graphs[it % self.R].replay()
 
+    def time_item(self, i: int, M: int, reps: int = 20) -> float:
+        """ms of one launch of item i at M rows: a graph of back-to-back launches
+        over the rotating weight copies (more than twice the L2), CUDA events
+        around its replays."""
+        n = self.copies_for(i)
+        g = capture_graph(lambda: [self._call(i, r, M) for r in range(n)])
+        ms = time_graph(g, reps) / n
+        del g
+        return ms
+
     def kernel_stats(self) -> dict:
         """Per kernel family: algorithmic bytes and device time of its launches in
-        one step, each launch timed in a graph of R back-to-back launches over the
-        rotating weight copies (CUDA events around the replays)."""
+        one step (time_item per launch)."""
         fam = {}
-        for i, (bits, K, N) in enumerate(self.items):
-            g = capture_graph(lambda i=i: [self._call(i, r, self.M) for r in range(self.R)])
-            ms = time_graph(g, 20) / self.R
+        for i, (bits, K, N, G) in enumerate(self.items[:self.n_step]):
+            ms = self.time_item(i, self.M)
             d = fam.setdefault(f"gemv_w{bits}a16", {"bytes": 0, "ms": 0.0, "launches": 0, "shapes": {}})
-            d["bytes"] += gemv_bytes(self.M, K, N, bits)
+            b = gemv_bytes(self.M, K, N, bits, G)
+            d["bytes"] += b
             d["ms"] += ms
             d["launches"] += 1
-            d["shapes"][f"{K}x{N}"] = {"us": round(ms * 1e3, 3),
-                                       "GB/s": round(gemv_bytes(self.M, K, N, bits) / (ms * 1e-3) / 1e9, 1)}
+            d["shapes"][f"{K}x{N}"] = {"us": round(ms * 1e3, 3), "GB/s": round(b / (ms * 1e-3) / 1e9, 1)}
         return fam
+
+    def extra_stats(self, peak_gbs: float) -> dict:
+        """The single W8A16 QuantLinear with per-output-channel scales (K=2048,
+        N=8192; M = 1 and 16) and the 8B gate|up shape (INT4, K=4096, N=28672, M=1)."""
+        out = {}
+        for i in range(self.n_step, len(self.items)):
+            bits, K, N, G = self.items[i]
+            name = (f"config1_w8a16_perchannel_K{K}_N{N}" if (bits, K, N, G) == CONFIG1
+                    else f"w4a16_gate_up_8b_K{K}_N{N}_G{G}")
+            for M in ((1, 16) if (bits, K, N, G) == CONFIG1 else (1,)):
+                ms = self.time_item(i, M)
+                gbs = gemv_bytes(M, K, N, bits, G) / (ms * 1e-3) / 1e9
+                out.setdefault(name, {})[f"M{M}"] = {"us": round(ms * 1e3, 3), "GB/s": round(gbs, 1),
+                                                     "frac": round(gbs / peak_gbs, 4)}
+        return out
 
     def e2e(self, steps: int) -> dict:
         """Same GEMVs through the public drop-in ops with host buffers: pinned
@@ -278,17 +323,17 @@ class GemvWorkload:
         torch = self.torch
         from liteweight_b200 import kernels
         host_act = {K: a[:self.M].cpu().pin_memory() for K, a in self.acts.items()}
-        host_out = [torch.empty(self.M, N, dtype=torch.float16).pin_memory() for _, _, N in self.items]
-        h2d = sum(self.M * K * 2 for _, K, _ in self.items)
-        d2h = sum(self.M * N * 2 for _, _, N in self.items)
+        host_out = [torch.empty(self.M, N, dtype=torch.float16).pin_memory() for _, _, N, _ in self.items]
+        h2d = sum(self.M * K * 2 for _, K, _, _ in self.items[:self.n_step])
+        d2h = sum(self.M * N * 2 for _, _, N, _ in self.items[:self.n_step])
 
         def one(it):
             copy = it % self.R
-            for i, (bits, K, N) in enumerate(self.items):
+            for i, (bits, K, N, G) in enumerate(self.items[:self.n_step]):
                 a = host_act[K].to(self.dev, non_blocking=True)
-                q, s = self.weights[copy][i]
+                q, s = self.weights[i][copy]
                 fn = kernels.matmul_int4 if bits == 4 else kernels.matmul_int8
-                host_out[i].copy_(fn(a, q, s, GROUP), non_blocking=True)
+                host_out[i].copy_(fn(a, q, s, G), non_blocking=True)
 
         for it in range(3):
             one(it)
@@ -308,12 +353,27 @@ class GemvWorkload:
         """Algorithmic GB/s vs M for both bit widths over the four shapes (graph-timed)."""
         out = {}
         for bits in (4, 8):
+            idx = [self.items.index((bits, K, N, GROUP)) for K, N in GEMV_SHAPES]
             for M in (1, 2, 4, 8, 16, 32, 64, 128, 256):
-                idx = [self.items.index((bits, K, N)) for K, N in GEMV_SHAPES]
                 g = capture_graph(lambda: [self._call(i, r, M) for r in range(self.R) for i in idx])
                 ms = time_graph(g, 5) / self.R
+                del g
                 tot_b = sum(gemv_bytes(M, K, N, bits) for K, N in GEMV_SHAPES)
                 out[f"w{bits}_M{M}"] = round(tot_b / (ms * 1e-3) / 1e9, 1)
+        return out
+
+    def summary(self, peak_gbs: float, sweep: bool = True) -> dict:
+        """The GEMV half of the headline metric, for the default line."""
+        fam = self.kernel_stats()
+        m1 = {}
+        for k, v in fam.items():
+            gbs = v["bytes"] / (v["ms"] * 1e-3) / 1e9
+            m1[k] = {"GB/s": round(gbs, 1), "frac": round(gbs / peak_gbs, 4), "shapes": v["shapes"]}
+        out = {"M1_llama_3_2_1b_shapes_G128": m1, **self.extra_stats(peak_gbs),
+               "timing": "graph of back-to-back launches over rotating weight copies > 2x L2, CUDA events",
+               "peak_gbs": peak_gbs}
+        if sweep:
+            out["gbs_vs_m"] = self.sweep()
         return out
 
 
@@ -342,8 +402,7 @@ class DecodeWorkload:
         self.spec = E.LlamaSpec(**arch, bits=cfg["bits"], group_size=GROUP)
         self.B, self.P, self.T = batch, prompt or cfg["prompt"], new or cfg["new"]
         self.tp, self.rank = dist.world, dist.rank
-        self.metric = (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only, batch {batch}, "
-                       f"prompt {self.P}, greedy, TP{self.tp})")
+        self.metric = decode_metric(model, batch, self.P, self.tp)
         max_seq = self.P + max(self.T, extra_steps) + 1
         g = torch.Generator(device=device).manual_seed(20251201)
         spec = self.spec
@@ -356,6 +415,7 @@ class DecodeWorkload:
         embed = (torch.randn(spec.vocab, spec.hidden, device=device, generator=g) * 0.02).half()
         norm = (1.0 + 0.1 * torch.randn(spec.hidden, device=device, generator=g)).half()
         cos, sin = E.rope_tables(E.default_inv_freq(spec.head_dim, spec.rope_theta), max_seq, 1.0, device)
+        self.embed, self.norm, self.cos, self.sin = embed, norm, cos, sin
         group = None
         if self.tp > 1:
             import torch.distributed as tdist
@@ -365,6 +425,28 @@ class DecodeWorkload:
         gp = torch.Generator().manual_seed(7)
         self.prompt = torch.randint(0, spec.vocab, (batch, self.P), generator=gp)
         torch.cuda.synchronize()
+
+    def layer_weights(self, li: int):
+        """Layer li's unsharded weights, regenerated from its seed (the same
+        tensors every rank sharded when the engine was built)."""
+        E = self.E
+        return E.synthetic_layers(E.LlamaSpec(**{**self.spec.__dict__, "n_layers": 1}), self.dev, seed=1000 + li)[0]
+
+    def teacher_forced_logits(self, ids, steps: int):
+        """The engine's logits [steps, B, V/TP] (this rank's vocabulary shard)
+        of decode steps 1..steps with the given generated ids forced: step j
+        predicts ids[:, j]."""
+        torch, eng = self.torch, self.eng
+        eng.start(self.prompt, forced=ids)
+        eng.prefill()
+        eng.capture()
+        out = []
+        for _ in range(steps):
+            eng.step(1)
+            out.append(eng.logits.float().clone())
+        torch.cuda.synchronize()
+        eng.check()
+        return torch.stack(out, 0)
 
     def prefill(self):
         """Load the prompt and run it through the model in chunks (the engine's
@@ -427,104 +509,250 @@ class DecodeWorkload:
                 "d2h_bytes_per_step": ids.numel() * 4, "ids": ids}
 
 
-class CpuDecode:
-    """The reference's CPU path for one decode step, on a bounded sample: the
-    oracle's QuantLinear arithmetic (dequantize the packed weights every call,
-    fp32 matmul; liteweight/quantize.py:30-60, :102-135) for the seven linears
-    of one layer at batch 1, split by output rows over the host cores, plus
-    the fp16 lm_head; per-token time = layers x layer time + lm_head time
-    (norms, RoPE and attention at batch 1 are <1% of the arithmetic and left
-    out)."""
+class TorchDecodeReference:
+    """Checker of the decode line's parity (never timed): a teacher-forced fp32
+    torch restatement, on the device, of the same packed weights through the
+    reference's arithmetic - every QuantLinear dequantizes exactly
+    (liteweight/quantize.py:30-43, :102-128) and multiplies in fp32 with an
+    fp16 result (:60) - and of the HF Llama layers around them with the fp16
+    rounding points of the fp16 model (transformers 5.5.0 modeling_llama.py:
+    RMSNorm :63-68, RoPE :138-167, fp32-softmax GQA attention :197-222,
+    SwiGLU :171-184, fp16 residual adds :320-335)."""
 
-    def __init__(self, model: str, batch: int = 1):
+    def __init__(self, wl: DecodeWorkload):
+        self.wl, self.torch = wl, wl.torch
+
+    def _dequant(self, q, s, bits, G):
+        torch = self.torch
+        n = q.shape[0]
+        if bits == 4:
+            b = q.view(torch.int8)
+            codes = torch.stack(((b << 4) >> 4, b >> 4), dim=-1).view(n, -1)
+        else:
+            codes = q
+        k = codes.shape[1]
+        w = codes.float().view(n, k // G, G) * s.float().unsqueeze(-1)
+        return w.view(n, k).half().float()
+
+    def _lin(self, x16, pair, bits, G):
+        q, s = pair
+        return (x16.float() @ self._dequant(q, s, bits, G).t()).half()
+
+    @staticmethod
+    def _rmsnorm(x16, w, eps):
+        xf = x16.float()
+        var = (xf * xf).mean(-1, keepdim=True)
+        return (w.float() * (xf * (1.0 / (var + eps).sqrt())).half().float()).half()
+
+    @staticmethod
+    def _rope(x16, cos, sin):
+        h = x16.shape[-1] // 2
+        rot = x16.new_empty(x16.shape)
+        rot[..., :h] = -x16[..., h:]
+        rot[..., h:] = x16[..., :h]
+        return ((x16.float() * cos.float()).half().float() + (rot.float() * sin.float()).half().float()).half()
+
+    def logits(self, tokens, first: int, count: int):
+        """fp32 logits [B, count, V] at positions first .. first+count-1 of the
+        int64 token rows [B, T] (each position sees tokens[:, :pos+1])."""
+        torch, wl = self.torch, self.wl
+        sp, dev = wl.spec, wl.dev
+        hd, nh, nkv = sp.head_dim, sp.n_heads, sp.n_kv_heads
+        B, T = tokens.shape
+        prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            x = wl.embed[tokens.to(dev)].half()                               # [B, T, H]
+            cos, sin = wl.cos[:T][:, None, :], wl.sin[:T][:, None, :]         # [T, 1, hd]
+            mask = torch.ones(T, T, dtype=torch.bool, device=dev).tril()
+            for li in range(sp.n_layers):
+                L = wl.layer_weights(li)
+                for b in range(B):
+                    xb = x[b]
+                    h = self._rmsnorm(xb, L.in_norm, sp.eps)
+                    q = self._rope(self._lin(h, L.q, sp.bits, sp.group_size).view(T, nh, hd), cos, sin)
+                    k = self._rope(self._lin(h, L.k, sp.bits, sp.group_size).view(T, nkv, hd), cos, sin)
+                    v = self._lin(h, L.v, sp.bits, sp.group_size).view(T, nkv, hd)
+                    rep = nh // nkv
+                    kf = k.float().repeat_interleave(rep, dim=1).transpose(0, 1)   # [nh, T, hd]
+                    vf = v.float().repeat_interleave(rep, dim=1).transpose(0, 1)
+                    sc = (q.float().transpose(0, 1) @ kf.transpose(1, 2)) * (hd ** -0.5)
+                    sc = sc.masked_fill(~mask, float("-inf")).softmax(-1)
+                    a = (sc @ vf).transpose(0, 1).reshape(T, nh * hd).half()
+                    del sc, kf, vf
+                    xb = (xb.float() + self._lin(a, L.o, sp.bits, sp.group_size).float()).half()
+                    h = self._rmsnorm(xb, L.post_norm, sp.eps)
+                    g = self._lin(h, L.gate, sp.bits, sp.group_size).float()
+                    u = self._lin(h, L.up, sp.bits, sp.group_size).float()
+                    act = ((g / (1.0 + torch.exp(-g))).half().float() * u).half()
+                    x[b] = (xb.float() + self._lin(act, L.down, sp.bits, sp.group_size).float()).half()
+                del L
+            h = self._rmsnorm(x[:, first:first + count], wl.norm, sp.eps)      # [B, count, H]
+            head = wl.embed.float()
+            return h.float() @ head.t()
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+
+
+def decode_parity(wl: DecodeWorkload, ids_host, rank: int, steps: int = 32) -> dict | None:
+    """Greedy match rate of the timed configuration's generated ids and the
+    max err / row tolerance of the first `steps` decode steps' logits, both
+    against TorchDecodeReference (rank 0 computes it; every rank runs the
+    engine's teacher-forced pass, a collective under tensor parallelism)."""
+    torch = wl.torch
+    steps = max(1, min(steps, wl.T - 1))
+    ids = ids_host.to(torch.int64)
+    got = wl.teacher_forced_logits(ids, steps)                      # [steps, B, Vs]
+    if rank != 0:
+        return None
+    toks = torch.cat([wl.prompt.to(torch.int64), ids], dim=1)        # [B, P + T]
+    P, T = wl.P, wl.T
+    ref = TorchDecodeReference(wl)
+    # positions P-1 .. P+T-2 predict ids[:, 0 .. T-1]; only T-1 of them need the full model
+    lg = ref.logits(toks[:, :P + T - 1], P - 1, T)                   # [B, T, V]
+    ref_ids = lg.argmax(-1).cpu()
+    match = float((ref_ids == ids).float().mean())
+    miss = (ref_ids != ids).nonzero()
+    first_mismatch = int(miss[:, 1].min()) if miss.numel() else None
+    vs = got.shape[-1]
+    r = lg[:, 1:1 + steps].transpose(0, 1)                           # [steps, B, V]
+    tol = 1e-2 * r.double().pow(2).sum(-1, keepdim=True).sqrt() / (r.shape[-1] ** 0.5)
+    err = (got.double() - r[..., :vs].double()).abs()
+    ratio = float((err / tol).max())
+    return {"match_rate": round(match, 4), "tokens_compared": int(ids.numel()),
+            "first_mismatch_step": first_mismatch, "logits_err_over_tol": round(ratio, 4),
+            "logits_steps_compared": steps, "logits_columns": f"vocab shard 0 of {wl.tp} ({vs} of {r.shape[-1]})",
+            "tolerance": "max-abs err <= 1e-2 * ||ref row||_2 / sqrt(V), per (step, sequence)",
+            "reference": "teacher-forced fp32 torch restatement of the same packed weights (exact dequant, fp32 "
+                         "matmul, HF fp16 rounding points), full depth, on the device"}
+
+
+def decode_config(model: str, batch: int, prompt: int, new: int, world: int, fold: bool, exchange: str) -> dict:
+    """The `config` object of a decode line (both arms print the same one)."""
+    cfg = MODELS[model]
+    from liteweight_b200 import engine as E
+    spec = E.LlamaSpec(**getattr(E, cfg["arch"]), bits=cfg["bits"], group_size=GROUP)
+    return {"workload": f"decode {cfg['name']} INT{cfg['bits']} G{GROUP}", "model": cfg["name"],
+            "global_batch": batch, "prompt": prompt, "new_tokens": new, "seq_len": prompt + new,
+            "parallelism": f"tp{world}",
+            "dequant": "per-chunk fp32 scale" if fold else "exact fp16(code*scale)",
+            "all_reduce": ("none" if world == 1 else
+                           "in-kernel peer-memory exchange over NVLink" if exchange == "peer"
+                           else "NCCL all_reduce in the step graph"),
+            "l2": f"inputs larger than L2 ({spec.weight_bytes_per_token() / world / 1e9:.2f} GB of weights per GPU "
+                  "per step)"}
+
+
+def decode_metric(model: str, batch: int, prompt: int, world: int) -> str:
+    cfg = MODELS[model]
+    return (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only, batch {batch}, "
+            f"prompt {prompt}, greedy, TP{world})")
+
+
+class CpuDecode:
+    """The reference's CPU path for one decode token: every quantized linear
+    of every layer dequantized and fp32-multiplied as liteweight's oracle does
+    (liteweight/quantize.py:30-60, :102-135; restated with torch ops by
+    oracle/torch_cpu.py), plus the fp16 lm_head through the same fp32 matmul,
+    at the configuration's batch; one BLAS call per linear over all host
+    threads (torch.set_num_threads(os.cpu_count())). Norms, RoPE and attention
+    at this batch are <1% of the arithmetic and left out. Weight codes are
+    random bytes (the work does not depend on the values); `distinct` layer
+    sets are cycled through the L layer positions."""
+
+    def __init__(self, model: str, batch: int = 1, distinct: int = 4):
+        import torch
         from liteweight_b200 import engine as E
-        from oracle import quant as oq
+        from oracle import torch_cpu
+        self.torch, self.tc = torch, torch_cpu
+        self.cores = os.cpu_count() or 1
+        torch.set_num_threads(self.cores)
         cfg = MODELS[model]
         self.spec = E.LlamaSpec(**getattr(E, cfg["arch"]), bits=cfg["bits"], group_size=GROUP)
-        self.oq, self.B = oq, batch
-        rng = np.random.default_rng(3)
-        self.lin = []
-        for name, n, k in self.spec.linear_shapes():
-            if self.spec.bits == 4:
-                q = rng.integers(0, 256, (n, k // 2), dtype=np.uint8)
-            else:
-                q = rng.integers(-127, 128, (n, k), dtype=np.int8)
-            s = (rng.random((n, k // GROUP)) * 2e-3 + 1e-4).astype(np.float16)
-            self.lin.append((name, q, s, rng.standard_normal((batch, k)).astype(np.float16)))
-        self.cores = os.cpu_count() or 1
-        self.pool = ThreadPoolExecutor(self.cores)
-        self.lm_rows = 8192
-        self.lm = (rng.standard_normal((self.lm_rows, self.spec.hidden)) * 0.02).astype(np.float16)
-        self.h = rng.standard_normal((batch, self.spec.hidden)).astype(np.float16)
+        self.B = batch
+        g = torch.Generator().manual_seed(3)
+        sp = self.spec
 
-    def _rows(self, fn, n):
-        blocks = np.array_split(np.arange(n), self.cores)
-        return np.concatenate(list(self.pool.map(fn, blocks)), axis=1)
+        def rows(n, make):   # n rows: a random 1024-row block repeated (generating all of them is slow)
+            blk = make(min(n, 1024))
+            return blk.repeat(-(-n // blk.shape[0]), 1)[:n].contiguous()
+        self.layers = []
+        for _ in range(min(distinct, sp.n_layers)):
+            lin = []
+            for _name, n, k in sp.linear_shapes():
+                if sp.bits == 4:
+                    q = rows(n, lambda r: torch.randint(0, 256, (r, k // 2), dtype=torch.uint8, generator=g))
+                else:
+                    q = rows(n, lambda r: torch.randint(-127, 128, (r, k), dtype=torch.int8, generator=g))
+                s = rows(n, lambda r: (torch.rand(r, k // GROUP, generator=g) * 2e-3 + 1e-4).half())
+                lin.append((q, s, k))
+            self.layers.append(lin)
+        self.acts = {k: torch.randn(batch, k, generator=g).half() for _n, _o, k in sp.linear_shapes()}
+        self.lm = rows(sp.vocab, lambda r: (torch.rand(r, sp.hidden, generator=g) * 0.04 - 0.02).half())
+        self.h = torch.randn(batch, sp.hidden, generator=g).half()
 
-    def linear(self, i: int) -> float:
-        name, q, s, act = self.lin[i]
+    def layer(self, li: int) -> float:
         t = time.perf_counter()
-        self._rows(lambda r: self.oq.packed_matmul(act, q[r], s[r], GROUP, self.spec.bits), q.shape[0])
+        for q, s, k in self.layers[li % len(self.layers)]:
+            self.tc.quant_linear(self.acts[k], q, s, GROUP, self.spec.bits)
         return time.perf_counter() - t
 
-    def lm_head_seconds(self) -> float:
+    def lm_head(self) -> float:
         t = time.perf_counter()
-        self._rows(lambda r: (self.h.astype(np.float32) @ self.lm[r].astype(np.float32).T).astype(np.float16),
-                   self.lm_rows)
-        return (time.perf_counter() - t) * self.spec.vocab / self.lm_rows
+        self.tc.fp16_linear(self.h, self.lm)
+        return time.perf_counter() - t
 
-    def measure(self, min_seconds: float = 10.0) -> dict:
+    def token(self, budget_s: float = 90.0) -> dict:
+        """One whole token (all L layers + lm_head) unless that would take more
+        than budget_s: then the layers timed so far are extrapolated to L."""
+        L = self.spec.n_layers
         t0 = time.perf_counter()
-        sums = [0.0] * len(self.lin)
-        n = 0
-        while n == 0 or time.perf_counter() - t0 < min_seconds:
-            for i in range(len(self.lin)):
-                sums[i] += self.linear(i)
-            n += 1
-        layer = sum(sums) / n
-        lm = self.lm_head_seconds()
-        tok_s = self.B / (self.spec.n_layers * layer + lm)
+        times = []
+        for li in range(L):
+            times.append(self.layer(li))
+            if time.perf_counter() - t0 > budget_s:
+                break
+        lm = self.lm_head()
+        layer_mean = sum(times) / len(times)
+        tok_s = self.B / (layer_mean * L + lm)
+        whole = len(times) == L
         return {"value": round(tok_s, 5), "unit": "tokens/s", "cores": self.cores, "kind": "port",
-                "layer_seconds": round(layer, 3), "lm_head_seconds": round(lm, 3),
-                "sample": f"{n} pass(es) over the 7 quantized linears of one layer (dequantize + fp32 matmul, "
-                          f"rows split over {self.cores} threads) + the fp16 lm_head on {self.lm_rows} vocab rows "
-                          f"scaled to {self.spec.vocab}; per token = {self.spec.n_layers} layers + lm_head"}
+                "seconds_per_token": round(layer_mean * L + lm, 3), "layer_seconds": round(layer_mean, 4),
+                "lm_head_seconds": round(lm, 4),
+                "sample": (f"one whole token: {L} layers x 7 quantized linears + the fp16 lm_head; "
+                           if whole else f"{len(times)} of {L} layers (x 7 linears) + the fp16 lm_head, "
+                                         f"extrapolated to {L} layers; ")
+                          + f"batch {self.B}, torch dequantize + fp32 matmul (oracle/torch_cpu.py), "
+                            f"torch.set_num_threads({self.cores})"}
 
-
-# ----------------------------------------------------------------- CPU baseline (reference path)
 
 class CpuGemv:
-    """The reference's CPU path for the same GEMVs: dequantize the packed weights
-    and fp32-matmul (liteweight/quantize.py:30-60, :102-135), as restated by the
-    oracle, split by output rows over the host cores."""
+    """The reference's CPU path for the GEMV step: the 8 M=1 QuantLinear calls
+    of the 1B shapes, dequantized and fp32-multiplied with torch ops
+    (oracle/torch_cpu.py) over all host threads."""
 
     def __init__(self, seed: int = 0):
-        from oracle import quant as oq
-        self.oq = oq
-        rng = np.random.default_rng(seed)
+        import torch
+        from oracle import torch_cpu
+        self.torch, self.tc = torch, torch_cpu
+        self.cores = os.cpu_count() or 1
+        torch.set_num_threads(self.cores)
+        g = torch.Generator().manual_seed(seed)
         self.items = []
         for bits in (4, 8):
             for K, N in GEMV_SHAPES:
                 if bits == 4:
-                    q = rng.integers(0, 256, (N, K // 2), dtype=np.uint8)
+                    q = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, generator=g)
                 else:
-                    q = rng.integers(-127, 128, (N, K), dtype=np.int8)
-                s = (rng.random((N, K // GROUP)) * 2e-3 + 1e-4).astype(np.float16)
-                act = rng.standard_normal((1, K)).astype(np.float16)
+                    q = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g)
+                s = (torch.rand(N, K // GROUP, generator=g) * 2e-3 + 1e-4).half()
+                act = torch.randn(1, K, generator=g).half()
                 self.items.append((bits, K, N, q, s, act))
-        self.cores = os.cpu_count() or 1
-        self.pool = ThreadPoolExecutor(self.cores)
         self.bytes_per_step = sum(gemv_bytes(1, K, N, b) for b, K, N, *_ in self.items)
-
-    def _gemv(self, bits, q, s, act):
-        n = q.shape[0]
-        blocks = np.array_split(np.arange(n), self.cores)
-        parts = list(self.pool.map(lambda r: self.oq.packed_matmul(act, q[r], s[r], GROUP, bits), blocks))
-        return np.concatenate(parts, axis=1)
 
     def step(self):
         for bits, K, N, q, s, act in self.items:
-            self._gemv(bits, q, s, act)
+            self.tc.quant_linear(act, q, s, GROUP, bits)
 
     def measure(self, min_seconds: float = 10.0, max_steps: int = 30) -> dict:
         self.step()
@@ -536,8 +764,8 @@ class CpuGemv:
         dt = (time.perf_counter() - t0) / n
         return {"value": round(self.bytes_per_step / dt / 1e9, 3), "unit": "GB/s", "cores": self.cores,
                 "kind": "port", "ms_per_step": round(dt * 1e3, 2),
-                "sample": f"{n} passes over the 8 M=1 GEMVs (INT4+INT8, 1B shapes), numpy dequantize + fp32 "
-                          f"matmul split by output rows over {self.cores} threads"}
+                "sample": f"{n} passes over the 8 M=1 GEMVs (INT4+INT8, 1B shapes), torch dequantize + fp32 "
+                          f"matmul (oracle/torch_cpu.py), torch.set_num_threads({self.cores})"}
 
 
 # ----------------------------------------------------------------- main
@@ -558,11 +786,17 @@ def smi_gpu_id(local_rank: int) -> str:
     return vis[local_rank] if local_rank < len(vis) else str(local_rank)
 
 
+def gemv_config(world: int) -> dict:
+    return {"workload": "gemv M=1 Llama-3.2-1B shapes (KxN 2048x2048, 2048x512, 2048x8192, 8192x2048) INT4+INT8 G128",
+            "parallelism": f"replicas x{world}",
+            "l2": "rotating weight copies, more than twice the L2 per rotation"}
+
+
 def run_reference_gemv(args, dist: Dist):
     if dist.rank != 0:
         return
     cpu = CpuGemv()
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 3)):
         cpu.step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -572,9 +806,10 @@ def run_reference_gemv(args, dist: Dist):
     line = {"impl": "reference", "metric": GemvWorkload.metric, "value": round(value, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8/int8 codes, fp32 acc",
-            "data": "synthetic", "config": {"workload": "gemv M=1 Llama-3.2-1B shapes INT4+INT8 G128"},
+            "data": "synthetic", "config": gemv_config(args.gpus),
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cpu.cores, "kind": "port",
-                             "sample": "every step = the 8 M=1 GEMVs, numpy dequantize + fp32 matmul"},
+                             "sample": "every step = the 8 M=1 GEMVs, torch dequantize + fp32 matmul "
+                                       f"(oracle/torch_cpu.py), torch.set_num_threads({cpu.cores})"},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -592,7 +827,7 @@ def run_gemv(args, dist: Dist):
     dist.init("nccl")
     lwbuild.build()
     nat.lib()
-    wl = GemvWorkload(dev, seed=1234 + dist.rank)
+    wl = GemvWorkload(dev, seed=1234 + dist.rank, extras=False)
     for it in range(args.warmup):
         wl.step(it)
     torch.cuda.synchronize()
@@ -634,10 +869,9 @@ def run_gemv(args, dist: Dist):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8/int8 codes x fp16, fp32 acc",
             "data": "synthetic",
-            "config": {"workload": "gemv M=1 Llama-3.2-1B shapes (KxN 2048x2048, 2048x512, 2048x8192, 8192x2048) "
-                                   "INT4+INT8 G128", "parallelism": f"replicas x{dist.world}",
-                       "l2": f"rotating {wl.R} weight copies ({wl.R * sum(N * K * b // 8 for b, K, N in wl.items) >> 20}"
-                             " MiB) > L2"},
+            "config": {**gemv_config(dist.world),
+                       "l2": f"rotating {wl.R} weight copies "
+                             f"({wl.R * sum(N * K * b // 8 for b, K, N, _ in wl.items[:wl.n_step]) >> 20} MiB) > L2"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "kernels": {k: {"launches_per_step": v["launches"],
                             "GB/s": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1), "shapes": v["shapes"]}
@@ -713,62 +947,60 @@ def run_decode(args, dist: Dist):
            "ms_per_call": round(e2e_ms, 3)}
     clocks = clk.summary()
     launches = args.steps * wl.eng.kernels_per_step()
+    parity = None if args.no_parity else decode_parity(wl, e["ids"], dist.rank)
+    gemv = None
+    if dist.world == 1 and not args.no_gemv:
+        gw = GemvWorkload(dev, seed=1234)
+        gemv = gw.summary(peak.peak_mem_bandwidth_gbs, sweep=not args.no_sweep)
+        del gw
     if dist.rank != 0:
         wl.eng.close()
         dist.close()
         return
-    cpu = CpuDecode(args.model, wl.B).measure() if dist.world == 1 else None
-    line = {"metric": wl.metric, "value": round(value, 2), "unit": "tokens/s", "n_gpus": dist.world,
+    cpu = CpuDecode(args.model, wl.B).token() if dist.world == 1 else None
+    line = {"metric": decode_metric(args.model, wl.B, wl.P, dist.world), "value": round(value, 2),
+            "unit": "tokens/s", "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": f"int{wl.spec.bits} weights x fp16, fp32 acc",
             "data": "synthetic (random-init weights, uniform random prompt ids)",
-            "config": {"workload": f"decode {MODELS[args.model]['name']} INT{wl.spec.bits} G{GROUP}",
-                       "model": MODELS[args.model]["name"], "global_batch": wl.B, "prompt": wl.P,
-                       "new_tokens": wl.T, "seq_len": wl.P + wl.T, "parallelism": f"tp{dist.world}",
-                       "dequant": "per-chunk fp32 scale" if args.fold else "exact fp16(code*scale)",
-                       "all_reduce": ("none" if dist.world == 1 else
-                                      "in-kernel peer-memory exchange over NVLink" if args.exchange == "peer"
-                                      else "NCCL all_reduce in the step graph"),
-                       "l2": f"inputs larger than L2 ({wl.spec.weight_bytes_per_token() / dist.world / 1e9:.2f} GB "
-                             "of weights per GPU per step)"},
-            "roofline": roofline, "decode_roofline": decode_roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "config": decode_config(args.model, wl.B, wl.P, wl.T, dist.world, args.fold, args.exchange),
+            "roofline": roofline, "decode_roofline": decode_roofline, "parity": parity, "gemv": gemv,
+            "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(launches), "kernels": {k: {kk: v[kk] for kk in ("launches", "us", "GB/s")}
                                                        for k, v in kstats.items()},
             "clocks": clocks}
+    if args.layers:
+        line["config"]["layers"] = args.layers
     print(json.dumps(line), flush=True)
     wl.eng.close()
     dist.close()
 
 
 def run_reference_decode(args, dist: Dist):
-    """The reference's CPU path on the box's cores: every step is one of the 7
-    quantized linears of a layer (rotating), dequantized and matmul'd as the
-    reference does; tokens/s = batch / (layers x summed linear times + lm_head)."""
+    """The reference's CPU path on the box's host cores (rank 0 only; the other
+    ranks exit): one whole decode token - every quantized linear of every
+    layer dequantized and fp32-multiplied as the reference's oracle does, plus
+    the fp16 lm_head (CpuDecode) - after `warmup` (at most 3) warm-up layers.
+    The line reports tokens/s of that token; `steps` and `warmup` echo the
+    arguments, the sample is described in cpu_baseline."""
     if dist.rank != 0:
         return
-    cpu = CpuDecode(args.model, args.batch)
-    for i in range(min(args.warmup, 7)):
-        cpu.linear(i % 7)
-    times = [[] for _ in range(7)]
-    t0 = time.perf_counter()
-    for it in range(args.steps):
-        times[it % 7].append(cpu.linear(it % 7))
-    wall = time.perf_counter() - t0
-    layer = sum(sum(t) / len(t) for t in times if t) * (7 / max(1, sum(1 for t in times if t)))
-    lm = cpu.lm_head_seconds()
-    tok_s = args.batch / (cpu.spec.n_layers * layer + lm)
     cfg = MODELS[args.model]
-    line = {"impl": "reference", "metric": (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only, "
-                                            f"batch {args.batch}, prompt {cfg['prompt']}, greedy, TP{args.gpus})"),
-            "value": round(tok_s, 5), "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
+    P, T = args.prompt or cfg["prompt"], args.new or cfg["new"]
+    cpu = CpuDecode(args.model, args.batch)
+    for i in range(min(args.warmup, 3)):
+        cpu.layer(i)
+    t0 = time.perf_counter()
+    tok = cpu.token()
+    wall = time.perf_counter() - t0
+    line = {"impl": "reference", "metric": decode_metric(args.model, args.batch, P, args.gpus),
+            "value": tok["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(wall * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": f"int{cfg['bits']} codes, fp32 acc",
-            "data": "synthetic",
-            "config": {"workload": f"decode {cfg['name']} INT{cfg['bits']} G{GROUP}", "global_batch": args.batch},
-            "cpu_baseline": {"value": round(tok_s, 5), "unit": "tokens/s", "cores": cpu.cores, "kind": "port",
-                             "sample": f"{args.steps} linears (rotating over a layer's 7) + fp16 lm_head sample, "
-                                       f"extrapolated to {cpu.spec.n_layers} layers"},
-            "e2e": {"value": round(tok_s, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "data": "synthetic (random codes and scales of the configuration's shapes)",
+            "config": decode_config(args.model, args.batch, P, T, args.gpus, args.fold, args.exchange),
+            "cpu_baseline": tok,
+            "e2e": {"value": tok["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -782,6 +1014,8 @@ def main():
     ap.add_argument("--model", choices=sorted(MODELS), default="8b")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the decode line's parity check (profiling runs)")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the decode line's GEMV figures (profiling runs)")
     ap.add_argument("--fold", action="store_true",
                     help="decode GEMVs scale each chunk sum in fp32 instead of dequantizing exactly")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",

@@ -109,3 +109,30 @@ def test_llama_oracle_matches_hf(golden_dir, fixture):
     # greedy picks along the teacher-forced path
     match = (ol.greedy(got.reshape(-1, got.shape[-1])) == d["tokens"].T.reshape(-1)).mean()
     assert match >= 0.9, match
+
+
+def test_torch_cpu_restatement_bit_exact(qg):
+    """The torch CPU restatement timed as the CPU baseline dequantizes exactly
+    like the reference (golden dq arrays) and its matmul equals the oracle's
+    fakequant result within the fp32-order bound."""
+    import torch
+    from oracle import torch_cpu as tc
+    for name in _cases(qg):
+        if f"{name}/dq8" not in qg:
+            continue
+        G = int(qg[f"{name}/G"])
+        for bits, key in ((8, "8"), (4, "4")):
+            q = torch.from_numpy(qg[f"{name}/q{key}"])
+            s = torch.from_numpy(qg[f"{name}/s{key}"])
+            d = (tc.dequantize_int8 if bits == 8 else tc.dequantize_int4)(q, s, G)
+            np.testing.assert_array_equal(d.numpy().view(np.uint16), qg[f"{name}/dq{key}"].view(np.uint16),
+                                          err_msg=f"{name} int{bits}")
+    d4 = tc.dequantize_int4(torch.from_numpy(qg["codes4/q"]), torch.from_numpy(qg["codes4/s"]), 128)
+    np.testing.assert_array_equal(d4.numpy().view(np.uint16), qg["codes4/dq"].view(np.uint16))
+    name = "tk_M3_K256_N40_G128"
+    act = qg[f"{name}/act"]
+    got = tc.quant_linear(torch.from_numpy(act), torch.from_numpy(qg[f"{name}/q4"]),
+                          torch.from_numpy(qg[f"{name}/s4"]), 128, 4).numpy().astype(np.float32)
+    ref = oq.packed_matmul(act, qg[f"{name}/q4"], qg[f"{name}/s4"], 128, 4).astype(np.float32)
+    big = np.maximum(np.abs(ref), np.abs(got)).astype(np.float16)
+    assert np.all(np.abs(got - ref) <= np.abs(np.spacing(big)).astype(np.float32) + 1e-6)

@@ -189,6 +189,12 @@ def test_gloo_tp2_decode_matches_unsharded_oracle():
 # ---------------------------------------------------------------- GPU, NCCL
 
 _GPU_MODEL = dict(hidden=512, inter=1024, layers=2, heads=8, kv=4, hd=64, vocab=1024, bits=4, seed=4)
+# eight ranks need eight kv heads (one per rank); o's and down's K slices stay whole 128-groups
+_GPU_MODEL_8 = dict(hidden=512, inter=1024, layers=2, heads=16, kv=8, hd=64, vocab=1024, bits=4, seed=4)
+
+
+def _gpu_model(world):
+    return _GPU_MODEL_8 if world > 4 else _GPU_MODEL
 
 
 def _nccl_worker(rank, world, port, out_path, exchange):
@@ -198,7 +204,7 @@ def _nccl_worker(rank, world, port, out_path, exchange):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     from liteweight_b200 import engine as E
-    w = random_model(**_GPU_MODEL)
+    w = random_model(**_gpu_model(world))
     to = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
     t1 = torch.zeros(1, device=dev)
     dist.all_reduce(t1)          # communicator up before graph capture
@@ -248,7 +254,7 @@ def _run_tp(exchange, world):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_decode_matches_oracle(world):
     """Tensor-parallel decode with the in-kernel peer exchange and with NCCL
     all-reduces: every rank picks the same tokens, both are within the row
@@ -264,7 +270,7 @@ def test_tp_decode_matches_oracle(world):
     if world == 2:
         assert np.array_equal(peer["logits"], nccl["logits"])
         assert np.array_equal(peer["tokens"], nccl["tokens"])
-    w = random_model(**_GPU_MODEL)
+    w = random_model(**_gpu_model(world))
     for r in (peer, nccl):
         ref = ol.teacher_forced_logits(w, r["prompt"], r["tokens"])
         g = r["logits"].reshape(-1, ref.shape[-1]).astype(np.float64)
