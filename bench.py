@@ -957,7 +957,7 @@ def run_decode(args, dist: Dist):
         wl.eng.close()
         dist.close()
         return
-    cpu = CpuDecode(args.model, wl.B).token() if dist.world == 1 else None
+    cpu = CpuDecode(args.model, wl.B).token() if (dist.world == 1 and not args.no_cpu) else None
     line = {"metric": decode_metric(args.model, wl.B, wl.P, dist.world), "value": round(value, 2),
             "unit": "tokens/s", "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
@@ -1016,6 +1016,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the decode line's parity check (profiling runs)")
     ap.add_argument("--no-gemv", action="store_true", help="skip the decode line's GEMV figures (profiling runs)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--fold", action="store_true",
                     help="decode GEMVs scale each chunk sum in fp32 instead of dequantizing exactly")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",

@@ -233,6 +233,9 @@ typedef struct {
   const lw_exchange_out* xout;  /* LW_EPI_PEER_*; read at the call */
   const int* prefill_seq;       /* NULL: decode (row m = sequence m). Else a prompt chunk: the M
                                    rows are positions *pos .. *pos + M - 1 of sequence *prefill_seq */
+  int sched_set;                /* 0 or 1: which of the workspace's two work-claim counters the
+                                   launch uses (M <= 8 dynamic schedule). Two launches that can
+                                   overlap (consecutive with pdl = 1) must use different sets. */
 } lw_fused_gemv_args;
 
 int lw_fused_gemv(const lw_fused_gemv_args* args, lw_stream_t stream);

@@ -45,6 +45,7 @@
 #include <cudaTypedefs.h>
 
 #include "gemv_host.cuh"
+#include "tma_host.cuh"
 
 namespace lw {
 
@@ -576,33 +577,7 @@ uint32_t tc_idesc(int mpad) {
   return d;
 }
 
-// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
-// (the library links the static runtime only).
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      f = nullptr;
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  }();
-  return fn;
-}
-
-// 2-D tiled tensor map: `rows` rows of `cols` elements, row stride `stride`
-// bytes, box {box_cols, box_rows}; reads past the edges fill zeros.
-bool encode_2d(CUtensorMap* m, CUtensorMapDataType type, const void* ptr, uint64_t cols, uint64_t rows,
-               uint64_t stride, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
-  auto enc = tensor_map_encoder();
-  if (!enc) return false;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {stride};
-  const cuuint32_t box[2] = {box_cols, box_rows};
-  const cuuint32_t elem[2] = {1, 1};
-  return enc(m, type, 2, const_cast<void*>(ptr), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
+using lw::encode_2d;
 
 int sm_count() {
   static int counts[64] = {};

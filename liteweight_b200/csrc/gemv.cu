@@ -230,11 +230,40 @@ bool stream_ok(const void* act, const void* w, int K, int G) {
          (BITS == 16 || (G % E == 0 && lw::group_shift(K, G) >= 0));
 }
 
+// The TMA-ring kernel's own conditions (gemv_ring.cuh): 16-byte activation
+// rows and weight rows (it reads whole 16-byte pieces; a row's last 128-byte
+// stage may run past K, the copy fills zeros there) and scale groups that
+// hold whole 16-byte pieces.
+template <int BITS>
+bool ring_ok(const void* act, const void* w, int K, int G) {
+  constexpr int E = lw::WT<BITS>::E;
+  return (K % 8 == 0) && ((size_t)K * BITS / 8) % 16 == 0 && aligned(w, 16) && aligned(act, 16) &&
+         (BITS == 16 || (G % E == 0 && lw::group_shift(K, G) >= 0));
+}
+
 // out[M,N] = act @ W^T (+bias): stream kernel in row blocks, or the generic kernel.
 template <int BITS>
 cudaError_t matmul_dispatch(const void* act, const void* w, const void* scales, const void* bias, void* out,
                             int M, int N, int K, int G, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (!stream_ok<BITS>(act, w, K, G)) {
+    // shapes the register-pipeline kernel cannot take may still suit the ring kernel
+    lw::RingPlan rpl;
+    if (M <= 8 && ws && ring_ok<BITS>(act, w, K, G) && lw::plan_ring<BITS, lw::PRO_PLAIN>(M, N, K, w, &rpl) &&
+        rpl.ws_bytes <= ws_bytes) {
+      lw::StreamParams p = {};
+      p.M = M;
+      p.act = static_cast<const __half*>(act);
+      p.w = static_cast<const uint8_t*>(w);
+      p.scales = static_cast<const __half*>(scales);
+      p.bias = static_cast<const __half*>(bias);
+      p.out = static_cast<__half*>(out);
+      p.lda = K;
+      p.ldo = N;
+      p.N = N;
+      p.K = K;
+      p.G = G;
+      return lw::launch_ring<BITS, lw::PRO_PLAIN, lw::EPI_PLAIN>(p, rpl, ws, 0, s, false);
+    }
     GemvParams p = {};
     p.act = static_cast<const __half*>(act);
     p.w = static_cast<const uint8_t*>(w);
@@ -344,7 +373,7 @@ const char* lw_status_string(int status) {
   }
 }
 
-int lw_abi_version(void) { return 111; }
+int lw_abi_version(void) { return 112; }
 
 int lw_take_device_error(void) {
   const int mine = lw_tu_take_error();

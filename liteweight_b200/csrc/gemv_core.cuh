@@ -241,9 +241,12 @@ LW_DEV float silu_f32(float x) { return x / (1.0f + expf(-x)); }
 
 // Epilogue for one tile: v[mt][i] holds D(row, col) with rows n_lo = 16*tile +
 // g (i = 0, 1) and n_hi = n_lo + 8 (i = 2, 3), cols m = 8*mt + 2t (+1 for odd i).
+// g is the tile row of the lane's lower row: lane / 4 unless the kernel maps
+// its lanes to the tile's rows in another order (gemv_ring.cuh).
 template <int MT, int EPI>
-LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4], int lane, uint32_t flag) {
-  const int g = lane >> 2, t = lane & 3;
+LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4], int lane, uint32_t flag,
+                        int g) {
+  const int t = lane & 3;
   const int n_lo = tile * 16 + g, n_hi = n_lo + 8;
   if constexpr (EPI == EPI_PLAIN || EPI == EPI_F32 || EPI == EPI_PEER_F32) {
 #pragma unroll
@@ -365,7 +368,18 @@ LW_DEV void finish_tile(const StreamParams& p, int tile, const float (&v)[MT][4]
 // all NT threads of the CTA; ends with a CTA barrier.
 constexpr int kStageBatch = 8;
 
-template <int BITS, int PRO, int NT>
+// Barrier over the NT threads that stage the activation: the whole CTA
+// (BAR == 0), or named barrier BAR when other warps of the CTA do not take part.
+template <int BAR, int NT>
+LW_DEV void stage_sync() {
+  if constexpr (BAR == 0) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+  }
+}
+
+template <int BITS, int PRO, int NT, int BAR = 0>
 LW_DEV void stage_activation(const StreamParams& p, __half* act_s, const __half* gam_s, float* ssq, uint32_t in_flag,
                              WaitBudget& wb) {
   constexpr int E = WT<BITS>::E;
@@ -454,7 +468,7 @@ LW_DEV void stage_activation(const StreamParams& p, __half* act_s, const __half*
     }
   }
   if constexpr (PRO != PRO_PLAIN) {
-    __syncthreads();
+    stage_sync<BAR, NT>();
     // modeling_llama.py:65-68: h = weight * fp16(x * rsqrt(mean(x^2) + eps))
     for (int m = 0; m < p.M; ++m) {
       float tot = 0.f;
@@ -478,7 +492,7 @@ LW_DEV void stage_activation(const StreamParams& p, __half* act_s, const __half*
       }
     }
   }
-  __syncthreads();
+  stage_sync<BAR, NT>();
 }
 
 // Copies the RMSNorm weight into shared memory (natural order). It does not
@@ -502,7 +516,7 @@ LW_DEV void flush_tile(const StreamParams& p, int tile, int seg_c0, int end_c, i
   const int C = p.kchunks;
   const bool whole = (seg_c0 == 0) && (end_c == C);
   if (whole) {
-    finish_tile<MT, EPI>(p, tile, acc, lane, out_flag);
+    finish_tile<MT, EPI>(p, tile, acc, lane, out_flag, lane >> 2);
     return;
   }
   const int first = (tile * C) / p.per;
@@ -533,7 +547,7 @@ LW_DEV void flush_tile(const StreamParams& p, int tile, int seg_c0, int end_c, i
         sum[mt][3] += f.w;
       }
     }
-    finish_tile<MT, EPI>(p, tile, sum, lane, out_flag);
+    finish_tile<MT, EPI>(p, tile, sum, lane, out_flag, lane >> 2);
     if (lane == 0) p.counters[tile] = 0;
   }
 }

@@ -7,7 +7,9 @@
 #include <algorithm>
 
 #include "gemv_core.cuh"
+#include "gemv_ring.cuh"
 #include "gemv_tma.cuh"
+#include "tma_host.cuh"
 
 namespace lw {
 
@@ -18,10 +20,15 @@ constexpr int kBatch = 2;                  // 16-byte chunks per row per registe
 template <int BITS>
 constexpr int kBatchOf = BITS == 16 ? 4 : kBatch;
 // Workspace layout: a fixed region of per-tile counters (kept zero between
-// calls, so any later call of any shape finds its counters zero), then the
-// fp32 slots, which are fully rewritten before they are read.
+// calls, so any later call of any shape finds its counters zero) whose last
+// kSchedBytes hold the ring kernel's two work-claim counter sets (also kept
+// zero), then the fp32 slots, which are fully rewritten before they are read.
 constexpr size_t kCounterBytes = 64 * 1024;
-constexpr int kMaxSplitTiles = (int)(kCounterBytes / 4);
+constexpr size_t kSchedBytes = 256;
+constexpr int kMaxSplitTiles = (int)((kCounterBytes - kSchedBytes) / 4);
+inline int* sched_counters(void* ws, int set) {
+  return reinterpret_cast<int*>(static_cast<char*>(ws) + kCounterBytes - kSchedBytes) + (set & 1) * kRingSchedInts;
+}
 
 inline int device_sm_count() {
   int dev = 0, n = 0;
@@ -147,6 +154,96 @@ cudaError_t plan_for(int M, int N, int K, bool allow_split, StreamPlan* pl) {
   return cudaSuccess;
 }
 
+// ------------------------------------------------------------------ ring GEMV
+// The TMA-ring kernel (gemv_ring.cuh) serves M <= 8 whenever its weight rows
+// can be a tensor map (row bytes a multiple of 16, weight 16-byte aligned) and
+// at least kRingMinStages ring slots fit beside the staged activation. Set
+// LW_B200_GEMV=stream to use the register-pipeline kernel instead.
+constexpr int kRingMinStages = 4;
+constexpr size_t kRingSmemMax = 232448;   // opt-in dynamic shared memory per CTA on sm_100
+constexpr size_t kRingStaticBytes = 4096; // the kernel's static shared memory, rounded up
+
+inline bool ring_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LW_B200_GEMV");
+    return !(v && (strcmp(v, "stream") == 0 || strcmp(v, "bulk") == 0));
+  }();
+  return on;
+}
+
+// Units per CTA the schedule aims for (more: finer balance, more split tiles).
+inline int ring_units_per_cta() {
+  static const int n = [] {
+    const char* v = getenv("LW_B200_RING_UNITS");
+    const int x = v ? atoi(v) : 0;
+    return x > 0 ? x : 4;
+  }();
+  return n;
+}
+
+struct RingPlan {
+  int spr, nst, upr, units, stages, grid, rowblocks, tiles, cp, kchunks;
+  size_t smem, ws_bytes;
+};
+
+template <int BITS, int PRO>
+bool plan_ring(int M, int N, int K, const void* w, RingPlan* pl) {
+  constexpr int KC = 4 * WT<BITS>::E;
+  if (!ring_enabled() || M < 1 || M > 8 || N < kRingRows) return false;
+  const size_t rowbytes = (size_t)K * BITS / 8;
+  if (rowbytes % 16 || rowbytes < 128 || (w && (reinterpret_cast<uintptr_t>(w) % 16))) return false;
+  pl->spr = (int)((rowbytes + 127) / 128);
+  pl->kchunks = 2 * pl->spr;
+  const int kpad = pl->kchunks * KC;
+  pl->cp = ((size_t)M * (kpad + 32) * 2 + gamma_bytes(PRO, K) <= (size_t)kStageBudget) ? kpad + 32 : kpad;
+  const size_t act = align_up((size_t)M * pl->cp * 2 + gamma_bytes(PRO, K), 16);
+  const size_t fixed = (size_t)kRingFixedBytes + act + kRingStaticBytes;
+  if (fixed + (size_t)kRingMinStages * kRingStageBytes > kRingSmemMax) return false;
+  pl->stages = (int)std::min<size_t>(kRingMaxStages, (kRingSmemMax - fixed) / kRingStageBytes);
+  pl->smem = (size_t)kRingFixedBytes + (size_t)pl->stages * kRingStageBytes + act;
+  pl->rowblocks = (N + kRingRows - 1) / kRingRows;
+  pl->tiles = pl->rowblocks * (kRingRows / 16);
+  if (pl->tiles > kMaxSplitTiles) return false;
+  const int sms = device_sm_count();
+  const long long total = (long long)pl->rowblocks * pl->spr;
+  const long long target = std::max<long long>(1, total / ((long long)sms * ring_units_per_cta()));
+  int nst = 1;
+  while (nst * 2 <= std::min<long long>(target, kRingMaxUnit) && nst * 2 <= pl->spr) nst *= 2;
+  pl->nst = nst;
+  pl->upr = (pl->spr + nst - 1) / nst;
+  pl->units = pl->rowblocks * pl->upr;
+  pl->grid = std::min(sms, pl->units);
+  pl->ws_bytes = kCounterBytes + (pl->upr > 1 ? (size_t)pl->tiles * pl->upr * 32 * 4 * 4 : 0);
+  return true;
+}
+
+template <int BITS, int PRO, int EPI>
+cudaError_t launch_ring(StreamParams p, const RingPlan& pl, void* ws, int sched_set, cudaStream_t s, bool pdl) {
+  RingParams rp;
+  memset(&rp, 0, sizeof(rp));
+  const size_t rowbytes = (size_t)p.K * BITS / 8;
+  if (!encode_2d(&rp.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, rowbytes, (uint64_t)p.N, rowbytes, 128, kRingRows,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  p.kchunks = pl.kchunks;
+  p.cp = pl.cp;
+  p.tiles = pl.tiles;
+  p.gshift = BITS < 16 ? group_shift(p.K, p.G) : 31;
+  rp.p = p;
+  rp.spr = pl.spr;
+  rp.nst = pl.nst;
+  rp.upr = pl.upr;
+  rp.units = pl.units;
+  rp.stages = pl.stages;
+  rp.sched = sched_counters(ws, sched_set);
+  rp.counters = static_cast<int*>(ws);
+  rp.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
+  auto kern = gemv_ring_kernel<BITS, PRO, EPI>;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+  if (e != cudaSuccess) return e;
+  return lw_launch(kern, dim3(pl.grid), dim3(kRingThreads), pl.smem, s, pdl, rp);
+}
+
 // Which plan a launch of these sizes uses: the bulk-copy kernel when it
 // applies (its tiles kept whole if the workspace is too small to split),
 // else the register-pipeline kernel.
@@ -179,7 +276,12 @@ cudaError_t launch_tma(StreamParams p, const StreamPlan& pl, void* ws, cudaStrea
 // large enough workspace the plan keeps tiles whole.
 template <int BITS, int PRO, int EPI>
 cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl,
-                                bool allow_fold = false) {
+                                bool allow_fold = false, int sched_set = 0) {
+  if (!allow_fold || !fold_scales<BITS>(p.K, p.G)) {
+    RingPlan rpl;
+    if (ws && plan_ring<BITS, PRO>(p.M, p.N, p.K, p.w, &rpl) && rpl.ws_bytes <= ws_bytes)
+      return launch_ring<BITS, PRO, EPI>(p, rpl, ws, sched_set, s, pdl);
+  }
   StreamPlan pl;
   if constexpr (BITS != 16 && EPI != EPI_PEER_ARGMAX) {
     if (choose_tma<BITS, PRO>(p.M, p.N, p.K, ws_bytes, &pl)) {
@@ -246,6 +348,11 @@ size_t stream_workspace(int M, int N, int K) {
   const int rows = stage_rows<BITS>(K);
   for (int m0 = 0; m0 < M; m0 += rows) {
     const int mb = std::min(rows, M - m0);
+    RingPlan rpl;
+    if (plan_ring<BITS, PRO>(mb, N, K, nullptr, &rpl)) {
+      need = std::max(need, rpl.ws_bytes);
+      continue;
+    }
     StreamPlan pl;
     if (BITS != 16 && EPI != EPI_PEER_ARGMAX && tma_enabled() && plan_tma<BITS, PRO>(mb, N, K, true, &pl)) {
       need = std::max(need, pl.ws_bytes);

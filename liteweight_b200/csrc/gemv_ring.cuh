@@ -1,0 +1,393 @@
+// Dequant GEMV for M <= 8 whose weight stream runs through a CTA-wide shared
+// memory ring fed by TMA tile copies (sm_100a).
+//
+// Same arithmetic, prologues and epilogues as gemv_stream_kernel
+// (gemv_core.cuh): out[m, n] = sum_k act[m, k] * W[n, k] with every weight
+// dequantized exactly (fp16(code * scale), liteweight/quantize.py:30-43,
+// :102-128), fp32 tensor-core sums, one fp16 rounding.
+//
+// Work. The weight matrix is cut into row blocks of 128 rows; a row block's
+// bytes into stages of 128 bytes per row (one 16 KB TMA box, 128-byte
+// swizzle); `nst` consecutive stages of one row block make a unit. Units are
+// handed out dynamically: CTA b starts with unit b and claims the next one
+// from a global counter (kept in the workspace; the last CTA to finish
+// claiming resets it), so SMs that get less memory bandwidth simply take
+// fewer units and all CTAs finish within about one unit of each other.
+//
+// Roles (one CTA per SM, 17 warps):
+//   warp 16    one lane claims units and issues each stage's TMA copy into
+//              the next free ring slot, writing the stage's unit id (and the
+//              unit this CTA takes after it) into the slot's header; the
+//              other lanes prefetch the unit's scale rows into L2. It starts
+//              before griddepcontrol.wait: weights do not depend on the
+//              previous kernel, so up to `stages` x 16 KB per SM stream in
+//              while that kernel finishes.
+//   warps 0-15 warp w owns tile w % 8 (16 rows) of the row block and chunk
+//              w / 8 (64 bytes per row) of every stage: per stage each lane
+//              reads 16 bytes of two rows, unpacks and scales them, and feeds
+//              mma.sync m16n8k16 with the staged activation as operand B.
+//              Each lane loads its scales for a whole unit at once, one unit
+//              ahead (the header names the next unit). At the end of a unit
+//              warp w + 8 hands its partial to warp w through shared memory
+//              (two buffers per tile, each guarded by a full / empty mbarrier);
+//              warp w finishes the tile (whole-row units) or combines it with
+//              the other units of the row block through the workspace slots,
+//              in unit order (deterministic, as gemv_stream_kernel's split
+//              tiles).
+// Lane (g, t) of a consumer warp holds tile rows pi(g) and pi(g) + 8, pi(g) =
+// (g >> 1) | ((g & 1) << 2): with the 128-byte swizzle (16-byte piece j of
+// row r at piece j ^ (r & 7)) the 8 lanes of each quarter warp then read 8
+// distinct bank groups. The epilogues take pi(g) as the lane's row.
+//
+// Every mbarrier wait is bounded: on expiry the kernel records LW_ERR_TIMEOUT
+// (device error flag), the roles stop at their next wait, and the producer
+// waits (bounded) for the copies it issued before the CTA exits.
+#pragma once
+
+#include <cuda.h>   // CUtensorMap
+
+#include "gemv_core.cuh"
+
+namespace lw {
+
+constexpr int kRingConsumerWarps = 16;
+constexpr int kRingConsumers = kRingConsumerWarps * 32;
+constexpr int kRingThreads = kRingConsumers + 32;
+constexpr int kRingRows = 128;                         // rows per row block (TMA box rows)
+constexpr int kRingStageBytes = kRingRows * 128;       // one 128 x 128-byte box
+constexpr int kRingMaxStages = 13;
+constexpr int kRingMaxUnit = 8;                        // stages per unit, at most
+constexpr int kRingHeadBytes = 1024;                   // barriers + headers
+constexpr int kRingCombBytes = 2 * 8 * 32 * 4 * 4;     // warp-pair hand-off, two parities, MT = 1
+// shared memory a launch needs besides its ring and staged activation (the
+// ring starts on a 1024-byte boundary, hence the slack)
+constexpr int kRingFixedBytes = kRingHeadBytes + kRingCombBytes + 1024;
+constexpr long long kRingWaitNs = 2000000000;          // 2 s: far beyond any healthy wait
+constexpr int kRingSchedInts = 4;                      // per schedule set: claim counter, done counter, pad
+
+struct RingParams {
+  StreamParams p;          // matmul, prologue, epilogue (p.kchunks = 2 * spr, p.cp staged row stride)
+  CUtensorMap tm_w;        // [N rows][K * BITS / 8 bytes] u8, box {128, 128}, 128-byte swizzle
+  int spr;                 // stages per row block (ceil(row bytes / 128))
+  int nst;                 // stages per unit
+  int upr;                 // units per row block (ceil(spr / nst))
+  int units;               // row blocks * upr
+  int stages;              // ring slots
+  int* sched;              // {claims, done}: zero before the first launch, left zero
+  float* slots;            // upr > 1: [tiles][upr][32][4] partial tiles
+  int* counters;           // upr > 1: [tiles] arrivals, zero before the first launch, left zero
+};
+
+LW_DEV void tma_load_box(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+LW_DEV void mbar_arrive_local(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+LW_DEV void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
+// Arrival on a split tile's counter: release (the warp's slot stores, ordered
+// before it by __syncwarp) and acquire (the other units' slots, when last) in
+// one GPU-scope round trip.
+LW_DEV int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// The lane's lower tile row (see the file comment).
+LW_DEV int ring_row(int g) { return (g >> 1) | ((g & 1) << 2); }
+
+template <int BITS, int PRO, int EPI>
+__global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid_constant__ RingParams rp) {
+  constexpr int MT = 1;
+  constexpr int E = WT<BITS>::E;
+  constexpr int KC = 4 * E;
+  constexpr bool SCALED = BITS < 16;
+  const StreamParams& p = rp.p;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ float ssq[kMaxM * kRingConsumerWarps];
+  __shared__ volatile int abort_s;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int S = rp.stages;
+  // layout: [ring barriers, headers, hand-off barriers | hand-off buffers |
+  // ring (1024-aligned: the swizzle pattern follows address bits 4-9) |
+  // staged activation, gamma]
+  const uint32_t base = smem_u32(smem_raw);
+  const uint32_t full0 = base, empty0 = base + 8u * kRingMaxStages;
+  int* hdr = reinterpret_cast<int*>(smem_raw + 16 * kRingMaxStages);   // [S][2]: unit, next unit
+  const uint32_t hfull0 = base + 512, hempty0 = base + 512 + 8 * 16;     // [tile][parity]
+  float* comb = reinterpret_cast<float*>(smem_raw + kRingHeadBytes);
+  const uint32_t ring_addr = (base + (uint32_t)(kRingHeadBytes + kRingCombBytes) + 1023u) & ~1023u;
+  uint8_t* ring = smem_raw + (ring_addr - base);
+  __half* act_s = reinterpret_cast<__half*>(ring + (size_t)S * kRingStageBytes);
+  __half* gam_s = act_s + (size_t)p.M * p.cp;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, kRingConsumerWarps);
+    }
+    for (int h = 0; h < 16; ++h) {
+      mbar_init(hfull0 + 8u * h, 32);
+      mbar_init(hempty0 + 8u * h, 32);
+    }
+    abort_s = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort_s) return false;
+    if (mbar_wait_bounded(bar, parity, kRingWaitNs)) return true;
+    abort_s = 1;
+    return false;
+  };
+
+  if (warp == kRingConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    int* sched = rp.sched;
+    auto claim = [&]() -> int {   // the next unit of this CTA, or rp.units when none is left
+      int c = 0;
+      if (lane == 0) c = (int)gridDim.x + atomicAdd(sched, 1);
+      c = __shfl_sync(0xffffffffu, c, 0);
+      return c < rp.units ? c : rp.units;
+    };
+    const int ngroups = SCALED ? p.K / p.G : 1;
+    int u = (int)blockIdx.x < rp.units ? (int)blockIdx.x : rp.units;
+    int nxt = u < rp.units ? claim() : rp.units;
+    int slot = 0;
+    uint32_t phase = 0;             // parity of the ring's current lap
+    uint32_t issued = 0;            // bit s: slot s holds a copy issued in the current lap or later
+    bool live = true;
+    if (u >= rp.units) nxt = rp.units;
+    while (live && u < rp.units) {
+      const int nn = nxt < rp.units ? claim() : rp.units;   // claimed one unit ahead of its use
+      const int rb = u / rp.upr, st0 = (u - rb * rp.upr) * rp.nst;
+      const int nst = min(rp.nst, rp.spr - st0);
+      if constexpr (SCALED) {
+        // the unit's scale rows into L2 (4 rows per lane), so that the
+        // consumers' loads one unit from now hit
+        const int g0 = min((st0 * 2 * KC) >> p.gshift, ngroups - 1);
+        for (int r = lane; r < kRingRows; r += 32) {
+          const int row = min(rb * kRingRows + r, p.N - 1);
+          prefetch_l2_line(p.scales + (size_t)row * ngroups + g0);
+        }
+      }
+      for (int st = 0; st < nst; ++st) {
+        // the slot's previous contents have been read by all consumer warps
+        if (!wait(empty0 + 8u * slot, phase ^ 1u)) {
+          live = false;
+          break;
+        }
+        if (lane == 0) {
+          hdr[2 * slot] = u;
+          hdr[2 * slot + 1] = nxt;
+          mbar_arrive_expect_tx(full0 + 8u * slot, (uint32_t)kRingStageBytes);
+          tma_load_box(ring_addr + (uint32_t)slot * kRingStageBytes, &rp.tm_w, (st0 + st) * 128,
+                       rb * kRingRows, full0 + 8u * slot);
+        }
+        issued |= 1u << slot;
+        if (++slot == S) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+      u = nxt;
+      nxt = nn;
+    }
+    if (live) {
+      // end of work: an empty stage with header -1
+      if (wait(empty0 + 8u * slot, phase ^ 1u)) {
+        if (lane == 0) {
+          hdr[2 * slot] = -1;
+          hdr[2 * slot + 1] = -1;
+          mbar_arrive_local(full0 + 8u * slot);
+        }
+      } else {
+        live = false;
+      }
+    }
+    if (lane == 0) {
+      // the last CTA to finish claiming resets the schedule for the next launch
+      __threadfence();
+      if (atomicAdd(sched + 1, 1) == (int)gridDim.x - 1) {
+        sched[0] = 0;
+        sched[1] = 0;
+        __threadfence();
+      }
+    }
+    // No copy may land after the CTA has exited: wait (bounded) for each
+    // slot's newest copy - this lap's for the slots before `slot`, the last
+    // lap's for the others. In a healthy run they have landed or land while
+    // the consumers drain the ring.
+    for (int s = 0; s < S; ++s) {
+      if (!((issued >> s) & 1u)) continue;
+      mbar_wait_bounded(full0 + 8u * s, (s < slot) ? phase : (phase ^ 1u), kRingWaitNs);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int g = lane >> 2, t = lane & 3;
+  const int tw = warp & 7, c = warp >> 3;
+  const int gr = ring_row(g);
+  const int ngroups = SCALED ? p.K / p.G : 1;
+  const unsigned short* sbase = reinterpret_cast<const unsigned short*>(p.scales);
+  // this lane's 16-byte piece of a stage, rows gr and gr + 8 of tile tw
+  const uint32_t piece_off = (uint32_t)((tw * 16 + gr) * 128 + (((4 * c + t) ^ gr) << 4));
+
+  // scales of a unit: one fp16 per stage for each of the lane's two rows
+  // (lo = row gr, hi = row gr + 8), loaded for the whole unit at once
+  auto load_scales = [&](int unit, uint32_t (&sv)[kRingMaxUnit]) {
+    if constexpr (SCALED) {
+      if (unit >= rp.units) return;
+      const int rb = unit / rp.upr, st0 = (unit - rb * rp.upr) * rp.nst;
+      const int nst = min(rp.nst, rp.spr - st0);
+      const int r0 = min(rb * kRingRows + tw * 16 + gr, p.N - 1);
+      const int r1 = min(rb * kRingRows + tw * 16 + gr + 8, p.N - 1);
+      const unsigned short* s0 = sbase + (size_t)r0 * ngroups;
+      const unsigned short* s1 = sbase + (size_t)r1 * ngroups;
+#pragma unroll
+      for (int st = 0; st < kRingMaxUnit; ++st) {
+        if (st < nst) {
+          const int grp = min((((st0 + st) * 2 + c) * KC + t * E) >> p.gshift, ngroups - 1);
+          sv[st] = (uint32_t)__ldg(s0 + grp) | ((uint32_t)__ldg(s1 + grp) << 16);
+        }
+      }
+    }
+  };
+
+  uint32_t cur[kRingMaxUnit], nx[kRingMaxUnit];
+#pragma unroll
+  for (int i = 0; i < kRingMaxUnit; ++i) cur[i] = nx[i] = 0;
+  load_scales((int)blockIdx.x, cur);   // the first unit is blockIdx.x: its scales before the wait
+
+  stage_gamma<PRO, kRingConsumers>(p, gam_s);
+  pdl_wait();
+  pdl_launch_dependents();
+  uint32_t in_flag = 0, out_flag = 0;
+  if constexpr (PRO == PRO_PEER_RESID_NORM) in_flag = exchange_flag(*p.in_step, p.in_tag, p.in_tags);
+  if constexpr (kPeerEpi<EPI>) out_flag = exchange_flag(*p.out_step, p.out_tag, p.out_tags);
+  WaitBudget wb;
+  stage_activation<BITS, PRO, kRingConsumers, 1>(p, act_s, gam_s, ssq, in_flag, wb);
+
+  const __half* arow[MT] = {act_s + (size_t)min(g, p.M - 1) * p.cp + t * 8};
+  int slot = 0;
+  uint32_t phase = 0;
+  int nunit = 0;   // units done: hand-off buffer nunit & 1, its use count nunit >> 1
+  for (;;) {
+    if (!wait(full0 + 8u * slot, phase)) break;
+    const int u = hdr[2 * slot];
+    if (u < 0) break;
+    const int nxt = hdr[2 * slot + 1];
+    load_scales(nxt, nx);
+    const int rb = u / rp.upr, ks = u - rb * rp.upr, st0 = ks * rp.nst;
+    const int nst = min(rp.nst, rp.spr - st0);
+    float acc[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
+    bool ok = true;
+#pragma unroll
+    for (int st = 0; st < kRingMaxUnit; ++st) {
+      if (st >= nst) break;
+      if (st > 0 && !wait(full0 + 8u * slot, phase)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* sp = ring + (size_t)slot * kRingStageBytes + piece_off;
+      const uint4 qa = lds128(sp), qb = lds128(sp + 8 * 128);
+      const int off = ((st0 + st) * 2 + c) * KC;
+      uint32_t sa = 0, sb = 0;
+      if constexpr (SCALED) {
+        sa = __byte_perm(cur[st], 0, 0x1010);
+        sb = __byte_perm(cur[st], 0, 0x3232);
+      }
+      gemv_piece<BITS, MT>(acc, qa, qb, sa, sb, arow, off);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_local(empty0 + 8u * slot);
+      if (++slot == S) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
+    if (!ok) break;
+    // ---- the unit's tile partials: warp w + 8 hands its half to warp w
+    const int par = nunit & 1;
+    const uint32_t use = (uint32_t)(nunit >> 1);
+    ++nunit;
+    const uint32_t hf = hfull0 + 8u * (2 * tw + par), he = hempty0 + 8u * (2 * tw + par);
+    float* cb = comb + (((size_t)par * 8 + tw) * 32 + lane) * 4;
+    if (c == 1) {
+      // the buffer's previous contents (two units ago) have been read
+      if (use > 0 && !wait(he, (use - 1) & 1u)) break;
+      *reinterpret_cast<float4*>(cb) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+      mbar_arrive_local(hf);
+    } else {
+      if (!wait(hf, use & 1u)) break;
+      const float4 o = *reinterpret_cast<const float4*>(cb);
+      mbar_arrive_local(he);
+      acc[0][0] += o.x;
+      acc[0][1] += o.y;
+      acc[0][2] += o.z;
+      acc[0][3] += o.w;
+      const int tile = rb * 8 + tw;
+      if (tile * 16 < p.N) {
+        if (rp.upr == 1) {
+          finish_tile<MT, EPI>(p, tile, acc, lane, out_flag, gr);
+        } else {
+          float* mine = rp.slots + (((size_t)tile * rp.upr + ks) * 32 + lane) * 4;
+          *reinterpret_cast<float4*>(mine) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+          __syncwarp();
+          int old = 0;
+          if (lane == 0) old = atom_add_acq_rel_gpu(rp.counters + tile, 1);
+          old = __shfl_sync(0xffffffffu, old, 0);
+          if (old == rp.upr - 1) {
+            __syncwarp();   // lane 0's acquire, then every lane reads the slots (from L2)
+            float sum[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
+            const float* src = rp.slots + ((size_t)tile * rp.upr * 32 + lane) * 4;
+            for (int k = 0; k < rp.upr; ++k) {
+              const float4 f = __ldcg(reinterpret_cast<const float4*>(src + (size_t)k * 32 * 4));
+              sum[0][0] += f.x;
+              sum[0][1] += f.y;
+              sum[0][2] += f.z;
+              sum[0][3] += f.w;
+            }
+            finish_tile<MT, EPI>(p, tile, sum, lane, out_flag, gr);
+            if (lane == 0) rp.counters[tile] = 0;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kRingMaxUnit; ++i) cur[i] = nx[i];
+  }
+
+  if constexpr (EPI == EPI_PEER_ARGMAX) {
+    // The last CTA to finish (every CTA's atomicMax is then in the local keys)
+    // sends this rank's keys to every rank as flagged words.
+    __shared__ int s_last;
+    named_sync(1, kRingConsumers);
+    if (tid == 0) {
+      __threadfence();
+      s_last = atomicAdd(p.out_arrivals, 1) == (int)gridDim.x - 1;
+    }
+    named_sync(1, kRingConsumers);
+    if (s_last) {
+      __threadfence();
+      const unsigned long long f16 = (unsigned long long)exchange_flag16(out_flag) << 48;
+      for (int m = tid; m < p.M; m += kRingConsumers) {
+        const unsigned long long word = (__ldcg(p.argmax_keys + m) & 0xFFFFFFFFFFFFull) | f16;
+#pragma unroll
+        for (int d = 0; d < kMaxRanks; ++d)
+          if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + (size_t)p.out_rank * p.M + m, word);
+      }
+      if (tid == 0) *p.out_arrivals = 0;
+    }
+  }
+}
+
+}  // namespace lw

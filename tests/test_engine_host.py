@@ -13,7 +13,7 @@ from liteweight_b200 import build as lwbuild
 def test_struct_layout_matches_library():
     lwbuild.build()
     E.check_abi()
-    assert ctypes.sizeof(E.FusedGemvArgs) == 248 and ctypes.sizeof(E.AttentionArgs) == 72
+    assert ctypes.sizeof(E.FusedGemvArgs) == 256 and ctypes.sizeof(E.AttentionArgs) == 72
     assert ctypes.sizeof(E.ExchangeOut) == 96 and ctypes.sizeof(E.ExchangeIn) == 48
 
 

@@ -380,3 +380,49 @@ def test_graph_survives_workspace_growth():
         del junk
     check_rows(out1, oq.packed_matmul(act1, q1, sc1, 128, 4), "graph replay after workspace growth")
     check_rows(big, oq.packed_matmul(act2, q2, sc2, 128, 4), "the call that grew the workspace")
+
+
+@pytest.mark.parametrize("bits,M,K,N,G", [
+    (4, 1, 2080, 1000, 32),      # row bytes 1040: the last 128-byte stage half past K; N not whole row blocks
+    (8, 3, 2064, 200, 16),       # INT8 row bytes 2064; 200 rows = 2 row blocks, the second ragged
+    (4, 8, 4096, 4096, 4096),    # per-output-channel scales (G = K), eight rows
+    (8, 1, 2048, 8192, 2048),    # the single W8A16 QuantLinear: per-output-channel, M = 1
+    (4, 2, 14336, 4096, 128),    # a long row (112 stages): many units per row block
+    (16, 5, 4096, 3000, 4096),   # fp16 weights
+])
+def test_ring_edges(bits, M, K, N, G):
+    """M <= 8 shapes on the TMA-ring GEMV: ragged row blocks, partial last
+    stages, per-channel scales, long rows; bit-identical on a repeat call (the
+    dynamic unit schedule does not change the sums) and the workspace's
+    counters (work claims included) are zero again afterwards."""
+    from liteweight_b200 import _native as nat
+    rng = np.random.default_rng(bits * 31 + M)
+    act = rng.standard_normal((M, K)).astype(np.float16)
+    if bits == 16:
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
+        q, s, ref = w, None, oq.matmul_dequant(act, w)
+    else:
+        q, s = quantized(N, K, G, bits, seed=N + K)
+        ref = oq.packed_matmul(act, q, s, G, bits)
+    a = torch.from_numpy(act).to(DEV)
+    qt = torch.from_numpy(q).to(DEV)
+    st = torch.from_numpy(s).to(DEV) if s is not None else None
+    need = int(nat.lib().lw_gemm_workspace_size(bits, M, N, K))
+    assert need >= 64 * 1024
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for _ in range(2):
+        o = torch.empty(M, N, dtype=torch.float16, device=DEV)
+        if bits == 16:
+            nat.call("lw_gemm_f16", a.data_ptr(), qt.data_ptr(), o.data_ptr(), M, N, K, ws.data_ptr(), need, stream)
+        else:
+            fn = "lw_gemm_w4a16" if bits == 4 else "lw_gemm_w8a16"
+            nat.call(fn, a.data_ptr(), qt.data_ptr(), st.data_ptr(), None, o.data_ptr(), M, N, K, G,
+                     ws.data_ptr(), need, stream)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert nat.lib().lw_take_device_error() == 0
+    check_rows(outs[0], ref, f"ring bits={bits} {M}x{K}x{N} G{G}")
+    assert torch.equal(outs[0], outs[1])
+    assert int(ws[: 64 * 1024].count_nonzero()) == 0
