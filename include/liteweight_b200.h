@@ -116,6 +116,18 @@ int lw_gemm_f16(const void* a, const void* w, void* out, int M, int N, int K, vo
  * for a contiguous b. */
 int lw_gemm_f16_kn(const void* a, const void* b, void* out, int M, int N, int K, lw_stream_t stream);
 
+/* ---- quantization on the GPU (bit-exact with liteweight/quantize.py:7-27, :65-99) ----
+ * weight [N,K] fp16 (weight_fp32 = 0) or fp32 (1); per group of group_size
+ * consecutive k: scale = max(absmax / 127 (INT8) or / 7 (INT4), 1e-8) in fp32,
+ * code = round-half-even(w / scale) clipped to [-127,127] / [-8,7], scales
+ * stored fp16 [N,K/group_size]; INT4 codes packed uint8 [N,K/2], even k in the
+ * low nibble. Replaces quantize_int8 / quantize_int4 for device tensors
+ * (liteweight/quantize.py:7, :65); weights must be finite. */
+int lw_quantize_int8(const void* weight, int weight_fp32, void* qweight, void* scales, int N, int K,
+                     int group_size, lw_stream_t stream);
+int lw_quantize_int4(const void* weight, int weight_fp32, void* qweight, void* scales, int N, int K,
+                     int group_size, lw_stream_t stream);
+
 /* ---- dequantization (bit-exact with liteweight/quantize.py:30-43, :102-128) ----
  * out fp16 [N,K] = fp16((float)code * (float)scale). */
 int lw_dequant_w8(const void* qweight, const void* scales, void* out, int N, int K, int group_size,

@@ -34,6 +34,8 @@ _SIGNATURES: dict[str, list] = {
     "lw_gemm_f16_kn": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
     "lw_dequant_w8": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
     "lw_dequant_w4": [c_void_p] * 3 + [c_int] * 3 + [c_void_p],
+    "lw_quantize_int8": [c_void_p, c_int, c_void_p, c_void_p] + [c_int] * 3 + [c_void_p],
+    "lw_quantize_int4": [c_void_p, c_int, c_void_p, c_void_p] + [c_int] * 3 + [c_void_p],
 }
 _RESTYPE = {"lw_status_string": ctypes.c_char_p, "lw_launch_count": ctypes.c_ulonglong,
             "lw_gemm_workspace_size": ctypes.c_size_t}

@@ -62,7 +62,12 @@ constexpr int kRingCombBytes = 2 * 8 * 32 * 4 * 4;     // warp-pair hand-off, tw
 // shared memory a launch needs besides its ring and staged activation (the
 // ring starts on a 1024-byte boundary, hence the slack)
 constexpr int kRingFixedBytes = kRingHeadBytes + kRingCombBytes + 1024;
-constexpr long long kRingWaitNs = 2000000000;          // 2 s: far beyond any healthy wait
+constexpr long long kRingWaitNs = 2000000000;          // 2 s: far beyond any copy or hand-off
+// The producer's wait for a free slot also spans the consumers' wait for the
+// previous kernel (programmatic dependent launch) and their wait for other
+// ranks (PRO_PEER_RESID_NORM, up to in_timeout_ns): its bound is this much
+// longer than the latter.
+constexpr long long kRingProducerWaitNs = 60000000000LL;
 constexpr int kRingSchedInts = 4;                      // per schedule set: claim counter, done counter, pad
 
 struct RingParams {
@@ -148,6 +153,21 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     abort_s = 1;
     return false;
   };
+  // the producer's wait for a free slot: long bound, gives up at once when
+  // a consumer has aborted
+  auto wait_free = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long limit = kRingProducerWaitNs + (PRO == PRO_PEER_RESID_NORM ? p.in_timeout_ns : 0);
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if (abort_s) return false;
+      if ((it & 255u) == 0u && (long long)(globaltimer_ns() - t0) > limit) break;
+    }
+    lw_record_error(LW_ERR_TIMEOUT);
+    abort_s = 1;
+    return false;
+  };
 
   if (warp == kRingConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -181,7 +201,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       }
       for (int st = 0; st < nst; ++st) {
         // the slot's previous contents have been read by all consumer warps
-        if (!wait(empty0 + 8u * slot, phase ^ 1u)) {
+        if (!wait_free(empty0 + 8u * slot, phase ^ 1u)) {
           live = false;
           break;
         }
@@ -203,7 +223,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     }
     if (live) {
       // end of work: an empty stage with header -1
-      if (wait(empty0 + 8u * slot, phase ^ 1u)) {
+      if (wait_free(empty0 + 8u * slot, phase ^ 1u)) {
         if (lane == 0) {
           hdr[2 * slot] = -1;
           hdr[2 * slot + 1] = -1;

@@ -13,7 +13,9 @@ drop-in contract, so the arithmetic is necessarily the same):
   On CUDA tensors it runs the library's bit-exact dequant kernel.
 
 These run wherever the tensors are (quantization happens on CPU when an HF
-model is converted there); none of them is on the matmul hot path.
+model is converted there); none of them is on the matmul hot path. CUDA
+tensors go through the library's kernels (lw_quantize_*, lw_dequant_*), which
+give the same bits.
 """
 
 from __future__ import annotations
@@ -34,8 +36,25 @@ def _rtn(weight: Tensor, group_size: int, qmax: float, lo: int, hi: int) -> tupl
     return q, scale.reshape(n, k // group_size).half()
 
 
+def _quant_cuda(fn: str, weight: Tensor, group_size: int, packed: bool) -> tuple[Tensor, Tensor]:
+    assert weight.ndim == 2, "weight must be [N, K]"
+    n, k = weight.shape
+    assert k % group_size == 0, f"K={k} must be divisible by group_size={group_size}"
+    if weight.dtype not in (torch.float16, torch.float32):
+        weight = weight.float()
+    weight = weight.contiguous()
+    q = torch.empty((n, k // 2) if packed else (n, k), dtype=torch.uint8 if packed else torch.int8,
+                    device=weight.device)
+    s = torch.empty((n, k // group_size), dtype=torch.float16, device=weight.device)
+    nat.call(fn, weight.data_ptr(), int(weight.dtype == torch.float32), q.data_ptr(), s.data_ptr(), n, k,
+             group_size, nat.stream_of(weight))
+    return q, s
+
+
 def quantize_int8(weight: Tensor, group_size: int = 128) -> tuple[Tensor, Tensor]:
     """fp16/fp32 [N, K] -> (int8 [N, K], fp16 scales [N, K // group_size])."""
+    if weight.is_cuda:
+        return _quant_cuda("lw_quantize_int8", weight, group_size, False)
     return _rtn(weight, group_size, 127.0, -127, 127)
 
 
@@ -59,6 +78,8 @@ def quantize_int4(weight: Tensor, group_size: int = 128) -> tuple[Tensor, Tensor
     """fp16/fp32 [N, K] -> (uint8 packed [N, K // 2], fp16 scales [N, K // group_size])."""
     assert weight.ndim == 2, "weight must be [N, K]"
     assert weight.shape[1] % 2 == 0
+    if weight.is_cuda:
+        return _quant_cuda("lw_quantize_int4", weight, group_size, True)
     q, s = _rtn(weight, group_size, 7.0, -8, 7)
     return pack_int4(q), s
 

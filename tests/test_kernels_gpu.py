@@ -410,6 +410,7 @@ def test_ring_edges(bits, M, K, N, G):
     need = int(nat.lib().lw_gemm_workspace_size(bits, M, N, K))
     assert need >= 64 * 1024
     ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    nat.lib().lw_take_device_error()   # start from clear device error flags
     stream = torch.cuda.current_stream().cuda_stream
     outs = []
     for _ in range(2):
@@ -426,3 +427,44 @@ def test_ring_edges(bits, M, K, N, G):
     check_rows(outs[0], ref, f"ring bits={bits} {M}x{K}x{N} G{G}")
     assert torch.equal(outs[0], outs[1])
     assert int(ws[: 64 * 1024].count_nonzero()) == 0
+
+
+def test_quantize_kernels_bit_exact(golden_dir):
+    """lw_quantize_int8/int4 reproduce the reference's quantize_int8/int4
+    bit for bit on its golden vectors (every group size there, round-half-even
+    ties, the per-output-channel case), from fp16 and from fp32 weights."""
+    from liteweight_b200 import quantize as lq
+    qg = dict(np.load(golden_dir / "quant_golden.npz"))
+    names = sorted({k.split("/")[0] for k in qg if k.endswith("/W")})
+    assert names
+    for name in names:
+        W, G = qg[f"{name}/W"], int(qg[f"{name}/G"])
+        for dt in (torch.float16, torch.float32):
+            if W.dtype == np.float32 and dt == torch.float16:
+                continue   # an fp32 golden input is only exact as fp32
+            w = torch.from_numpy(W).to(device=DEV, dtype=dt)
+            q8, s8 = lq.quantize_int8(w, G)
+            q4, s4 = lq.quantize_int4(w, G)
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(q8.cpu().numpy(), qg[f"{name}/q8"], err_msg=f"{name} {dt}")
+            np.testing.assert_array_equal(s8.cpu().numpy().view(np.uint16), qg[f"{name}/s8"].view(np.uint16))
+            np.testing.assert_array_equal(q4.cpu().numpy(), qg[f"{name}/q4"], err_msg=f"{name} {dt}")
+            np.testing.assert_array_equal(s4.cpu().numpy().view(np.uint16), qg[f"{name}/s4"].view(np.uint16))
+
+
+@pytest.mark.parametrize("N,K,G", [(4096, 4096, 128), (1000, 2048, 2048), (64, 6, 3), (33, 60, 15), (128, 256, 32)])
+def test_quantize_kernels_match_oracle(N, K, G):
+    """Large, per-channel and odd group sizes (INT4 bytes straddling two groups)
+    against the numpy oracle, bit for bit."""
+    from liteweight_b200 import quantize as lq
+    rng = np.random.default_rng(N + K + G)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float16)
+    W[0, :G] = 0.0                                   # an all-zero group: scale clamped to 1e-8
+    w = torch.from_numpy(W).to(DEV)
+    for bits, fn, ofn in ((8, lq.quantize_int8, oq.quantize_int8), (4, lq.quantize_int4, oq.quantize_int4)):
+        q, s = fn(w, G)
+        rq, rs = ofn(W, G)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(q.cpu().numpy(), rq, err_msg=f"int{bits} codes {N}x{K} G{G}")
+        np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), rs.view(np.uint16),
+                                      err_msg=f"int{bits} scales {N}x{K} G{G}")
