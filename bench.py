@@ -391,7 +391,7 @@ class DecodeWorkload:
 
     def __init__(self, device, dist: "Dist", model: str, batch: int, extra_steps: int, fold: bool = False,
                  exchange: str = "peer", prompt: int | None = None, new: int | None = None,
-                 layers: int | None = None):
+                 layers: int | None = None, lm_head_bits: int = 16):
         import torch
         from liteweight_b200 import engine as E
         cfg = MODELS[model]
@@ -402,7 +402,8 @@ class DecodeWorkload:
         self.spec = E.LlamaSpec(**arch, bits=cfg["bits"], group_size=GROUP)
         self.B, self.P, self.T = batch, prompt or cfg["prompt"], new or cfg["new"]
         self.tp, self.rank = dist.world, dist.rank
-        self.metric = decode_metric(model, batch, self.P, self.tp)
+        self.lm_bits = lm_head_bits
+        self.metric = decode_metric(model, batch, self.P, self.tp, lm_head_bits)
         max_seq = self.P + max(self.T, extra_steps) + 1
         g = torch.Generator(device=device).manual_seed(20251201)
         spec = self.spec
@@ -416,12 +417,19 @@ class DecodeWorkload:
         norm = (1.0 + 0.1 * torch.randn(spec.hidden, device=device, generator=g)).half()
         cos, sin = E.rope_tables(E.default_inv_freq(spec.head_dim, spec.rope_theta), max_seq, 1.0, device)
         self.embed, self.norm, self.cos, self.sin = embed, norm, cos, sin
+        # the lm_head is the tied embedding: fp16 as liteweight keeps it, or quantized
+        # like swap_linears does when the head is not skipped
+        self.lm_quant = None
+        if lm_head_bits != 16:
+            from liteweight_b200.quantize import quantize_int4, quantize_int8
+            q, sc = (quantize_int4 if lm_head_bits == 4 else quantize_int8)(embed, GROUP)
+            self.lm_quant = (q, sc, lm_head_bits, GROUP)
         group = None
         if self.tp > 1:
             import torch.distributed as tdist
             group = tdist.group.WORLD
         self.eng = E.DecodeEngine(spec, packed, embed, norm, None, cos, sin, batch, max_seq, device, self.rank,
-                                  self.tp, group, fold_scales=fold, exchange=exchange)
+                                  self.tp, group, fold_scales=fold, exchange=exchange, lm_head_quant=self.lm_quant)
         gp = torch.Generator().manual_seed(7)
         self.prompt = torch.randint(0, spec.vocab, (batch, self.P), generator=gp)
         torch.cuda.synchronize()
@@ -464,7 +472,8 @@ class DecodeWorkload:
     def bytes_per_step(self, ctx: int) -> int:
         """Weight bytes (this rank's shard, incl. fp16 lm_head shard) + KV bytes read."""
         sp = self.spec
-        return sp.weight_bytes_per_token() // self.tp + self.B * sp.kv_bytes_per_position() * ctx // self.tp
+        return (sp.weight_bytes_per_token(lm_head_bits=self.lm_bits) // self.tp
+                + self.B * sp.kv_bytes_per_position() * ctx // self.tp)
 
     def kernel_stats(self, ctx: int) -> dict:
         """Per kernel class: one step's launches captured alone in a graph,
@@ -481,7 +490,8 @@ class DecodeWorkload:
             "o": wbytes(H, nq * hd) + 2 * self.B * nq * hd,
             "gu": wbytes(2 * I, H) + 2 * self.B * H,
             "down": wbytes(H, I) + 2 * self.B * I,
-            "lm_head": (sp.vocab // self.tp) * H * 2 + 2 * self.B * H,
+            "lm_head": ((sp.vocab // self.tp) * H * 2 if self.lm_bits == 16 else
+                        wbytes(sp.vocab // self.tp, H) * self.lm_bits // sp.bits) + 2 * self.B * H,
         }
         out = {}
         for name, b in per_launch.items():
@@ -588,7 +598,11 @@ class TorchDecodeReference:
                     x[b] = (xb.float() + self._lin(act, L.down, sp.bits, sp.group_size).float()).half()
                 del L
             h = self._rmsnorm(x[:, first:first + count], wl.norm, sp.eps)      # [B, count, H]
-            head = wl.embed.float()
+            if wl.lm_quant is not None:
+                q, sc, bits, grp = wl.lm_quant
+                head = self._dequant(q, sc, bits, grp)
+            else:
+                head = wl.embed.float()
             return h.float() @ head.t()
         finally:
             torch.backends.cuda.matmul.allow_tf32 = prev_tf32
@@ -627,25 +641,29 @@ def decode_parity(wl: DecodeWorkload, ids_host, rank: int, steps: int = 32) -> d
                          "matmul, HF fp16 rounding points), full depth, on the device"}
 
 
-def decode_config(model: str, batch: int, prompt: int, new: int, world: int, fold: bool, exchange: str) -> dict:
+def decode_config(model: str, batch: int, prompt: int, new: int, world: int, fold: bool, exchange: str,
+                  lm_head_bits: int = 16) -> dict:
     """The `config` object of a decode line (both arms print the same one)."""
     cfg = MODELS[model]
     from liteweight_b200 import engine as E
     spec = E.LlamaSpec(**getattr(E, cfg["arch"]), bits=cfg["bits"], group_size=GROUP)
     return {"workload": f"decode {cfg['name']} INT{cfg['bits']} G{GROUP}", "model": cfg["name"],
+            "lm_head": ("fp16 (liteweight skips it)" if lm_head_bits == 16
+                        else f"INT{lm_head_bits} G{GROUP} (swap_linears without the skip)"),
             "global_batch": batch, "prompt": prompt, "new_tokens": new, "seq_len": prompt + new,
             "parallelism": f"tp{world}",
             "dequant": "per-chunk fp32 scale" if fold else "exact fp16(code*scale)",
             "all_reduce": ("none" if world == 1 else
                            "in-kernel peer-memory exchange over NVLink" if exchange == "peer"
                            else "NCCL all_reduce in the step graph"),
-            "l2": f"inputs larger than L2 ({spec.weight_bytes_per_token() / world / 1e9:.2f} GB of weights per GPU "
-                  "per step)"}
+            "l2": f"inputs larger than L2 ({spec.weight_bytes_per_token(lm_head_bits=lm_head_bits) / world / 1e9:.2f}"
+                  " GB of weights per GPU per step)"}
 
 
-def decode_metric(model: str, batch: int, prompt: int, world: int) -> str:
+def decode_metric(model: str, batch: int, prompt: int, world: int, lm_head_bits: int = 16) -> str:
     cfg = MODELS[model]
-    return (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only, batch {batch}, "
+    head = "" if lm_head_bits == 16 else f", INT{lm_head_bits} lm_head"
+    return (f"decode tokens/s ({cfg['name']} INT{cfg['bits']} G{GROUP} weight-only{head}, batch {batch}, "
             f"prompt {prompt}, greedy, TP{world})")
 
 
@@ -660,11 +678,12 @@ class CpuDecode:
     random bytes (the work does not depend on the values); `distinct` layer
     sets are cycled through the L layer positions."""
 
-    def __init__(self, model: str, batch: int = 1, distinct: int = 4):
+    def __init__(self, model: str, batch: int = 1, distinct: int = 4, lm_head_bits: int = 16):
         import torch
         from liteweight_b200 import engine as E
         from oracle import torch_cpu
         self.torch, self.tc = torch, torch_cpu
+        self.lm_bits = lm_head_bits
         self.cores = os.cpu_count() or 1
         torch.set_num_threads(self.cores)
         cfg = MODELS[model]
@@ -689,6 +708,12 @@ class CpuDecode:
             self.layers.append(lin)
         self.acts = {k: torch.randn(batch, k, generator=g).half() for _n, _o, k in sp.linear_shapes()}
         self.lm = rows(sp.vocab, lambda r: (torch.rand(r, sp.hidden, generator=g) * 0.04 - 0.02).half())
+        if lm_head_bits != 16:   # a quantized head runs as one more QuantLinear
+            self.lm = rows(sp.vocab, lambda r: torch.randint(0, 256, (r, sp.hidden * lm_head_bits // 8),
+                                                             dtype=torch.uint8, generator=g)
+                           if lm_head_bits == 4 else
+                           torch.randint(-127, 128, (r, sp.hidden), dtype=torch.int8, generator=g))
+            self.lm_s = rows(sp.vocab, lambda r: (torch.rand(r, sp.hidden // GROUP, generator=g) * 2e-3).half())
         self.h = torch.randn(batch, sp.hidden, generator=g).half()
 
     def layer(self, li: int) -> float:
@@ -699,7 +724,10 @@ class CpuDecode:
 
     def lm_head(self) -> float:
         t = time.perf_counter()
-        self.tc.fp16_linear(self.h, self.lm)
+        if self.lm_bits == 16:
+            self.tc.fp16_linear(self.h, self.lm)
+        else:
+            self.tc.quant_linear(self.h, self.lm, self.lm_s, GROUP, self.lm_bits)
         return time.perf_counter() - t
 
     def token(self, budget_s: float = 90.0) -> dict:
@@ -713,14 +741,15 @@ class CpuDecode:
             if time.perf_counter() - t0 > budget_s:
                 break
         lm = self.lm_head()
+        head = "fp16" if self.lm_bits == 16 else f"INT{self.lm_bits}"
         layer_mean = sum(times) / len(times)
         tok_s = self.B / (layer_mean * L + lm)
         whole = len(times) == L
         return {"value": round(tok_s, 5), "unit": "tokens/s", "cores": self.cores, "kind": "port",
                 "seconds_per_token": round(layer_mean * L + lm, 3), "layer_seconds": round(layer_mean, 4),
                 "lm_head_seconds": round(lm, 4),
-                "sample": (f"one whole token: {L} layers x 7 quantized linears + the fp16 lm_head; "
-                           if whole else f"{len(times)} of {L} layers (x 7 linears) + the fp16 lm_head, "
+                "sample": (f"one whole token: {L} layers x 7 quantized linears + the {head} lm_head; "
+                           if whole else f"{len(times)} of {L} layers (x 7 linears) + the {head} lm_head, "
                                          f"extrapolated to {L} layers; ")
                           + f"batch {self.B}, torch dequantize + fp32 matmul (oracle/torch_cpu.py), "
                             f"torch.set_num_threads({self.cores})"}
@@ -897,7 +926,8 @@ def run_decode(args, dist: Dist):
     lwbuild.build()
     nat.lib()
     wl = DecodeWorkload(dev, dist, args.model, args.batch, args.warmup + args.steps, fold=args.fold,
-                        exchange=args.exchange, prompt=args.prompt, new=args.new, layers=args.layers)
+                        exchange=args.exchange, prompt=args.prompt, new=args.new, layers=args.layers,
+                        lm_head_bits=args.lm_head_bits)
     if dist.world > 1:   # NCCL communicator up before graph capture
         t = torch.zeros(1, device=dev)
         dist.pg.all_reduce(t)
@@ -957,13 +987,15 @@ def run_decode(args, dist: Dist):
         wl.eng.close()
         dist.close()
         return
-    cpu = CpuDecode(args.model, wl.B).token() if (dist.world == 1 and not args.no_cpu) else None
-    line = {"metric": decode_metric(args.model, wl.B, wl.P, dist.world), "value": round(value, 2),
+    cpu = (CpuDecode(args.model, wl.B, lm_head_bits=args.lm_head_bits).token()
+           if (dist.world == 1 and not args.no_cpu) else None)
+    line = {"metric": decode_metric(args.model, wl.B, wl.P, dist.world, args.lm_head_bits), "value": round(value, 2),
             "unit": "tokens/s", "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": f"int{wl.spec.bits} weights x fp16, fp32 acc",
             "data": "synthetic (random-init weights, uniform random prompt ids)",
-            "config": decode_config(args.model, wl.B, wl.P, wl.T, dist.world, args.fold, args.exchange),
+            "config": decode_config(args.model, wl.B, wl.P, wl.T, dist.world, args.fold, args.exchange,
+                                    args.lm_head_bits),
             "roofline": roofline, "decode_roofline": decode_roofline, "parity": parity, "gemv": gemv,
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(launches), "kernels": {k: {kk: v[kk] for kk in ("launches", "us", "GB/s")}
@@ -987,18 +1019,19 @@ def run_reference_decode(args, dist: Dist):
         return
     cfg = MODELS[args.model]
     P, T = args.prompt or cfg["prompt"], args.new or cfg["new"]
-    cpu = CpuDecode(args.model, args.batch)
+    cpu = CpuDecode(args.model, args.batch, lm_head_bits=args.lm_head_bits)
     for i in range(min(args.warmup, 3)):
         cpu.layer(i)
     t0 = time.perf_counter()
     tok = cpu.token()
     wall = time.perf_counter() - t0
-    line = {"impl": "reference", "metric": decode_metric(args.model, args.batch, P, args.gpus),
+    line = {"impl": "reference", "metric": decode_metric(args.model, args.batch, P, args.gpus, args.lm_head_bits),
             "value": tok["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(wall * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": f"int{cfg['bits']} codes, fp32 acc",
             "data": "synthetic (random codes and scales of the configuration's shapes)",
-            "config": decode_config(args.model, args.batch, P, T, args.gpus, args.fold, args.exchange),
+            "config": decode_config(args.model, args.batch, P, T, args.gpus, args.fold, args.exchange,
+                                    args.lm_head_bits),
             "cpu_baseline": tok,
             "e2e": {"value": tok["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -1017,6 +1050,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true", help="skip the decode line's parity check (profiling runs)")
     ap.add_argument("--no-gemv", action="store_true", help="skip the decode line's GEMV figures (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--lm-head-bits", type=int, choices=[16, 8, 4], default=16,
+                    help="16: fp16 lm_head as liteweight keeps it (default); 8 / 4: quantized (opt-in)")
     ap.add_argument("--fold", action="store_true",
                     help="decode GEMVs scale each chunk sum in fp32 instead of dequantizing exactly")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",

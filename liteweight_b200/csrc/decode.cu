@@ -636,7 +636,11 @@ inline bool al(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p)
   X(4, lw::PRO_PLAIN, lw::EPI_F32)                          \
   X(8, lw::PRO_PLAIN, lw::EPI_F32)                          \
   X(16, lw::PRO_NORM, lw::EPI_ARGMAX)                       \
-  X(16, lw::PRO_RESID_NORM, lw::EPI_ARGMAX)
+  X(16, lw::PRO_RESID_NORM, lw::EPI_ARGMAX)                 \
+  X(4, lw::PRO_NORM, lw::EPI_ARGMAX)                        \
+  X(8, lw::PRO_NORM, lw::EPI_ARGMAX)                        \
+  X(4, lw::PRO_RESID_NORM, lw::EPI_ARGMAX)                  \
+  X(8, lw::PRO_RESID_NORM, lw::EPI_ARGMAX)
 
 int validate(const lw_fused_gemv_args* a) {
   if (!a) return LW_ERR_NULL_POINTER;

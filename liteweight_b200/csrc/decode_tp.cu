@@ -26,7 +26,11 @@
   X(4, lw::PRO_PLAIN, lw::EPI_PEER_F32)                     \
   X(8, lw::PRO_PLAIN, lw::EPI_PEER_F32)                     \
   X(16, lw::PRO_PEER_RESID_NORM, lw::EPI_PEER_ARGMAX)      \
-  X(16, lw::PRO_NORM, lw::EPI_PEER_ARGMAX)
+  X(16, lw::PRO_NORM, lw::EPI_PEER_ARGMAX)                  \
+  X(4, lw::PRO_PEER_RESID_NORM, lw::EPI_PEER_ARGMAX)        \
+  X(8, lw::PRO_PEER_RESID_NORM, lw::EPI_PEER_ARGMAX)        \
+  X(4, lw::PRO_NORM, lw::EPI_PEER_ARGMAX)                   \
+  X(8, lw::PRO_NORM, lw::EPI_PEER_ARGMAX)
 
 namespace lw {
 

@@ -229,6 +229,9 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           hdr[2 * slot + 1] = -1;
           mbar_arrive_local(full0 + 8u * slot);
         }
+        // this slot's last copy was consumed (hence landed) before it was
+        // released, and its barrier has now completed one phase more: no wait
+        issued &= ~(1u << slot);
       } else {
         live = false;
       }

@@ -155,12 +155,16 @@ class LlamaSpec:
         return [("q", self.n_heads * hd, h), ("k", self.n_kv_heads * hd, h), ("v", self.n_kv_heads * hd, h),
                 ("o", h, self.n_heads * hd), ("gate", i, h), ("up", i, h), ("down", h, i)]
 
-    def weight_bytes_per_token(self, include_lm_head: bool = True) -> int:
-        """Bytes one decode step must read: packed weights + fp16 scales (+ lm_head, norms)."""
+    def weight_bytes_per_token(self, include_lm_head: bool = True, lm_head_bits: int = 16) -> int:
+        """Bytes one decode step must read: packed weights + fp16 scales (+ lm_head, norms).
+        lm_head_bits 16: the fp16 lm_head (liteweight keeps it unquantized); 8 / 4:
+        a quantized one with this spec's group size."""
         per_layer = sum(n * k * self.bits // 8 + 2 * n * (k // self.group_size) for _, n, k in self.linear_shapes())
         total = self.n_layers * (per_layer + 4 * self.hidden)
         if include_lm_head:
-            total += self.vocab * self.hidden * 2 + 2 * self.hidden
+            v, h = self.vocab, self.hidden
+            total += (v * h * 2 if lm_head_bits == 16
+                      else v * h * lm_head_bits // 8 + 2 * v * (h // self.group_size)) + 2 * h
         return total
 
     def kv_bytes_per_position(self) -> int:
@@ -402,7 +406,8 @@ class DecodeEngine:
     def __init__(self, spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
                  lm_head: torch.Tensor | None, rope_cos: torch.Tensor, rope_sin: torch.Tensor, batch: int,
                  max_seq: int, device=None, tp_rank: int = 0, tp_size: int = 1, tp_group=None, pdl: bool = True,
-                 fold_scales: bool = False, exchange: str = "peer", exchange_timeout_s: float = 10.0):
+                 fold_scales: bool = False, exchange: str = "peer", exchange_timeout_s: float = 10.0,
+                 lm_head_quant: tuple | None = None):
         assert exchange in ("peer", "nccl")
         self.spec, self.B, self.S = spec, batch, max_seq
         self.fold = int(fold_scales)
@@ -419,8 +424,20 @@ class DecodeEngine:
         dev, H, hd = self.device, spec.hidden, spec.head_dim
         self.layers = layers
         self.embed = embed.to(device=dev, dtype=torch.float16).contiguous()
-        head = self.embed if lm_head is None else lm_head.to(device=dev, dtype=torch.float16).contiguous()
-        self.lm_head = shard_rows(head, tp_rank, tp_size)
+        # lm_head: fp16 [V, H] (liteweight keeps it unquantized; tied to the embedding when None),
+        # or lm_head_quant = (qweight, scales, bits, group_size) in liteweight's format (what
+        # swap_linears makes of it when it is not skipped)
+        self.lm_bits, self.lm_group, self.lm_scales = 16, spec.hidden, None
+        if lm_head_quant is not None:
+            q, sc, bits, grp = lm_head_quant
+            assert bits in (4, 8) and spec.hidden % grp == 0
+            self.lm_bits, self.lm_group = bits, grp
+            self.lm_head = shard_rows(q.to(dev).contiguous(), tp_rank, tp_size).contiguous()
+            self.lm_scales = shard_rows(sc.to(device=dev, dtype=torch.float16).contiguous(), tp_rank,
+                                        tp_size).contiguous()
+        else:
+            head = self.embed if lm_head is None else lm_head.to(device=dev, dtype=torch.float16).contiguous()
+            self.lm_head = shard_rows(head, tp_rank, tp_size)
         self.final_norm = final_norm.to(device=dev, dtype=torch.float16).contiguous()
         self.rope_cos = rope_cos.to(dev).contiguous()
         self.rope_sin = rope_sin.to(dev).contiguous()
@@ -574,8 +591,9 @@ class DecodeEngine:
         head = dict(epilogue=EPI_ARGMAX, argmax_keys=bufs.keys)
         if ex is not None:
             head.update(epilogue=EPI_PEER_ARGMAX, xout=ex.out_ptr(2 * len(self.layers)))
-        a = self._gemv(rows, bits=16, N=self.vshard, K=H, group_size=H, weight=self.lm_head, gamma=self.final_norm,
-                       out=bufs.logits, ldo=self.vshard, argmax_offset=self.tp_rank * self.vshard, **head, **pro)
+        a = self._gemv(rows, bits=self.lm_bits, N=self.vshard, K=H, group_size=self.lm_group, weight=self.lm_head,
+                       scales=self.lm_scales, gamma=self.final_norm, out=bufs.logits, ldo=self.vshard,
+                       argmax_offset=self.tp_rank * self.vshard, **head, **pro)
         calls.append(("gemv", a, "lm_head"))
         gemv_args.append(a)
         if tp and ex is None:
@@ -638,8 +656,9 @@ class DecodeEngine:
         if tp:   # the last down partial joins the residual stream (h is not used)
             calls.append(norm(self.final_norm, True))
         last = bufs.x.data_ptr() + 2 * (rows - 1) * H
-        a = self._gemv(1, bits=16, prologue=PRO_NORM, epilogue=EPI_ARGMAX, N=self.vshard, K=H, group_size=H,
-                       weight=self.lm_head, gamma=self.final_norm, act=last, lda=H,
+        a = self._gemv(1, bits=self.lm_bits, prologue=PRO_NORM, epilogue=EPI_ARGMAX, N=self.vshard, K=H,
+                       group_size=self.lm_group, weight=self.lm_head, scales=self.lm_scales,
+                       gamma=self.final_norm, act=last, lda=H,
                        out=bufs.logits.data_ptr() + 2 * (rows - 1) * self.vshard, ldo=self.vshard,
                        argmax_keys=bufs.keys.data_ptr() + 8 * (rows - 1), argmax_offset=self.tp_rank * self.vshard)
         calls.append(("gemv", a, "lm_head"))
@@ -901,6 +920,9 @@ def supports(model) -> bool:
         return False
     if not all(isinstance(m, QuantLinear) and m.bias is None for m in qls):
         return False
+    head = getattr(model, "lm_head", None)
+    if isinstance(head, QuantLinear) and head.bias is not None:
+        return False
     cfg = getattr(model, "config", None)
     return cfg is not None and getattr(cfg, "hidden_act", "silu") == "silu" and torch.cuda.is_available() \
         and next(model.parameters()).is_cuda
@@ -939,21 +961,30 @@ def engine_from_hf(model, batch: int, max_seq: int, tp_rank: int = 0, tp_size: i
     x = torch.zeros(1, 1, spec.hidden, dtype=torch.float16, device=dev)
     with torch.no_grad():
         cos, sin = rot(x, torch.arange(max_seq, device=dev)[None])
-    lm_w = model.lm_head.weight.data
-    tied = lm_w.data_ptr() == model.model.embed_tokens.weight.data_ptr()
+    from liteweight_b200.quantlinear import QuantLinear
+    head = model.lm_head
+    lm_w, lm_q = None, None
+    if isinstance(head, QuantLinear):
+        # swap_linears without skip=("lm_head",): the head is quantized too
+        assert head.bias is None, "a biased lm_head is not supported"
+        lm_q = (head.qweight, head.scales, head.bits, head.group_size)
+    elif head.weight.data.data_ptr() != model.model.embed_tokens.weight.data.data_ptr():
+        lm_w = head.weight.data
     return DecodeEngine(spec, packed, model.model.embed_tokens.weight.data, model.model.norm.weight.data,
-                        None if tied else lm_w, cos[0], sin[0], batch, max_seq, dev, tp_rank, tp_size, tp_group, pdl)
+                        lm_w, cos[0], sin[0], batch, max_seq, dev, tp_rank, tp_size, tp_group, pdl,
+                        lm_head_quant=lm_q)
 
 
 def build_engine(spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm: torch.Tensor,
                  lm_head: torch.Tensor | None, inv_freq: torch.Tensor, batch: int, max_seq: int, device,
                  attention_scaling: float = 1.0, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
-                 pdl: bool = True, fold_scales: bool = False, exchange: str = "peer") -> DecodeEngine:
+                 pdl: bool = True, fold_scales: bool = False, exchange: str = "peer",
+                 lm_head_quant: tuple | None = None) -> DecodeEngine:
     """Engine from unsharded LayerWeights (liteweight-format tensors, any device)."""
     packed = [PackedLayer(lw, spec, tp_rank, tp_size, device) for lw in layers]
     cos, sin = rope_tables(inv_freq, max_seq, attention_scaling, device)
     return DecodeEngine(spec, packed, embed, final_norm, lm_head, cos, sin, batch, max_seq, device, tp_rank,
-                        tp_size, tp_group, pdl, fold_scales, exchange)
+                        tp_size, tp_group, pdl, fold_scales, exchange, lm_head_quant=lm_head_quant)
 
 
 def synthetic_layers(spec: LlamaSpec, device, seed: int = 0, std: float = 0.02) -> list:

@@ -23,6 +23,7 @@ class _TinyWorkload:
         self.norm = (1.0 + 0.1 * torch.randn(self.spec.hidden, generator=g)).half()
         self.inv_freq = E.default_inv_freq(self.spec.head_dim, self.spec.rope_theta)
         self.cos, self.sin = E.rope_tables(self.inv_freq, 64, 1.0, "cpu")
+        self.lm_quant = None
 
     def layer_weights(self, li):
         return E.synthetic_layers(E.LlamaSpec(**{**self.spec.__dict__, "n_layers": 1}), self.dev, seed=1000 + li,
