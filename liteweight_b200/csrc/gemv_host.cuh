@@ -171,29 +171,24 @@ inline bool ring_enabled() {
   return on;
 }
 
-// Units per CTA the schedule aims for (more: finer balance, more split tiles).
-inline int ring_units_per_cta() {
-  static const int n = [] {
-    const char* v = getenv("LW_B200_RING_UNITS");
-    const int x = v ? atoi(v) : 0;
-    return x > 0 ? x : 4;
-  }();
-  return n;
-}
-
 struct RingPlan {
-  int spr, nst, upr, units, stages, grid, rowblocks, tiles, cp, kchunks;
+  int spr, boxes_last, units, stages, grid, cp, kchunks;
   size_t smem, ws_bytes;
 };
 
 template <int BITS, int PRO>
 bool plan_ring(int M, int N, int K, const void* w, RingPlan* pl) {
   constexpr int KC = 4 * WT<BITS>::E;
-  if (!ring_enabled() || M < 1 || M > 8 || N < kRingRows) return false;
+  if (!ring_enabled() || M < 1 || M > 8 || N < 16) return false;
   const size_t rowbytes = (size_t)K * BITS / 8;
   if (rowbytes % 16 || rowbytes < 128 || (w && (reinterpret_cast<uintptr_t>(w) % 16))) return false;
-  pl->spr = (int)((rowbytes + 127) / 128);
-  pl->kchunks = 2 * pl->spr;
+  pl->spr = (int)((rowbytes + kRingStageRowBytes - 1) / kRingStageRowBytes);
+  // a unit's scales ride in registers for up to kRingMaxUnit stages; fp16 rows
+  // are whole stages (a box left unissued keeps stale bytes, harmless only
+  // for integer codes, which are finite whatever they are)
+  if (BITS < 16 ? pl->spr > kRingMaxUnit : rowbytes % kRingStageRowBytes != 0) return false;
+  pl->boxes_last = (int)((rowbytes - (size_t)(pl->spr - 1) * kRingStageRowBytes + 127) / 128);
+  pl->kchunks = 16 * pl->spr;
   const int kpad = pl->kchunks * KC;
   pl->cp = ((size_t)M * (kpad + 32) * 2 + gamma_bytes(PRO, K) <= (size_t)kStageBudget) ? kpad + 32 : kpad;
   const size_t act = align_up((size_t)M * pl->cp * 2 + gamma_bytes(PRO, K), 16);
@@ -201,19 +196,9 @@ bool plan_ring(int M, int N, int K, const void* w, RingPlan* pl) {
   if (fixed + (size_t)kRingMinStages * kRingStageBytes > kRingSmemMax) return false;
   pl->stages = (int)std::min<size_t>(kRingMaxStages, (kRingSmemMax - fixed) / kRingStageBytes);
   pl->smem = (size_t)kRingFixedBytes + (size_t)pl->stages * kRingStageBytes + act;
-  pl->rowblocks = (N + kRingRows - 1) / kRingRows;
-  pl->tiles = pl->rowblocks * (kRingRows / 16);
-  if (pl->tiles > kMaxSplitTiles) return false;
-  const int sms = device_sm_count();
-  const long long total = (long long)pl->rowblocks * pl->spr;
-  const long long target = std::max<long long>(1, total / ((long long)sms * ring_units_per_cta()));
-  int nst = 1;
-  while (nst * 2 <= std::min<long long>(target, kRingMaxUnit) && nst * 2 <= pl->spr) nst *= 2;
-  pl->nst = nst;
-  pl->upr = (pl->spr + nst - 1) / nst;
-  pl->units = pl->rowblocks * pl->upr;
-  pl->grid = std::min(sms, pl->units);
-  pl->ws_bytes = kCounterBytes + (pl->upr > 1 ? (size_t)pl->tiles * pl->upr * 32 * 4 * 4 : 0);
+  pl->units = (N + 15) / 16;
+  pl->grid = std::min(device_sm_count(), pl->units);
+  pl->ws_bytes = kCounterBytes;   // the work-claim counters at its end
   return true;
 }
 
@@ -222,22 +207,19 @@ cudaError_t launch_ring(StreamParams p, const RingPlan& pl, void* ws, int sched_
   RingParams rp;
   memset(&rp, 0, sizeof(rp));
   const size_t rowbytes = (size_t)p.K * BITS / 8;
-  if (!encode_2d(&rp.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, rowbytes, (uint64_t)p.N, rowbytes, 128, kRingRows,
+  if (!encode_2d(&rp.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, rowbytes, (uint64_t)p.N, rowbytes, 128, 16,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   p.kchunks = pl.kchunks;
   p.cp = pl.cp;
-  p.tiles = pl.tiles;
+  p.tiles = pl.units;
   p.gshift = BITS < 16 ? group_shift(p.K, p.G) : 31;
   rp.p = p;
   rp.spr = pl.spr;
-  rp.nst = pl.nst;
-  rp.upr = pl.upr;
+  rp.boxes_last = pl.boxes_last;
   rp.units = pl.units;
   rp.stages = pl.stages;
   rp.sched = sched_counters(ws, sched_set);
-  rp.counters = static_cast<int*>(ws);
-  rp.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
   auto kern = gemv_ring_kernel<BITS, PRO, EPI>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;

@@ -6,42 +6,39 @@
 // dequantized exactly (fp16(code * scale), liteweight/quantize.py:30-43,
 // :102-128), fp32 tensor-core sums, one fp16 rounding.
 //
-// Work. The weight matrix is cut into row blocks of 128 rows; a row block's
-// bytes into stages of 128 bytes per row (one 16 KB TMA box, 128-byte
-// swizzle); `nst` consecutive stages of one row block make a unit. Units are
-// handed out dynamically: CTA b starts with unit b and claims the next one
-// from a global counter (kept in the workspace; the last CTA to finish
-// claiming resets it), so SMs that get less memory bandwidth simply take
-// fewer units and all CTAs finish within about one unit of each other.
+// Work. A unit is one 16-row tile of the weight matrix over all of K. Its
+// bytes stream in stages of 16 rows x 1024 bytes (16 KB: eight 16-row x
+// 128-byte TMA boxes, 128-byte swizzle), `spr` stages per unit. CTA b takes
+// units b and b + grid, then claims further ones from a global counter (in
+// the workspace; the last CTA to finish claiming resets it), with two claims
+// in flight ahead of their use: SMs that get less memory bandwidth take fewer
+// units, and all CTAs finish within about one unit of each other. A tile is
+// never split between CTAs: no partial sum leaves the SM.
 //
 // Roles (one CTA per SM, 17 warps):
-//   warp 16    one lane claims units and issues each stage's TMA copy into
-//              the next free ring slot, writing the stage's unit id (and the
-//              unit this CTA takes after it) into the slot's header; the
-//              other lanes prefetch the unit's scale rows into L2. It starts
-//              before griddepcontrol.wait: weights do not depend on the
-//              previous kernel, so up to `stages` x 16 KB per SM stream in
-//              while that kernel finishes.
-//   warps 0-15 warp w owns tile w % 8 (16 rows) of the row block and chunk
-//              w / 8 (64 bytes per row) of every stage: per stage each lane
-//              reads 16 bytes of two rows, unpacks and scales them, and feeds
-//              mma.sync m16n8k16 with the staged activation as operand B.
-//              Each lane loads its scales for a whole unit at once, one unit
-//              ahead (the header names the next unit). At the end of a unit
-//              warp w + 8 hands its partial to warp w through shared memory
-//              (two buffers per tile, each guarded by a full / empty mbarrier);
-//              warp w finishes the tile (whole-row units) or combines it with
-//              the other units of the row block through the workspace slots,
-//              in unit order (deterministic, as gemv_stream_kernel's split
-//              tiles).
-// Lane (g, t) of a consumer warp holds tile rows pi(g) and pi(g) + 8, pi(g) =
-// (g >> 1) | ((g & 1) << 2): with the 128-byte swizzle (16-byte piece j of
-// row r at piece j ^ (r & 7)) the 8 lanes of each quarter warp then read 8
-// distinct bank groups. The epilogues take pi(g) as the lane's row.
+//   warp 16    one lane issues each stage's copies into the next free ring
+//              slot and writes the stage's unit id, and the unit this CTA
+//              takes after it, into the slot's header; lanes 0-15 prefetch
+//              that next unit's scale rows into L2. It starts before
+//              griddepcontrol.wait: weights do not depend on the previous
+//              kernel, so up to `stages` x 16 KB per SM stream in while that
+//              kernel finishes.
+//   warps 0-15 warp w owns chunk w (64 bytes of each row) of every stage: per
+//              stage each lane reads 16 bytes of two rows, unpacks and scales
+//              them, and feeds mma.sync m16n8k16 with the staged activation
+//              as operand B. Each lane loads its scales for a whole unit at
+//              once, one unit ahead (the header names the next unit). At the
+//              end of a unit every warp writes its partial tile to shared
+//              memory and warp (unit % 16) sums the 16 partials in warp order
+//              (the same sums on every run) and applies the epilogue.
+// Lane (g, t) holds tile rows pi(g) and pi(g) + 8, pi(g) = (g >> 1) |
+// ((g & 1) << 2): with the 128-byte swizzle (16-byte piece j of row r at
+// piece j ^ (r & 7)) the 8 lanes of each quarter warp then read 8 distinct
+// bank groups. The epilogues take pi(g) as the lane's row.
 //
-// Every mbarrier wait is bounded: on expiry the kernel records LW_ERR_TIMEOUT
-// (device error flag), the roles stop at their next wait, and the producer
-// waits (bounded) for the copies it issued before the CTA exits.
+// Every wait is bounded: on expiry the kernel records LW_ERR_TIMEOUT (device
+// error flag), the roles stop at their next wait, and the producer waits
+// (bounded) for the copies it issued before the CTA exits.
 #pragma once
 
 #include <cuda.h>   // CUtensorMap
@@ -53,12 +50,13 @@ namespace lw {
 constexpr int kRingConsumerWarps = 16;
 constexpr int kRingConsumers = kRingConsumerWarps * 32;
 constexpr int kRingThreads = kRingConsumers + 32;
-constexpr int kRingRows = 128;                         // rows per row block (TMA box rows)
-constexpr int kRingStageBytes = kRingRows * 128;       // one 128 x 128-byte box
+constexpr int kRingStageRowBytes = 1024;               // bytes of each tile row per stage
+constexpr int kRingBoxes = kRingStageRowBytes / 128;   // 16-row x 128-byte TMA boxes per stage
+constexpr int kRingStageBytes = 16 * kRingStageRowBytes;
 constexpr int kRingMaxStages = 13;
-constexpr int kRingMaxUnit = 8;                        // stages per unit, at most
+constexpr int kRingMaxUnit = 8;                        // stages of a unit with scales (row bytes <= 8 KB)
 constexpr int kRingHeadBytes = 1024;                   // barriers + headers
-constexpr int kRingCombBytes = 2 * 8 * 32 * 4 * 4;     // warp-pair hand-off, two parities, MT = 1
+constexpr int kRingCombBytes = 2 * kRingConsumerWarps * 32 * 16;   // partial tiles, two buffers
 // shared memory a launch needs besides its ring and staged activation (the
 // ring starts on a 1024-byte boundary, hence the slack)
 constexpr int kRingFixedBytes = kRingHeadBytes + kRingCombBytes + 1024;
@@ -71,16 +69,13 @@ constexpr long long kRingProducerWaitNs = 60000000000LL;
 constexpr int kRingSchedInts = 4;                      // per schedule set: claim counter, done counter, pad
 
 struct RingParams {
-  StreamParams p;          // matmul, prologue, epilogue (p.kchunks = 2 * spr, p.cp staged row stride)
-  CUtensorMap tm_w;        // [N rows][K * BITS / 8 bytes] u8, box {128, 128}, 128-byte swizzle
-  int spr;                 // stages per row block (ceil(row bytes / 128))
-  int nst;                 // stages per unit
-  int upr;                 // units per row block (ceil(spr / nst))
-  int units;               // row blocks * upr
+  StreamParams p;          // matmul, prologue, epilogue (p.kchunks = 16 * spr, p.cp staged row stride)
+  CUtensorMap tm_w;        // [N rows][K * BITS / 8 bytes] u8, box {128, 16}, 128-byte swizzle
+  int spr;                 // stages per unit (ceil(row bytes / 1024))
+  int boxes_last;          // TMA boxes of a unit's last stage that start inside the row
+  int units;               // ceil(N / 16)
   int stages;              // ring slots
   int* sched;              // {claims, done}: zero before the first launch, left zero
-  float* slots;            // upr > 1: [tiles][upr][32][4] partial tiles
-  int* counters;           // upr > 1: [tiles] arrivals, zero before the first launch, left zero
 };
 
 LW_DEV void tma_load_box(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -94,14 +89,6 @@ LW_DEV void mbar_arrive_local(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 LW_DEV void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
-// Arrival on a split tile's counter: release (the warp's slot stores, ordered
-// before it by __syncwarp) and acquire (the other units' slots, when last) in
-// one GPU-scope round trip.
-LW_DEV int atom_add_acq_rel_gpu(int* p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 
 // The lane's lower tile row (see the file comment).
 LW_DEV int ring_row(int g) { return (g >> 1) | ((g & 1) << 2); }
@@ -119,14 +106,14 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int S = rp.stages;
-  // layout: [ring barriers, headers, hand-off barriers | hand-off buffers |
+  // layout: [ring barriers, headers, partial-tile barriers | partial tiles |
   // ring (1024-aligned: the swizzle pattern follows address bits 4-9) |
   // staged activation, gamma]
   const uint32_t base = smem_u32(smem_raw);
   const uint32_t full0 = base, empty0 = base + 8u * kRingMaxStages;
   int* hdr = reinterpret_cast<int*>(smem_raw + 16 * kRingMaxStages);   // [S][2]: unit, next unit
-  const uint32_t hfull0 = base + 512, hempty0 = base + 512 + 8 * 16;     // [tile][parity]
-  float* comb = reinterpret_cast<float*>(smem_raw + kRingHeadBytes);
+  const uint32_t cfull0 = base + 512, cempty0 = base + 512 + 16;      // [buffer]
+  float* comb = reinterpret_cast<float*>(smem_raw + kRingHeadBytes);   // [buffer][warp][lane][4]
   const uint32_t ring_addr = (base + (uint32_t)(kRingHeadBytes + kRingCombBytes) + 1023u) & ~1023u;
   uint8_t* ring = smem_raw + (ring_addr - base);
   __half* act_s = reinterpret_cast<__half*>(ring + (size_t)S * kRingStageBytes);
@@ -137,9 +124,9 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       mbar_init(full0 + 8u * s, 1);
       mbar_init(empty0 + 8u * s, kRingConsumerWarps);
     }
-    for (int h = 0; h < 16; ++h) {
-      mbar_init(hfull0 + 8u * h, 32);
-      mbar_init(hempty0 + 8u * h, 32);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(cfull0 + 8u * h, kRingConsumers);
+      mbar_init(cempty0 + 8u * h, 32);
     }
     abort_s = 0;
     fence_mbar_init();
@@ -153,64 +140,64 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     abort_s = 1;
     return false;
   };
-  // the producer's wait for a free slot: long bound, gives up at once when
-  // a consumer has aborted
-  auto wait_free = [&](uint32_t bar, uint32_t parity) -> bool {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long limit = kRingProducerWaitNs + (PRO == PRO_PEER_RESID_NORM ? p.in_timeout_ns : 0);
-    const unsigned long long t0 = globaltimer_ns();
-    for (uint32_t it = 1;; ++it) {
-      if (mbar_try_wait(bar, parity)) return true;
-      if (abort_s) return false;
-      if ((it & 255u) == 0u && (long long)(globaltimer_ns() - t0) > limit) break;
-    }
-    lw_record_error(LW_ERR_TIMEOUT);
-    abort_s = 1;
-    return false;
-  };
 
   if (warp == kRingConsumerWarps) {
     // ------------------------------------------------------------ producer
     int* sched = rp.sched;
-    auto claim = [&]() -> int {   // the next unit of this CTA, or rp.units when none is left
-      int c = 0;
-      if (lane == 0) c = (int)gridDim.x + atomicAdd(sched, 1);
+    const int units = rp.units;
+    const int grid = (int)gridDim.x;
+    // the free-slot wait: long bound, gives up at once when a consumer aborted
+    auto wait_free = [&](uint32_t bar, uint32_t parity) -> bool {
+      if (mbar_try_wait(bar, parity)) return true;
+      const long long limit = kRingProducerWaitNs + (PRO == PRO_PEER_RESID_NORM ? p.in_timeout_ns : 0);
+      const unsigned long long t0 = globaltimer_ns();
+      for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (abort_s) return false;
+        if ((it & 255u) == 0u && (long long)(globaltimer_ns() - t0) > limit) break;
+      }
+      lw_record_error(LW_ERR_TIMEOUT);
+      abort_s = 1;
+      return false;
+    };
+    // claims (units 2 * grid and up): lane 0 keeps two atomics in flight ahead of their use
+    auto issue_claim = [&]() -> int { return lane == 0 ? 2 * grid + atomicAdd(sched, 1) : 0; };
+    auto resolve = [&](int c) -> int {
       c = __shfl_sync(0xffffffffu, c, 0);
-      return c < rp.units ? c : rp.units;
+      return c < units ? c : units;
     };
     const int ngroups = SCALED ? p.K / p.G : 1;
-    int u = (int)blockIdx.x < rp.units ? (int)blockIdx.x : rp.units;
-    int nxt = u < rp.units ? claim() : rp.units;
+    const int srow_lines = SCALED ? (ngroups * 2 + 127) / 128 : 0;   // 128-byte lines of a row's scales
+    int u = (int)blockIdx.x;          // the grid never exceeds the unit count
+    int nxt = min(u + grid, units);
+    int q1 = issue_claim(), q2 = issue_claim();
     int slot = 0;
-    uint32_t phase = 0;             // parity of the ring's current lap
-    uint32_t issued = 0;            // bit s: slot s holds a copy issued in the current lap or later
+    uint32_t phase = 0;               // parity of the ring's current lap
+    uint32_t issued = 0;              // bit s: slot s has held a copy
     bool live = true;
-    if (u >= rp.units) nxt = rp.units;
-    while (live && u < rp.units) {
-      const int nn = nxt < rp.units ? claim() : rp.units;   // claimed one unit ahead of its use
-      const int rb = u / rp.upr, st0 = (u - rb * rp.upr) * rp.nst;
-      const int nst = min(rp.nst, rp.spr - st0);
+    while (live && u < units) {
       if constexpr (SCALED) {
-        // the unit's scale rows into L2 (4 rows per lane), so that the
-        // consumers' loads one unit from now hit
-        const int g0 = min((st0 * 2 * KC) >> p.gshift, ngroups - 1);
-        for (int r = lane; r < kRingRows; r += 32) {
-          const int row = min(rb * kRingRows + r, p.N - 1);
-          prefetch_l2_line(p.scales + (size_t)row * ngroups + g0);
+        // the next unit's scale rows into L2 (one unit ahead of the consumers' loads)
+        if (nxt < units && lane < 16) {
+          const char* row = reinterpret_cast<const char*>(p.scales + (size_t)min(nxt * 16 + lane, p.N - 1) * ngroups);
+          for (int l = 0; l < srow_lines; ++l) prefetch_l2_line(row + 128 * l);
         }
       }
-      for (int st = 0; st < nst; ++st) {
+      for (int st = 0; st < rp.spr; ++st) {
         // the slot's previous contents have been read by all consumer warps
         if (!wait_free(empty0 + 8u * slot, phase ^ 1u)) {
           live = false;
           break;
         }
         if (lane == 0) {
+          const int nb = st + 1 < rp.spr ? kRingBoxes : rp.boxes_last;
           hdr[2 * slot] = u;
           hdr[2 * slot + 1] = nxt;
-          mbar_arrive_expect_tx(full0 + 8u * slot, (uint32_t)kRingStageBytes);
-          tma_load_box(ring_addr + (uint32_t)slot * kRingStageBytes, &rp.tm_w, (st0 + st) * 128,
-                       rb * kRingRows, full0 + 8u * slot);
+          mbar_arrive_expect_tx(full0 + 8u * slot, (uint32_t)(nb * 16 * 128));
+          const uint32_t dst = ring_addr + (uint32_t)slot * kRingStageBytes;
+          for (int b = 0; b < nb; ++b)
+            tma_load_box(dst + (uint32_t)b * 2048u, &rp.tm_w, st * kRingStageRowBytes + b * 128, u * 16,
+                         full0 + 8u * slot);
         }
         issued |= 1u << slot;
         if (++slot == S) {
@@ -219,7 +206,11 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
         }
       }
       u = nxt;
-      nxt = nn;
+      if (u < units) {
+        nxt = resolve(q1);   // claimed two units ago
+        q1 = q2;
+        q2 = issue_claim();
+      }
     }
     if (live) {
       // end of work: an empty stage with header -1
@@ -237,9 +228,12 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       }
     }
     if (lane == 0) {
-      // the last CTA to finish claiming resets the schedule for the next launch
+      // The last CTA to finish claiming resets the schedule for the next
+      // launch. The claims still in flight are waited for first (their
+      // results are consumed), so none reaches the counter after the reset.
+      asm volatile("" ::"r"(q1), "r"(q2));
       __threadfence();
-      if (atomicAdd(sched + 1, 1) == (int)gridDim.x - 1) {
+      if (atomicAdd(sched + 1, 1) == grid - 1) {
         sched[0] = 0;
         sched[1] = 0;
         __threadfence();
@@ -247,8 +241,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     }
     // No copy may land after the CTA has exited: wait (bounded) for each
     // slot's newest copy - this lap's for the slots before `slot`, the last
-    // lap's for the others. In a healthy run they have landed or land while
-    // the consumers drain the ring.
+    // lap's for the others. In a healthy run they have landed.
     for (int s = 0; s < S; ++s) {
       if (!((issued >> s) & 1u)) continue;
       mbar_wait_bounded(full0 + 8u * s, (s < slot) ? phase : (phase ^ 1u), kRingWaitNs);
@@ -258,28 +251,24 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
 
   // -------------------------------------------------------------- consumers
   const int g = lane >> 2, t = lane & 3;
-  const int tw = warp & 7, c = warp >> 3;
   const int gr = ring_row(g);
   const int ngroups = SCALED ? p.K / p.G : 1;
   const unsigned short* sbase = reinterpret_cast<const unsigned short*>(p.scales);
-  // this lane's 16-byte piece of a stage, rows gr and gr + 8 of tile tw
-  const uint32_t piece_off = (uint32_t)((tw * 16 + gr) * 128 + (((4 * c + t) ^ gr) << 4));
+  // this lane's 16-byte piece of a stage: box warp / 2, its half warp % 2, rows gr and gr + 8
+  const uint32_t piece_off = (uint32_t)((warp >> 1) * 2048 + gr * 128 + (((4 * (warp & 1) + t) ^ gr) << 4));
 
   // scales of a unit: one fp16 per stage for each of the lane's two rows
   // (lo = row gr, hi = row gr + 8), loaded for the whole unit at once
   auto load_scales = [&](int unit, uint32_t (&sv)[kRingMaxUnit]) {
     if constexpr (SCALED) {
-      if (unit >= rp.units) return;
-      const int rb = unit / rp.upr, st0 = (unit - rb * rp.upr) * rp.nst;
-      const int nst = min(rp.nst, rp.spr - st0);
-      const int r0 = min(rb * kRingRows + tw * 16 + gr, p.N - 1);
-      const int r1 = min(rb * kRingRows + tw * 16 + gr + 8, p.N - 1);
+      if (unit < 0 || unit >= rp.units) return;
+      const int r0 = min(unit * 16 + gr, p.N - 1), r1 = min(unit * 16 + gr + 8, p.N - 1);
       const unsigned short* s0 = sbase + (size_t)r0 * ngroups;
       const unsigned short* s1 = sbase + (size_t)r1 * ngroups;
 #pragma unroll
       for (int st = 0; st < kRingMaxUnit; ++st) {
-        if (st < nst) {
-          const int grp = min((((st0 + st) * 2 + c) * KC + t * E) >> p.gshift, ngroups - 1);
+        if (st < rp.spr) {
+          const int grp = min(((st * 16 + warp) * KC + t * E) >> p.gshift, ngroups - 1);
           sv[st] = (uint32_t)__ldg(s0 + grp) | ((uint32_t)__ldg(s1 + grp) << 16);
         }
       }
@@ -303,32 +292,20 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   const __half* arow[MT] = {act_s + (size_t)min(g, p.M - 1) * p.cp + t * 8};
   int slot = 0;
   uint32_t phase = 0;
-  int nunit = 0;   // units done: hand-off buffer nunit & 1, its use count nunit >> 1
+  int nunit = 0;   // units done: partial-tile buffer nunit & 1, its use count nunit >> 1
+
   for (;;) {
     if (!wait(full0 + 8u * slot, phase)) break;
     const int u = hdr[2 * slot];
     if (u < 0) break;
-    const int nxt = hdr[2 * slot + 1];
-    load_scales(nxt, nx);
-    const int rb = u / rp.upr, ks = u - rb * rp.upr, st0 = ks * rp.nst;
-    const int nst = min(rp.nst, rp.spr - st0);
+    load_scales(hdr[2 * slot + 1], nx);
     float acc[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
     bool ok = true;
-#pragma unroll
-    for (int st = 0; st < kRingMaxUnit; ++st) {
-      if (st >= nst) break;
-      if (st > 0 && !wait(full0 + 8u * slot, phase)) {
-        ok = false;
-        break;
-      }
+    auto one = [&](int st, uint32_t sv) {
       const uint8_t* sp = ring + (size_t)slot * kRingStageBytes + piece_off;
       const uint4 qa = lds128(sp), qb = lds128(sp + 8 * 128);
-      const int off = ((st0 + st) * 2 + c) * KC;
-      uint32_t sa = 0, sb = 0;
-      if constexpr (SCALED) {
-        sa = __byte_perm(cur[st], 0, 0x1010);
-        sb = __byte_perm(cur[st], 0, 0x3232);
-      }
+      const int off = (st * 16 + warp) * KC;
+      const uint32_t sa = __byte_perm(sv, 0, 0x1010), sb = __byte_perm(sv, 0, 0x3232);
       gemv_piece<BITS, MT>(acc, qa, qb, sa, sb, arow, off);
       __syncwarp();
       if (lane == 0) mbar_arrive_local(empty0 + 8u * slot);
@@ -336,54 +313,51 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
         slot = 0;
         phase ^= 1u;
       }
+    };
+    if constexpr (SCALED) {
+#pragma unroll
+      for (int st = 0; st < kRingMaxUnit; ++st) {
+        if (st >= rp.spr) break;
+        if (st > 0 && !wait(full0 + 8u * slot, phase)) {
+          ok = false;
+          break;
+        }
+        one(st, cur[st]);
+      }
+    } else {
+#pragma unroll 1
+      for (int st = 0; st < rp.spr; ++st) {
+        if (st > 0 && !wait(full0 + 8u * slot, phase)) {
+          ok = false;
+          break;
+        }
+        one(st, 0u);
+      }
     }
     if (!ok) break;
-    // ---- the unit's tile partials: warp w + 8 hands its half to warp w
+    // ---- the unit's 16 partial tiles: warp u % 16 sums them in warp order
     const int par = nunit & 1;
     const uint32_t use = (uint32_t)(nunit >> 1);
     ++nunit;
-    const uint32_t hf = hfull0 + 8u * (2 * tw + par), he = hempty0 + 8u * (2 * tw + par);
-    float* cb = comb + (((size_t)par * 8 + tw) * 32 + lane) * 4;
-    if (c == 1) {
-      // the buffer's previous contents (two units ago) have been read
-      if (use > 0 && !wait(he, (use - 1) & 1u)) break;
-      *reinterpret_cast<float4*>(cb) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-      mbar_arrive_local(hf);
-    } else {
-      if (!wait(hf, use & 1u)) break;
-      const float4 o = *reinterpret_cast<const float4*>(cb);
-      mbar_arrive_local(he);
-      acc[0][0] += o.x;
-      acc[0][1] += o.y;
-      acc[0][2] += o.z;
-      acc[0][3] += o.w;
-      const int tile = rb * 8 + tw;
-      if (tile * 16 < p.N) {
-        if (rp.upr == 1) {
-          finish_tile<MT, EPI>(p, tile, acc, lane, out_flag, gr);
-        } else {
-          float* mine = rp.slots + (((size_t)tile * rp.upr + ks) * 32 + lane) * 4;
-          *reinterpret_cast<float4*>(mine) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-          __syncwarp();
-          int old = 0;
-          if (lane == 0) old = atom_add_acq_rel_gpu(rp.counters + tile, 1);
-          old = __shfl_sync(0xffffffffu, old, 0);
-          if (old == rp.upr - 1) {
-            __syncwarp();   // lane 0's acquire, then every lane reads the slots (from L2)
-            float sum[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
-            const float* src = rp.slots + ((size_t)tile * rp.upr * 32 + lane) * 4;
-            for (int k = 0; k < rp.upr; ++k) {
-              const float4 f = __ldcg(reinterpret_cast<const float4*>(src + (size_t)k * 32 * 4));
-              sum[0][0] += f.x;
-              sum[0][1] += f.y;
-              sum[0][2] += f.z;
-              sum[0][3] += f.w;
-            }
-            finish_tile<MT, EPI>(p, tile, sum, lane, out_flag, gr);
-            if (lane == 0) rp.counters[tile] = 0;
-          }
-        }
+    // the buffer's previous contents (two units ago) have been read
+    if (use > 0 && !wait(cempty0 + 8u * par, (use - 1) & 1u)) break;
+    float* cb = comb + (size_t)par * kRingConsumerWarps * 32 * 4;
+    *reinterpret_cast<float4*>(cb + ((size_t)warp * 32 + lane) * 4) =
+        make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+    mbar_arrive_local(cfull0 + 8u * par);
+    if (warp == (u & (kRingConsumerWarps - 1))) {
+      if (!wait(cfull0 + 8u * par, use & 1u)) break;
+      float sum[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int w = 0; w < kRingConsumerWarps; ++w) {
+        const float4 f = *reinterpret_cast<const float4*>(cb + ((size_t)w * 32 + lane) * 4);
+        sum[0][0] += f.x;
+        sum[0][1] += f.y;
+        sum[0][2] += f.z;
+        sum[0][3] += f.w;
       }
+      mbar_arrive_local(cempty0 + 8u * par);
+      finish_tile<MT, EPI>(p, u, sum, lane, out_flag, gr);
     }
 #pragma unroll
     for (int i = 0; i < kRingMaxUnit; ++i) cur[i] = nx[i];

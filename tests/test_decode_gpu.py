@@ -232,3 +232,62 @@ def test_chunked_prefill(bits, batch, P, down_block, path, monkeypatch):
     assert (got == ref_tokens).mean() >= 0.8
     oracle = ol.teacher_forced_logits(w, prompt, got)
     assert (oracle.argmax(-1) == got.T).mean() >= 0.9
+
+
+@pytest.mark.parametrize("head_bits,bits", [(4, 4), (8, 4), (8, 8)])
+def test_quantized_lm_head_vs_oracle(head_bits, bits):
+    """The lm_head quantized like swap_linears does when it is not skipped:
+    the engine's logits (the GEMV dequantizes the head exactly) match the
+    oracle whose head is the dequantized fp16 weight, and both pick alike."""
+    from liteweight_b200 import engine as E
+    w = random_model(512, 1024, 2, 8, 2, 64, 1000, bits, seed=21 + head_bits)
+    quant, deq = ((oq.quantize_int4, oq.dequantize_int4) if head_bits == 4
+                  else (oq.quantize_int8, oq.dequantize_int8))
+    hq, hs = quant(w.embed, 128)
+    w.lm_head = deq(hq, hs, 128)
+    s = w.shape
+    spec = E.LlamaSpec(hidden=s.hidden, inter=s.inter, n_layers=s.n_layers, n_heads=s.n_heads,
+                       n_kv_heads=s.n_kv_heads, head_dim=s.head_dim, vocab=s.vocab, bits=bits, group_size=128,
+                       eps=s.eps)
+    layers = []
+    for L in w.layers:
+        lin = {n: (_t(getattr(L, n).qweight), _t(getattr(L, n).scales)) for n in
+               ("q", "k", "v", "o", "gate", "up", "down")}
+        layers.append(E.LayerWeights(in_norm=_t(L.in_norm), post_norm=_t(L.post_norm), **lin))
+    eng = E.build_engine(spec, layers, _t(w.embed), _t(w.norm), None, torch.from_numpy(w.inv_freq), 2, 48, DEV,
+                         lm_head_quant=(_t(hq), _t(hs), head_bits, 128))
+    P, T = 6, 6
+    prompt = np.random.default_rng(head_bits).integers(0, 1000, (2, P))
+    got = run_engine(eng, prompt, P + T - 1)
+    gen = eng.generated(T).cpu().numpy()
+    oracle = ol.teacher_forced_logits(w, prompt, gen)
+    assert_rows(got, oracle, f"lm_head int{head_bits}")
+    # the tensor-core prompt path ends with the same quantized head
+    out = eng.generate(torch.from_numpy(prompt), T).numpy()
+    assert (out == gen).mean() >= 0.8
+
+
+def test_generate_with_quantized_head_matches_hf_loop():
+    """swap_linears(skip=()) quantizes the lm_head as well: generate() runs it
+    on the engine (the head's QuantLinear buffers) and agrees with the HF loop."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from liteweight_b200 import engine as E
+    from liteweight_b200.generate import _generate_hf, generate
+    from liteweight_b200.quantlinear import QuantLinear
+    from liteweight_b200.serialize import swap_linears
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=64, vocab_size=640, rms_norm_eps=1e-5, tie_word_embeddings=False,
+                      max_position_embeddings=512, rope_parameters={"rope_type": "default", "rope_theta": 500000.0})
+    torch.manual_seed(6)
+    model = LlamaForCausalLM(cfg).half().eval()
+    swap_linears(model, group_size=128, bits=4, skip=())
+    model = model.to(DEV)
+    assert isinstance(model.lm_head, QuantLinear) and E.supports(model)
+    tok = _Tok()
+    prompt = " ".join(str(i) for i in np.random.default_rng(2).integers(0, 640, 10))
+    text = generate(model, tok, prompt, max_new_tokens=8)
+    ids = tok(prompt).input_ids.to(DEV)
+    ref = tok.decode(_generate_hf(model, ids, 8, 0.0, None, set()))
+    a, b = text.split(), ref.split()
+    assert len(a) == 8
+    assert sum(x == y for x, y in zip(a, b)) >= 6, (a, b)
