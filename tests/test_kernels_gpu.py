@@ -341,22 +341,25 @@ def test_workspace_reuse_across_shapes():
 def test_graph_survives_workspace_growth():
     """A graph captured with a small shape keeps its workspace after a larger
     shape grows the stream's workspace: replaying it afterwards still matches
-    the oracle, and the larger call's output is right too."""
+    the oracle, and the larger call's output is right too. (M = 12 runs the
+    split-tile kernel, whose workspace grows with N.)"""
     from liteweight_b200 import _native as nat
     k = kern()
     rng = np.random.default_rng(23)
+    M = 12
     s_ = torch.cuda.Stream()
     with torch.cuda.stream(s_):
         key = (torch.device(DEV).index or 0, s_.cuda_stream)
         old = nat._workspaces.pop(key, None)   # start this stream from a small workspace
         if old is not None:
             nat._retired.append(old)
-        q1, sc1 = quantized(512, 4096, 128, 4, seed=31)     # M=1, K=4096: a split-tile plan
-        act1 = rng.standard_normal((1, 4096)).astype(np.float16)
+        q1, sc1 = quantized(512, 4096, 128, 4, seed=31)
+        act1 = rng.standard_normal((M, 4096)).astype(np.float16)
         a1 = torch.from_numpy(act1).to(DEV)
         qt1, st1 = torch.from_numpy(q1).to(DEV), torch.from_numpy(sc1).to(DEV)
-        need1 = int(nat.lib().lw_gemm_workspace_size(4, 1, 512, 4096))
-        assert need1 > 0
+        need1 = int(nat.lib().lw_gemm_workspace_size(4, M, 512, 4096))
+        need2 = int(nat.lib().lw_gemm_workspace_size(4, M, 28672, 4096))
+        assert 0 < need1 and need2 > max(need1, 1 << 20), (need1, need2)
         k.matmul_int4(a1, qt1, st1)
         torch.cuda.synchronize()
         small_ws = nat._workspaces[key].data_ptr()
@@ -365,7 +368,7 @@ def test_graph_survives_workspace_growth():
             out1 = k.matmul_int4(a1, qt1, st1)
         # a much larger split-tile problem grows (replaces) the stream's workspace
         q2, sc2 = quantized(28672, 4096, 128, 4, seed=32)
-        act2 = rng.standard_normal((1, 4096)).astype(np.float16)
+        act2 = rng.standard_normal((M, 4096)).astype(np.float16)
         big = k.matmul_int4(torch.from_numpy(act2).to(DEV), torch.from_numpy(q2).to(DEV),
                             torch.from_numpy(sc2).to(DEV))
         torch.cuda.synchronize()
