@@ -171,6 +171,15 @@ inline bool ring_enabled() {
   return on;
 }
 
+// LW_B200_RING_3D=0 issues the eight 2-D boxes per stage even when the 3-D view applies.
+inline bool ring_3d_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LW_B200_RING_3D");
+    return !(v && strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
 struct RingPlan {
   int spr, boxes_last, units, stages, grid, cp, kchunks;
   size_t smem, ws_bytes;
@@ -186,7 +195,9 @@ bool plan_ring(int M, int N, int K, const void* w, RingPlan* pl) {
   // a unit's scales ride in registers for up to kRingMaxUnit stages; fp16 rows
   // are whole stages (a box left unissued keeps stale bytes, harmless only
   // for integer codes, which are finite whatever they are)
-  if (BITS < 16 ? pl->spr > kRingMaxUnit : rowbytes % kRingStageRowBytes != 0) return false;
+  if (BITS < 16 ? pl->spr > kRingMaxUnit
+                : rowbytes % (ring_3d_enabled() ? 128 : kRingStageRowBytes) != 0)   // (3-D copies fill zeros)
+    return false;
   pl->boxes_last = (int)((rowbytes - (size_t)(pl->spr - 1) * kRingStageRowBytes + 127) / 128);
   pl->kchunks = 16 * pl->spr;
   const int kpad = pl->kchunks * KC;
@@ -207,9 +218,13 @@ cudaError_t launch_ring(StreamParams p, const RingPlan& pl, void* ws, int sched_
   RingParams rp;
   memset(&rp, 0, sizeof(rp));
   const size_t rowbytes = (size_t)p.K * BITS / 8;
-  if (!encode_2d(&rp.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, rowbytes, (uint64_t)p.N, rowbytes, 128, 16,
-                 CU_TENSOR_MAP_SWIZZLE_128B))
-    return cudaErrorInvalidValue;
+  // whole 128-byte chunks: the 3-D view, one copy per stage; else 2-D boxes
+  rp.map3d = rowbytes % 128 == 0 && ring_3d_enabled();
+  const bool ok = rp.map3d ? encode_3d(&rp.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, 128, (uint64_t)p.N,
+                                       rowbytes / 128, rowbytes, 128, 128, 16, kRingBoxes, CU_TENSOR_MAP_SWIZZLE_128B)
+                           : encode_2d(&rp.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, rowbytes, (uint64_t)p.N,
+                                       rowbytes, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok) return cudaErrorInvalidValue;
   p.kchunks = pl.kchunks;
   p.cp = pl.cp;
   p.tiles = pl.units;

@@ -7,8 +7,10 @@
 // :102-128), fp32 tensor-core sums, one fp16 rounding.
 //
 // Work. A unit is one 16-row tile of the weight matrix over all of K. Its
-// bytes stream in stages of 16 rows x 1024 bytes (16 KB: eight 16-row x
-// 128-byte TMA boxes, 128-byte swizzle), `spr` stages per unit. CTA b takes
+// bytes stream in stages of 16 rows x 1024 bytes (16 KB: one 3-D TMA box of
+// 8 chunks x 16 rows x 128 bytes - eight 16-row x 128-byte 2-D boxes when the
+// row bytes are not whole 128-byte chunks - 128-byte swizzle), `spr` stages
+// per unit. CTA b takes
 // units b and b + grid, then claims further ones from a global counter (in
 // the workspace; the last CTA to finish claiming resets it), with two claims
 // in flight ahead of their use: SMs that get less memory bandwidth take fewer
@@ -75,6 +77,7 @@ struct RingParams {
   int boxes_last;          // TMA boxes of a unit's last stage that start inside the row
   int units;               // ceil(N / 16)
   int stages;              // ring slots
+  int map3d;               // 1: tm_w is the 3-D view {128 bytes, rows, row bytes / 128}, one box per stage
   int* sched;              // {claims, done}: zero before the first launch, left zero
 };
 
@@ -83,6 +86,13 @@ LW_DEV void tma_load_box(uint32_t dst, const CUtensorMap* map, int x, int y, uin
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
           "r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+LW_DEV void tma_load_box3(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
 LW_DEV void mbar_arrive_local(uint32_t bar) {
@@ -190,14 +200,20 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           break;
         }
         if (lane == 0) {
-          const int nb = st + 1 < rp.spr ? kRingBoxes : rp.boxes_last;
           hdr[2 * slot] = u;
           hdr[2 * slot + 1] = nxt;
-          mbar_arrive_expect_tx(full0 + 8u * slot, (uint32_t)(nb * 16 * 128));
           const uint32_t dst = ring_addr + (uint32_t)slot * kRingStageBytes;
-          for (int b = 0; b < nb; ++b)
-            tma_load_box(dst + (uint32_t)b * 2048u, &rp.tm_w, st * kRingStageRowBytes + b * 128, u * 16,
-                         full0 + 8u * slot);
+          if (rp.map3d) {
+            // one copy: chunks past the row end are filled with zeros (and counted)
+            mbar_arrive_expect_tx(full0 + 8u * slot, (uint32_t)kRingStageBytes);
+            tma_load_box3(dst, &rp.tm_w, 0, u * 16, st * kRingBoxes, full0 + 8u * slot);
+          } else {
+            const int nb = st + 1 < rp.spr ? kRingBoxes : rp.boxes_last;
+            mbar_arrive_expect_tx(full0 + 8u * slot, (uint32_t)(nb * 16 * 128));
+            for (int b = 0; b < nb; ++b)
+              tma_load_box(dst + (uint32_t)b * 2048u, &rp.tm_w, st * kRingStageRowBytes + b * 128, u * 16,
+                           full0 + 8u * slot);
+          }
         }
         issued |= 1u << slot;
         if (++slot == S) {

@@ -37,3 +37,25 @@ inline bool encode_2d(CUtensorMap* m, CUtensorMapDataType type, const void* ptr,
 }
 
 }  // namespace lw
+
+namespace lw {
+
+// 3-D tiled tensor map over dims {d0, d1, d2} (d0 innermost, contiguous) with
+// byte strides s1 (dim 1) and s2 (dim 2), box {b0, b1, b2}. The strides need
+// not grow with the dimension: a row-major [rows][bytes] matrix viewed as
+// {128 bytes, rows, bytes / 128} (s1 = row bytes, s2 = 128) gives boxes whose
+// shared-memory image is [chunk][row][128 bytes].
+inline bool encode_3d(CUtensorMap* m, CUtensorMapDataType type, const void* ptr, uint64_t d0, uint64_t d1,
+                      uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2,
+                      CUtensorMapSwizzle swizzle) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  return enc(m, type, 3, const_cast<void*>(ptr), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace lw
