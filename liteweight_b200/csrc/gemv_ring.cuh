@@ -19,9 +19,9 @@
 //
 // Roles (one CTA per SM, 17 warps):
 //   warp 16    one lane issues each stage's copies into the next free ring
-//              slot and writes the stage's unit id, and the unit this CTA
-//              takes after it, into the slot's header; lanes 0-15 prefetch
-//              that next unit's scale rows into L2. It starts before
+//              slot and writes the stage's unit id, and the two units this
+//              CTA takes after it, into the slot's header; lanes 0-15 prefetch
+//              the scale rows of the unit two ahead into L2. It starts before
 //              griddepcontrol.wait: weights do not depend on the previous
 //              kernel, so up to `stages` x 16 KB per SM stream in while that
 //              kernel finishes.
@@ -29,7 +29,7 @@
 //              stage each lane reads 16 bytes of two rows, unpacks and scales
 //              them, and feeds mma.sync m16n8k16 with the staged activation
 //              as operand B. Each lane loads its scales for a whole unit at
-//              once, one unit ahead (the header names the next unit). At the
+//              once, two units ahead (the header names them). At the
 //              end of a unit every warp writes its partial tile to shared
 //              memory and warp (unit % 16) sums the 16 partials in warp order
 //              (the same sums on every run) and applies the epilogue.
@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   // staged activation, gamma]
   const uint32_t base = smem_u32(smem_raw);
   const uint32_t full0 = base, empty0 = base + 8u * kRingMaxStages;
-  int* hdr = reinterpret_cast<int*>(smem_raw + 16 * kRingMaxStages);   // [S][2]: unit, next unit
+  int* hdr = reinterpret_cast<int*>(smem_raw + 16 * kRingMaxStages);   // [S][4]: unit, the two after it
   const uint32_t cfull0 = base + 512, cempty0 = base + 512 + 16;      // [buffer]
   float* comb = reinterpret_cast<float*>(smem_raw + kRingHeadBytes);   // [buffer][warp][lane][4]
   const uint32_t ring_addr = (base + (uint32_t)(kRingHeadBytes + kRingCombBytes) + 1023u) & ~1023u;
@@ -170,8 +170,10 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       abort_s = 1;
       return false;
     };
-    // claims (units 2 * grid and up): lane 0 keeps two atomics in flight ahead of their use
-    auto issue_claim = [&]() -> int { return lane == 0 ? 2 * grid + atomicAdd(sched, 1) : 0; };
+    // Units: b, b + grid, b + 2 grid, then claims (3 grid and up). Lane 0
+    // keeps four claim atomics in flight; the two units after the current one
+    // are always known (the consumers load scales two units ahead).
+    auto issue_claim = [&]() -> int { return lane == 0 ? 3 * grid + atomicAdd(sched, 1) : 0; };
     auto resolve = [&](int c) -> int {
       c = __shfl_sync(0xffffffffu, c, 0);
       return c < units ? c : units;
@@ -179,17 +181,18 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     const int ngroups = SCALED ? p.K / p.G : 1;
     const int srow_lines = SCALED ? (ngroups * 2 + 127) / 128 : 0;   // 128-byte lines of a row's scales
     int u = (int)blockIdx.x;          // the grid never exceeds the unit count
-    int nxt = min(u + grid, units);
-    int q1 = issue_claim(), q2 = issue_claim();
+    int n1 = min(u + grid, units), n2 = min(u + 2 * grid, units);
+    int qa = issue_claim(), qb = issue_claim(), qc = issue_claim(), qd = issue_claim();
     int slot = 0;
     uint32_t phase = 0;               // parity of the ring's current lap
     uint32_t issued = 0;              // bit s: slot s has held a copy
     bool live = true;
     while (live && u < units) {
       if constexpr (SCALED) {
-        // the next unit's scale rows into L2 (one unit ahead of the consumers' loads)
-        if (nxt < units && lane < 16) {
-          const char* row = reinterpret_cast<const char*>(p.scales + (size_t)min(nxt * 16 + lane, p.N - 1) * ngroups);
+        // the scale rows of the unit two ahead into L2 (the consumers load them
+        // when they start this unit, `stages` slots from now)
+        if (n2 < units && lane < 16) {
+          const char* row = reinterpret_cast<const char*>(p.scales + (size_t)min(n2 * 16 + lane, p.N - 1) * ngroups);
           for (int l = 0; l < srow_lines; ++l) prefetch_l2_line(row + 128 * l);
         }
       }
@@ -200,8 +203,9 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           break;
         }
         if (lane == 0) {
-          hdr[2 * slot] = u;
-          hdr[2 * slot + 1] = nxt;
+          hdr[4 * slot] = u;
+          hdr[4 * slot + 1] = n1;
+          hdr[4 * slot + 2] = n2;
           const uint32_t dst = ring_addr + (uint32_t)slot * kRingStageBytes;
           if (rp.map3d) {
             // one copy: chunks past the row end are filled with zeros (and counted)
@@ -221,19 +225,21 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           phase ^= 1u;
         }
       }
-      u = nxt;
-      if (u < units) {
-        nxt = resolve(q1);   // claimed two units ago
-        q1 = q2;
-        q2 = issue_claim();
+      u = n1;
+      n1 = n2;
+      if (n2 < units) {
+        n2 = resolve(qa);   // claimed four units ago
+        qa = qb;
+        qb = qc;
+        qc = qd;
+        qd = issue_claim();
       }
     }
     if (live) {
       // end of work: an empty stage with header -1
       if (wait_free(empty0 + 8u * slot, phase ^ 1u)) {
         if (lane == 0) {
-          hdr[2 * slot] = -1;
-          hdr[2 * slot + 1] = -1;
+          hdr[4 * slot] = -1;
           mbar_arrive_local(full0 + 8u * slot);
         }
         // this slot's last copy was consumed (hence landed) before it was
@@ -247,7 +253,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       // The last CTA to finish claiming resets the schedule for the next
       // launch. The claims still in flight are waited for first (their
       // results are consumed), so none reaches the counter after the reset.
-      asm volatile("" ::"r"(q1), "r"(q2));
+      asm volatile("" ::"r"(qa), "r"(qb), "r"(qc), "r"(qd));
       __threadfence();
       if (atomicAdd(sched + 1, 1) == grid - 1) {
         sched[0] = 0;
@@ -291,10 +297,12 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     }
   };
 
-  uint32_t cur[kRingMaxUnit], nx[kRingMaxUnit];
+  uint32_t cur[kRingMaxUnit], nx1[kRingMaxUnit], nx2[kRingMaxUnit];
 #pragma unroll
-  for (int i = 0; i < kRingMaxUnit; ++i) cur[i] = nx[i] = 0;
-  load_scales((int)blockIdx.x, cur);   // the first unit is blockIdx.x: its scales before the wait
+  for (int i = 0; i < kRingMaxUnit; ++i) cur[i] = nx1[i] = nx2[i] = 0;
+  // the first two units are blockIdx.x and blockIdx.x + grid: their scales before the wait
+  load_scales((int)blockIdx.x, cur);
+  load_scales((int)(blockIdx.x + gridDim.x), nx1);
 
   stage_gamma<PRO, kRingConsumers>(p, gam_s);
   pdl_wait();
@@ -312,9 +320,9 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
 
   for (;;) {
     if (!wait(full0 + 8u * slot, phase)) break;
-    const int u = hdr[2 * slot];
+    const int u = hdr[4 * slot];
     if (u < 0) break;
-    load_scales(hdr[2 * slot + 1], nx);
+    load_scales(hdr[4 * slot + 2], nx2);   // two units ahead
     float acc[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
     bool ok = true;
     auto one = [&](int st, uint32_t sv) {
@@ -376,7 +384,10 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       finish_tile<MT, EPI>(p, u, sum, lane, out_flag, gr);
     }
 #pragma unroll
-    for (int i = 0; i < kRingMaxUnit; ++i) cur[i] = nx[i];
+    for (int i = 0; i < kRingMaxUnit; ++i) {
+      cur[i] = nx1[i];
+      nx1[i] = nx2[i];
+    }
   }
 
   if constexpr (EPI == EPI_PEER_ARGMAX) {

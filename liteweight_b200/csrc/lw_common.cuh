@@ -233,22 +233,26 @@ LW_DEV __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 // Same unpack without scaling, in PTX: the sign flip is folded into each LOP3
 // constant ((x & m) ^ c, c = 0x6400.. | 0x0008..), the fp16 constants live in
 // registers (1032 and the (1/16, -72) rescale of the high nibbles).
+// Every constant is a register operand (a LOP3 takes one immediate at most;
+// a second one would cost a move per use), so the compiler keeps them in
+// registers across the unrolled loops.
 LW_DEV void unpack_int4_word(uint32_t q, uint32_t (&o)[4]) {
   const uint32_t k1032 = 0x64086408u, k1_16 = 0x2C002C00u, km72 = 0xD480D480u;
+  const uint32_t mlo = 0x000F000Fu, mhi = 0x00F000F0u, xlo = 0x64086408u, xhi = 0x64806480u;
   asm("{\n"
       " .reg .b32 y, a, b, c, d;\n"
       " shr.u32 y, %4, 8;\n"
-      " lop3.b32 a, %4, 0x000F000F, 0x64086408, 0x6a;\n"
-      " lop3.b32 b, %4, 0x00F000F0, 0x64806480, 0x6a;\n"
-      " lop3.b32 c, y, 0x000F000F, 0x64086408, 0x6a;\n"
-      " lop3.b32 d, y, 0x00F000F0, 0x64806480, 0x6a;\n"
+      " lop3.b32 a, %4, %8, %10, 0x6a;\n"
+      " lop3.b32 b, %4, %9, %11, 0x6a;\n"
+      " lop3.b32 c, y, %8, %10, 0x6a;\n"
+      " lop3.b32 d, y, %9, %11, 0x6a;\n"
       " sub.f16x2 %0, a, %5;\n"
       " fma.rn.f16x2 %1, b, %6, %7;\n"
       " sub.f16x2 %2, c, %5;\n"
       " fma.rn.f16x2 %3, d, %6, %7;\n"
       "}\n"
       : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
-      : "r"(q), "r"(k1032), "r"(k1_16), "r"(km72));
+      : "r"(q), "r"(k1032), "r"(k1_16), "r"(km72), "r"(mlo), "r"(mhi), "r"(xlo), "r"(xhi));
 }
 
 // fp16x2 product, round to nearest (one rounding of the exact product).
@@ -261,17 +265,17 @@ LW_DEV uint32_t hmul2_rn(uint32_t a, uint32_t b) {
 // 4 INT8 codes (bytes 0..3 = elements k0..k0+3) to two half2 (0,1) (2,3).
 // u = byte ^ 0x80 = code + 128; fp16 bits 0x64uu = 1024 + u; minus 1152.
 LW_DEV void dequant_int8_word(uint32_t q, uint32_t (&o)[2]) {
-  const uint32_t k1152 = 0x64806480u, magic = 0x64646464u;
+  const uint32_t k1152 = 0x64806480u, magic = 0x64646464u, sign = 0x80808080u;
   asm("{\n"
       " .reg .b32 x, a, b;\n"
-      " xor.b32 x, %2, 0x80808080;\n"
+      " xor.b32 x, %2, %5;\n"
       " prmt.b32 a, x, %4, 0x4140;\n"
       " prmt.b32 b, x, %4, 0x4342;\n"
       " sub.f16x2 %0, a, %3;\n"
       " sub.f16x2 %1, b, %3;\n"
       "}\n"
       : "=r"(o[0]), "=r"(o[1])
-      : "r"(q), "r"(k1152), "r"(magic));
+      : "r"(q), "r"(k1152), "r"(magic), "r"(sign));
 }
 
 // Permute 8 halves (h0..h7) to (h0,h4)(h1,h5)(h2,h6)(h3,h7): the element
