@@ -248,7 +248,7 @@ cudaError_t matmul_dispatch(const void* act, const void* w, const void* scales, 
   if (!stream_ok<BITS>(act, w, K, G)) {
     // shapes the register-pipeline kernel cannot take may still suit the ring kernel
     lw::RingPlan rpl;
-    if (M <= 8 && ws && ring_ok<BITS>(act, w, K, G) && lw::plan_ring<BITS, lw::PRO_PLAIN>(M, N, K, w, &rpl) &&
+    if (M <= 8 && ws && ring_ok<BITS>(act, w, K, G) && lw::plan_ring<BITS, lw::PRO_PLAIN>(M, N, K, G, w, scales, &rpl) &&
         rpl.ws_bytes <= ws_bytes) {
       lw::StreamParams p = {};
       p.M = M;

@@ -185,10 +185,19 @@ struct RingPlan {
   size_t smem, ws_bytes;
 };
 
+// scales: the unit copy needs 16-byte aligned blocks of whole 16-byte multiples
+// (16 rows x groups x 2 bytes; for the last tile, (N mod 16) rows) that fit a
+// unit buffer; a null `scales` (sizing only) skips the alignment check.
 template <int BITS, int PRO>
-bool plan_ring(int M, int N, int K, const void* w, RingPlan* pl) {
+bool plan_ring(int M, int N, int K, int G, const void* w, const void* scales, RingPlan* pl) {
   constexpr int KC = 4 * WT<BITS>::E;
   if (!ring_enabled() || M < 1 || M > 8 || N < 16) return false;
+  if (BITS < 16) {
+    const long long ngroups = G > 0 ? K / G : 0;
+    if (ngroups < 1 || ngroups * 32 > kRingMaxScaleBytes || ((long long)N * ngroups) % 8 ||
+        (scales && reinterpret_cast<uintptr_t>(scales) % 16))
+      return false;
+  }
   const size_t rowbytes = (size_t)K * BITS / 8;
   if (rowbytes % 16 || rowbytes < 128 || (w && (reinterpret_cast<uintptr_t>(w) % 16))) return false;
   pl->spr = (int)((rowbytes + kRingStageRowBytes - 1) / kRingStageRowBytes);
@@ -276,7 +285,7 @@ cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaS
                                 bool allow_fold = false, int sched_set = 0) {
   if (!allow_fold || !fold_scales<BITS>(p.K, p.G)) {
     RingPlan rpl;
-    if (ws && plan_ring<BITS, PRO>(p.M, p.N, p.K, p.w, &rpl) && rpl.ws_bytes <= ws_bytes)
+    if (ws && plan_ring<BITS, PRO>(p.M, p.N, p.K, p.G, p.w, p.scales, &rpl) && rpl.ws_bytes <= ws_bytes)
       return launch_ring<BITS, PRO, EPI>(p, rpl, ws, sched_set, s, pdl);
   }
   StreamPlan pl;
@@ -345,11 +354,10 @@ size_t stream_workspace(int M, int N, int K) {
   const int rows = stage_rows<BITS>(K);
   for (int m0 = 0; m0 < M; m0 += rows) {
     const int mb = std::min(rows, M - m0);
+    // the ring kernel (when the group size suits it: not known here) needs
+    // the counter region; the split-tile kernel is its fallback
     RingPlan rpl;
-    if (plan_ring<BITS, PRO>(mb, N, K, nullptr, &rpl)) {
-      need = std::max(need, rpl.ws_bytes);
-      continue;
-    }
+    if (plan_ring<BITS, PRO>(mb, N, K, BITS < 16 ? K : 0, nullptr, nullptr, &rpl)) need = std::max(need, rpl.ws_bytes);
     StreamPlan pl;
     if (BITS != 16 && EPI != EPI_PEER_ARGMAX && tma_enabled() && plan_tma<BITS, PRO>(mb, N, K, true, &pl)) {
       need = std::max(need, pl.ws_bytes);

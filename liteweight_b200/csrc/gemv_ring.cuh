@@ -10,29 +10,30 @@
 // bytes stream in stages of 16 rows x 1024 bytes (16 KB: one 3-D TMA box of
 // 8 chunks x 16 rows x 128 bytes - eight 16-row x 128-byte 2-D boxes when the
 // row bytes are not whole 128-byte chunks - 128-byte swizzle), `spr` stages
-// per unit. CTA b takes
-// units b and b + grid, then claims further ones from a global counter (in
-// the workspace; the last CTA to finish claiming resets it), with two claims
-// in flight ahead of their use: SMs that get less memory bandwidth take fewer
-// units, and all CTAs finish within about one unit of each other. A tile is
-// never split between CTAs: no partial sum leaves the SM.
+// per unit; its fp16 scales (16 consecutive rows of the scale matrix, one
+// contiguous block) arrive with one bulk copy into one of four unit buffers.
+// CTA b takes units b and b + grid, then claims further ones from a global
+// counter (in the workspace; the last CTA to finish claiming resets it), with
+// four claims in flight ahead of their use: SMs that get less memory
+// bandwidth take fewer units, and all CTAs finish within about one unit of
+// each other. A tile is never split between CTAs: no partial sum leaves the
+// SM.
 //
 // Roles (one CTA per SM, 17 warps):
-//   warp 16    one lane issues each stage's copies into the next free ring
-//              slot and writes the stage's unit id, and the two units this
-//              CTA takes after it, into the slot's header; lanes 0-15 prefetch
-//              the scale rows of the unit two ahead into L2. It starts before
-//              griddepcontrol.wait: weights do not depend on the previous
-//              kernel, so up to `stages` x 16 KB per SM stream in while that
-//              kernel finishes.
+//   warp 16    one lane copies each unit's scales into the next free unit
+//              buffer and issues each stage's weight copy into the next free
+//              ring slot, writing the stage's unit id into the slot's header.
+//              It starts before griddepcontrol.wait: weights do not depend on
+//              the previous kernel, so up to `stages` x 16 KB per SM stream in
+//              while that kernel finishes.
 //   warps 0-15 warp w owns chunk w (64 bytes of each row) of every stage: per
 //              stage each lane reads 16 bytes of two rows, unpacks and scales
 //              them, and feeds mma.sync m16n8k16 with the staged activation
-//              as operand B. Each lane loads its scales for a whole unit at
-//              once, two units ahead (the header names them). At the
-//              end of a unit every warp writes its partial tile to shared
-//              memory and warp (unit % 16) sums the 16 partials in warp order
-//              (the same sums on every run) and applies the epilogue.
+//              as operand B; it takes its scales for the whole unit from the
+//              unit buffer at the unit's start. At the end of a unit every
+//              warp writes its partial tile to shared memory and warp
+//              (unit % 16) sums the 16 partials in warp order (the same sums
+//              on every run) and applies the epilogue.
 // Lane (g, t) holds tile rows pi(g) and pi(g) + 8, pi(g) = (g >> 1) |
 // ((g & 1) << 2): with the 128-byte swizzle (16-byte piece j of row r at
 // piece j ^ (r & 7)) the 8 lanes of each quarter warp then read 8 distinct
@@ -57,11 +58,13 @@ constexpr int kRingBoxes = kRingStageRowBytes / 128;   // 16-row x 128-byte TMA 
 constexpr int kRingStageBytes = 16 * kRingStageRowBytes;
 constexpr int kRingMaxStages = 13;
 constexpr int kRingMaxUnit = 8;                        // stages of a unit with scales (row bytes <= 8 KB)
+constexpr int kRingScaleBufs = 4;                      // unit scale buffers
+constexpr int kRingMaxScaleBytes = 4096;               // one buffer: 16 rows x up to 128 groups x 2 bytes
 constexpr int kRingHeadBytes = 1024;                   // barriers + headers
 constexpr int kRingCombBytes = 2 * kRingConsumerWarps * 32 * 16;   // partial tiles, two buffers
 // shared memory a launch needs besides its ring and staged activation (the
 // ring starts on a 1024-byte boundary, hence the slack)
-constexpr int kRingFixedBytes = kRingHeadBytes + kRingCombBytes + 1024;
+constexpr int kRingFixedBytes = kRingHeadBytes + kRingCombBytes + kRingScaleBufs * kRingMaxScaleBytes + 1024;
 constexpr long long kRingWaitNs = 2000000000;          // 2 s: far beyond any copy or hand-off
 // The producer's wait for a free slot also spans the consumers' wait for the
 // previous kernel (programmatic dependent launch) and their wait for other
@@ -72,9 +75,9 @@ constexpr int kRingSchedInts = 4;                      // per schedule set: clai
 
 struct RingParams {
   StreamParams p;          // matmul, prologue, epilogue (p.kchunks = 16 * spr, p.cp staged row stride)
-  CUtensorMap tm_w;        // [N rows][K * BITS / 8 bytes] u8, box {128, 16}, 128-byte swizzle
+  CUtensorMap tm_w;        // weight rows [N][K * BITS / 8 bytes] u8, 128-byte swizzle (see map3d)
   int spr;                 // stages per unit (ceil(row bytes / 1024))
-  int boxes_last;          // TMA boxes of a unit's last stage that start inside the row
+  int boxes_last;          // 2-D boxes of a unit's last stage that start inside the row
   int units;               // ceil(N / 16)
   int stages;              // ring slots
   int map3d;               // 1: tm_w is the 3-D view {128 bytes, rows, row bytes / 128}, one box per stage
@@ -116,15 +119,19 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int S = rp.stages;
-  // layout: [ring barriers, headers, partial-tile barriers | partial tiles |
-  // ring (1024-aligned: the swizzle pattern follows address bits 4-9) |
-  // staged activation, gamma]
+  const int ngroups = SCALED ? p.K / p.G : 1;
+  // layout: [ring barriers, headers, partial-tile and scale-buffer barriers |
+  // partial tiles | unit scale buffers | ring (1024-aligned: the swizzle
+  // pattern follows address bits 4-9) | staged activation, gamma]
   const uint32_t base = smem_u32(smem_raw);
   const uint32_t full0 = base, empty0 = base + 8u * kRingMaxStages;
-  int* hdr = reinterpret_cast<int*>(smem_raw + 16 * kRingMaxStages);   // [S][4]: unit, the two after it
-  const uint32_t cfull0 = base + 512, cempty0 = base + 512 + 16;      // [buffer]
+  int* hdr = reinterpret_cast<int*>(smem_raw + 16 * kRingMaxStages);   // [S][2]: unit
+  const uint32_t cfull0 = base + 512, cempty0 = base + 528;           // [partial-tile buffer]
+  const uint32_t sfull0 = base + 544, sempty0 = base + 576;           // [scale buffer]
   float* comb = reinterpret_cast<float*>(smem_raw + kRingHeadBytes);   // [buffer][warp][lane][4]
-  const uint32_t ring_addr = (base + (uint32_t)(kRingHeadBytes + kRingCombBytes) + 1023u) & ~1023u;
+  const uint32_t sbuf_off = (uint32_t)(kRingHeadBytes + kRingCombBytes);
+  const uint32_t ring_addr =
+      (base + sbuf_off + (uint32_t)(kRingScaleBufs * kRingMaxScaleBytes) + 1023u) & ~1023u;
   uint8_t* ring = smem_raw + (ring_addr - base);
   __half* act_s = reinterpret_cast<__half*>(ring + (size_t)S * kRingStageBytes);
   __half* gam_s = act_s + (size_t)p.M * p.cp;
@@ -135,8 +142,12 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       mbar_init(empty0 + 8u * s, kRingConsumerWarps);
     }
     for (int h = 0; h < 2; ++h) {
-      mbar_init(cfull0 + 8u * h, kRingConsumers);
-      mbar_init(cempty0 + 8u * h, 32);
+      mbar_init(cfull0 + 8u * h, kRingConsumerWarps);
+      mbar_init(cempty0 + 8u * h, 1);
+    }
+    for (int j = 0; j < kRingScaleBufs; ++j) {
+      mbar_init(sfull0 + 8u * j, 1);
+      mbar_init(sempty0 + 8u * j, kRingConsumerWarps);
     }
     abort_s = 0;
     fence_mbar_init();
@@ -170,32 +181,35 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       abort_s = 1;
       return false;
     };
-    // Units: b, b + grid, b + 2 grid, then claims (3 grid and up). Lane 0
-    // keeps four claim atomics in flight; the two units after the current one
-    // are always known (the consumers load scales two units ahead).
-    auto issue_claim = [&]() -> int { return lane == 0 ? 3 * grid + atomicAdd(sched, 1) : 0; };
+    // units b, b + grid, then claims (2 grid and up); lane 0 keeps four claim atomics in flight
+    auto issue_claim = [&]() -> int { return lane == 0 ? 2 * grid + atomicAdd(sched, 1) : 0; };
     auto resolve = [&](int c) -> int {
       c = __shfl_sync(0xffffffffu, c, 0);
       return c < units ? c : units;
     };
-    const int ngroups = SCALED ? p.K / p.G : 1;
-    const int srow_lines = SCALED ? (ngroups * 2 + 127) / 128 : 0;   // 128-byte lines of a row's scales
     int u = (int)blockIdx.x;          // the grid never exceeds the unit count
-    int n1 = min(u + grid, units), n2 = min(u + 2 * grid, units);
+    int nxt = min(u + grid, units);
     int qa = issue_claim(), qb = issue_claim(), qc = issue_claim(), qd = issue_claim();
-    int slot = 0;
+    int slot = 0, nunit = 0;
     uint32_t phase = 0;               // parity of the ring's current lap
     uint32_t issued = 0;              // bit s: slot s has held a copy
     bool live = true;
     while (live && u < units) {
       if constexpr (SCALED) {
-        // the scale rows of the unit two ahead into L2 (the consumers load them
-        // when they start this unit, `stages` slots from now)
-        if (n2 < units && lane < 16) {
-          const char* row = reinterpret_cast<const char*>(p.scales + (size_t)min(n2 * 16 + lane, p.N - 1) * ngroups);
-          for (int l = 0; l < srow_lines; ++l) prefetch_l2_line(row + 128 * l);
+        // the unit's scales: rows u*16 .. u*16+15 are one contiguous block
+        const int j = nunit & (kRingScaleBufs - 1);
+        if (!wait_free(sempty0 + 8u * j, ((nunit / kRingScaleBufs) & 1) ^ 1u)) {
+          live = false;
+          break;
+        }
+        if (lane == 0) {
+          const uint32_t bytes = (uint32_t)(min(16, p.N - u * 16) * ngroups * 2);
+          mbar_arrive_expect_tx(sfull0 + 8u * j, bytes);
+          bulk_g2s(base + sbuf_off + (uint32_t)j * kRingMaxScaleBytes, p.scales + (size_t)u * 16 * ngroups, bytes,
+                   sfull0 + 8u * j);
         }
       }
+      ++nunit;
       for (int st = 0; st < rp.spr; ++st) {
         // the slot's previous contents have been read by all consumer warps
         if (!wait_free(empty0 + 8u * slot, phase ^ 1u)) {
@@ -203,9 +217,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           break;
         }
         if (lane == 0) {
-          hdr[4 * slot] = u;
-          hdr[4 * slot + 1] = n1;
-          hdr[4 * slot + 2] = n2;
+          hdr[2 * slot] = u;
           const uint32_t dst = ring_addr + (uint32_t)slot * kRingStageBytes;
           if (rp.map3d) {
             // one copy: chunks past the row end are filled with zeros (and counted)
@@ -225,10 +237,9 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           phase ^= 1u;
         }
       }
-      u = n1;
-      n1 = n2;
-      if (n2 < units) {
-        n2 = resolve(qa);   // claimed four units ago
+      u = nxt;
+      if (u < units) {
+        nxt = resolve(qa);   // claimed four units ago
         qa = qb;
         qb = qc;
         qc = qd;
@@ -239,7 +250,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       // end of work: an empty stage with header -1
       if (wait_free(empty0 + 8u * slot, phase ^ 1u)) {
         if (lane == 0) {
-          hdr[4 * slot] = -1;
+          hdr[2 * slot] = -1;
           mbar_arrive_local(full0 + 8u * slot);
         }
         // this slot's last copy was consumed (hence landed) before it was
@@ -263,10 +274,15 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     }
     // No copy may land after the CTA has exited: wait (bounded) for each
     // slot's newest copy - this lap's for the slots before `slot`, the last
-    // lap's for the others. In a healthy run they have landed.
+    // lap's for the others - and for each scale buffer's newest copy. In a
+    // healthy run they have all landed.
     for (int s = 0; s < S; ++s) {
       if (!((issued >> s) & 1u)) continue;
       mbar_wait_bounded(full0 + 8u * s, (s < slot) ? phase : (phase ^ 1u), kRingWaitNs);
+    }
+    if constexpr (SCALED) {
+      for (int k = max(0, nunit - kRingScaleBufs); k < nunit; ++k)
+        mbar_wait_bounded(sfull0 + 8u * (k & (kRingScaleBufs - 1)), (k / kRingScaleBufs) & 1, kRingWaitNs);
     }
     return;
   }
@@ -274,35 +290,10 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   // -------------------------------------------------------------- consumers
   const int g = lane >> 2, t = lane & 3;
   const int gr = ring_row(g);
-  const int ngroups = SCALED ? p.K / p.G : 1;
-  const unsigned short* sbase = reinterpret_cast<const unsigned short*>(p.scales);
   // this lane's 16-byte piece of a stage: box warp / 2, its half warp % 2, rows gr and gr + 8
   const uint32_t piece_off = (uint32_t)((warp >> 1) * 2048 + gr * 128 + (((4 * (warp & 1) + t) ^ gr) << 4));
-
-  // scales of a unit: one fp16 per stage for each of the lane's two rows
-  // (lo = row gr, hi = row gr + 8), loaded for the whole unit at once
-  auto load_scales = [&](int unit, uint32_t (&sv)[kRingMaxUnit]) {
-    if constexpr (SCALED) {
-      if (unit < 0 || unit >= rp.units) return;
-      const int r0 = min(unit * 16 + gr, p.N - 1), r1 = min(unit * 16 + gr + 8, p.N - 1);
-      const unsigned short* s0 = sbase + (size_t)r0 * ngroups;
-      const unsigned short* s1 = sbase + (size_t)r1 * ngroups;
-#pragma unroll
-      for (int st = 0; st < kRingMaxUnit; ++st) {
-        if (st < rp.spr) {
-          const int grp = min(((st * 16 + warp) * KC + t * E) >> p.gshift, ngroups - 1);
-          sv[st] = (uint32_t)__ldg(s0 + grp) | ((uint32_t)__ldg(s1 + grp) << 16);
-        }
-      }
-    }
-  };
-
-  uint32_t cur[kRingMaxUnit], nx1[kRingMaxUnit], nx2[kRingMaxUnit];
-#pragma unroll
-  for (int i = 0; i < kRingMaxUnit; ++i) cur[i] = nx1[i] = nx2[i] = 0;
-  // the first two units are blockIdx.x and blockIdx.x + grid: their scales before the wait
-  load_scales((int)blockIdx.x, cur);
-  load_scales((int)(blockIdx.x + gridDim.x), nx1);
+  // scale group of this lane's piece in stage st
+  auto group_of = [&](int st) -> int { return min(((st * 16 + warp) * KC + t * E) >> p.gshift, ngroups - 1); };
 
   stage_gamma<PRO, kRingConsumers>(p, gam_s);
   pdl_wait();
@@ -316,20 +307,35 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   const __half* arow[MT] = {act_s + (size_t)min(g, p.M - 1) * p.cp + t * 8};
   int slot = 0;
   uint32_t phase = 0;
-  int nunit = 0;   // units done: partial-tile buffer nunit & 1, its use count nunit >> 1
-
+  int nunit = 0;   // units done: partial-tile buffer nunit & 1, scale buffer nunit % 4
   for (;;) {
     if (!wait(full0 + 8u * slot, phase)) break;
-    const int u = hdr[4 * slot];
+    const int u = hdr[2 * slot];
     if (u < 0) break;
-    load_scales(hdr[4 * slot + 2], nx2);   // two units ahead
+    // the unit's scales, one fp16 per stage for each of the lane's two rows
+    // (lo = row gr, hi = row gr + 8; rows past N read row N - 1)
+    uint32_t sv[kRingMaxUnit];
+    if constexpr (SCALED) {
+      const int j = nunit & (kRingScaleBufs - 1);
+      if (!wait(sfull0 + 8u * j, (nunit / kRingScaleBufs) & 1)) break;
+      const unsigned short* sb =
+          reinterpret_cast<const unsigned short*>(smem_raw + sbuf_off + j * kRingMaxScaleBytes);
+      const int last = p.N - 1 - u * 16;
+      const unsigned short* s0 = sb + min(gr, last) * ngroups;
+      const unsigned short* s1 = sb + min(gr + 8, last) * ngroups;
+#pragma unroll
+      for (int st = 0; st < kRingMaxUnit; ++st)
+        if (st < rp.spr) sv[st] = (uint32_t)s0[group_of(st)] | ((uint32_t)s1[group_of(st)] << 16);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_local(sempty0 + 8u * j);
+    }
     float acc[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
     bool ok = true;
-    auto one = [&](int st, uint32_t sv) {
+    auto one = [&](int st, uint32_t s2) {
       const uint8_t* sp = ring + (size_t)slot * kRingStageBytes + piece_off;
       const uint4 qa = lds128(sp), qb = lds128(sp + 8 * 128);
       const int off = (st * 16 + warp) * KC;
-      const uint32_t sa = __byte_perm(sv, 0, 0x1010), sb = __byte_perm(sv, 0, 0x3232);
+      const uint32_t sa = __byte_perm(s2, 0, 0x1010), sb = __byte_perm(s2, 0, 0x3232);
       gemv_piece<BITS, MT>(acc, qa, qb, sa, sb, arow, off);
       __syncwarp();
       if (lane == 0) mbar_arrive_local(empty0 + 8u * slot);
@@ -346,7 +352,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           ok = false;
           break;
         }
-        one(st, cur[st]);
+        one(st, sv[st]);
       }
     } else {
 #pragma unroll 1
@@ -368,7 +374,8 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     float* cb = comb + (size_t)par * kRingConsumerWarps * 32 * 4;
     *reinterpret_cast<float4*>(cb + ((size_t)warp * 32 + lane) * 4) =
         make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-    mbar_arrive_local(cfull0 + 8u * par);
+    __syncwarp();
+    if (lane == 0) mbar_arrive_local(cfull0 + 8u * par);
     if (warp == (u & (kRingConsumerWarps - 1))) {
       if (!wait(cfull0 + 8u * par, use & 1u)) break;
       float sum[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
@@ -380,13 +387,9 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
         sum[0][2] += f.z;
         sum[0][3] += f.w;
       }
-      mbar_arrive_local(cempty0 + 8u * par);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_local(cempty0 + 8u * par);
       finish_tile<MT, EPI>(p, u, sum, lane, out_flag, gr);
-    }
-#pragma unroll
-    for (int i = 0; i < kRingMaxUnit; ++i) {
-      cur[i] = nx1[i];
-      nx1[i] = nx2[i];
     }
   }
 
