@@ -520,14 +520,15 @@ class DecodeWorkload:
 
 
 class TorchDecodeReference:
-    """Checker of the decode line's parity (never timed): a teacher-forced fp32
-    torch restatement, on the device, of the same packed weights through the
+    """Checker of the decode line's parity (never timed): a teacher-forced
+    torch computation, on the device, of the same packed weights through the
     reference's arithmetic - every QuantLinear dequantizes exactly
     (liteweight/quantize.py:30-43, :102-128) and multiplies in fp32 with an
-    fp16 result (:60) - and of the HF Llama layers around them with the fp16
-    rounding points of the fp16 model (transformers 5.5.0 modeling_llama.py:
-    RMSNorm :63-68, RoPE :138-167, fp32-softmax GQA attention :197-222,
-    SwiGLU :171-184, fp16 residual adds :320-335)."""
+    fp16 result (:60) - and of the HF Llama layers around them as the fp16 HF
+    model computes them on a GPU (transformers 5.5.0 modeling_llama.py:
+    RMSNorm with rsqrt :63-68, RoPE :138-167, SwiGLU :171-184, fp16 residual
+    adds :320-335, and attention through torch's scaled_dot_product_attention
+    on fp16 tensors, the "sdpa" implementation HF selects by default)."""
 
     def __init__(self, wl: DecodeWorkload):
         self.wl, self.torch = wl, wl.torch
@@ -550,9 +551,10 @@ class TorchDecodeReference:
 
     @staticmethod
     def _rmsnorm(x16, w, eps):
+        import torch
         xf = x16.float()
-        var = (xf * xf).mean(-1, keepdim=True)
-        return (w.float() * (xf * (1.0 / (var + eps).sqrt())).half().float()).half()
+        var = xf.pow(2).mean(-1, keepdim=True)
+        return (w * (xf * torch.rsqrt(var + eps)).half())
 
     @staticmethod
     def _rope(x16, cos, sin):
@@ -574,7 +576,6 @@ class TorchDecodeReference:
         try:
             x = wl.embed[tokens.to(dev)].half()                               # [B, T, H]
             cos, sin = wl.cos[:T][:, None, :], wl.sin[:T][:, None, :]         # [T, 1, hd]
-            mask = torch.ones(T, T, dtype=torch.bool, device=dev).tril()
             for li in range(sp.n_layers):
                 L = wl.layer_weights(li)
                 for b in range(B):
@@ -584,12 +585,12 @@ class TorchDecodeReference:
                     k = self._rope(self._lin(h, L.k, sp.bits, sp.group_size).view(T, nkv, hd), cos, sin)
                     v = self._lin(h, L.v, sp.bits, sp.group_size).view(T, nkv, hd)
                     rep = nh // nkv
-                    kf = k.float().repeat_interleave(rep, dim=1).transpose(0, 1)   # [nh, T, hd]
-                    vf = v.float().repeat_interleave(rep, dim=1).transpose(0, 1)
-                    sc = (q.float().transpose(0, 1) @ kf.transpose(1, 2)) * (hd ** -0.5)
-                    sc = sc.masked_fill(~mask, float("-inf")).softmax(-1)
-                    a = (sc @ vf).transpose(0, 1).reshape(T, nh * hd).half()
-                    del sc, kf, vf
+                    kx = k.repeat_interleave(rep, dim=1).transpose(0, 1)          # repeat_kv: [nh, T, hd]
+                    vx = v.repeat_interleave(rep, dim=1).transpose(0, 1)
+                    a = torch.nn.functional.scaled_dot_product_attention(
+                        q.transpose(0, 1)[None], kx[None], vx[None], is_causal=True, scale=hd ** -0.5)
+                    a = a[0].transpose(0, 1).reshape(T, nh * hd)
+                    del kx, vx
                     xb = (xb.float() + self._lin(a, L.o, sp.bits, sp.group_size).float()).half()
                     h = self._rmsnorm(xb, L.post_norm, sp.eps)
                     g = self._lin(h, L.gate, sp.bits, sp.group_size).float()
@@ -637,8 +638,8 @@ def decode_parity(wl: DecodeWorkload, ids_host, rank: int, steps: int = 32) -> d
             "first_mismatch_step": first_mismatch, "logits_err_over_tol": round(ratio, 4),
             "logits_steps_compared": steps, "logits_columns": f"vocab shard 0 of {wl.tp} ({vs} of {r.shape[-1]})",
             "tolerance": "max-abs err <= 1e-2 * ||ref row||_2 / sqrt(V), per (step, sequence)",
-            "reference": "teacher-forced fp32 torch restatement of the same packed weights (exact dequant, fp32 "
-                         "matmul, HF fp16 rounding points), full depth, on the device"}
+            "reference": "teacher-forced torch on the device: the same packed weights dequantized exactly with fp32 "
+                         "matmuls, the HF fp16 Llama layers with sdpa attention, full depth"}
 
 
 def decode_config(model: str, batch: int, prompt: int, new: int, world: int, fold: bool, exchange: str,
