@@ -69,6 +69,7 @@ struct TcGemmParams {
   const __half* scales;
   __half* out;
   const __half* residual;
+  const __half* bias;   // LW_TC_EPI_RESID: fp16 [N] added to the fp16 result (QuantLinear's bias), or null
   int ldo;
   int M, Mpad, N, K, G, gshift, kblocks;
   int splits, kb_per, stages;
@@ -222,6 +223,7 @@ LW_DEV void tc_epilogue(const TcGemmParams& p, int n, int m, float y, int lane) 
   } else if constexpr (EPI == LW_TC_EPI_RESID) {
     if (m >= p.M || n >= p.N) return;
     y = r16(y);
+    if (p.bias) y = r16(y + __half2float(p.bias[n]));
     if (p.residual) y = r16(__half2float(p.residual[(size_t)m * p.ldo + n]) + y);
     p.out[(size_t)m * p.ldo + n] = __float2half_rn(y);
   } else {
@@ -624,7 +626,43 @@ int lw_gemm_tc_take_error() { return lw_tu_take_error(); }
 
 extern "C" {
 
-int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
+namespace {
+int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t stream);
+}
+
+int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) { return prefill_gemm(a, nullptr, stream); }
+
+}  // extern "C"
+
+// out[M, N] = act[M, K] @ dequant(W)^T (+ bias), the drop-in matmul past the
+// GEMV crossover: lw_prefill_gemm's plain epilogue in row blocks of up to
+// kTcMaxM rows. The caller has checked the shape (N % 128, K % 64, a group
+// size of >= 32 that is a power of two or K, 16-byte aligned act and weight).
+int lw_tc_matmul(int bits, const void* act, const void* w, const void* scales, const void* bias, void* out, int M,
+                 int N, int K, int G, cudaStream_t s) {
+  for (int m0 = 0; m0 < M; m0 += lw::kTcMaxM) {
+    lw_prefill_gemm_args a = {};
+    a.bits = bits;
+    a.epilogue = LW_TC_EPI_RESID;
+    a.M = std::min(lw::kTcMaxM, M - m0);
+    a.N = N;
+    a.K = K;
+    a.group_size = G;
+    a.lda = K;
+    a.ldo = N;
+    a.act = static_cast<const __half*>(act) + (size_t)m0 * K;
+    a.weight = w;
+    a.scales = scales;
+    a.out = static_cast<__half*>(out) + (size_t)m0 * N;
+    const int st = prefill_gemm(&a, bias, reinterpret_cast<lw_stream_t>(s));
+    if (st) return st;
+  }
+  return LW_OK;
+}
+
+extern "C" {
+namespace {
+int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t stream) {
   if (!a || !a->act || !a->weight || !a->scales || !a->out) return LW_ERR_NULL_POINTER;
   if (a->bits != 4 && a->bits != 8) return LW_ERR_UNSUPPORTED;
   if (a->M <= 0 || a->M > lw::kTcMaxM || a->N <= 0 || a->N % lw::kTcTileN || a->K <= 0 || a->K % lw::kTcKBlock)
@@ -654,6 +692,7 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
   p.scales = static_cast<const __half*>(a->scales);
   p.out = static_cast<__half*>(a->out);
   p.residual = static_cast<const __half*>(a->residual);
+  p.bias = static_cast<const __half*>(bias);
   p.ldo = a->ldo;
   p.M = a->M;
   p.Mpad = (a->M + 15) / 16 * 16;
@@ -723,6 +762,7 @@ int lw_prefill_gemm(const lw_prefill_gemm_args* a, lw_stream_t stream) {
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;
 }
+}  // namespace
 
 namespace {
 int rmsnorm_rows_launch(void* x, const float* psum, const void* gamma, void* h, int M, int K, float eps, int pdl,

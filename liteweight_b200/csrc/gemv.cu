@@ -241,10 +241,44 @@ bool ring_ok(const void* act, const void* w, int K, int G) {
          (BITS == 16 || (G % E == 0 && lw::group_shift(K, G) >= 0));
 }
 
-// out[M,N] = act @ W^T (+bias): stream kernel in row blocks, or the generic kernel.
+}  // namespace
+
+// The tcgen05 GEMM (gemm_tc.cu) as a plain matmul with bias.
+int lw_tc_matmul(int bits, const void* act, const void* w, const void* scales, const void* bias, void* out, int M,
+                 int N, int K, int G, cudaStream_t s);
+
+namespace {
+
+// Rows from which the drop-in matmuls run on the tensor cores (tcgen05 GEMM)
+// instead of the GEMV: past them a GEMV launch stages at most 32 rows and
+// re-reads the weights per row block, while the GEMM takes 256 rows per pass.
+// LW_B200_TC_MIN_M overrides it (0 disables the GEMM route).
+int tc_min_rows() {
+  static const int m = [] {
+    const char* v = getenv("LW_B200_TC_MIN_M");
+    return v ? atoi(v) : 33;
+  }();
+  return m;
+}
+
+// Shapes the tcgen05 GEMM tiles: 128-row weight tiles, K in blocks of 64, a
+// scale group of >= 32 that is a power of two or K, 16-byte aligned rows.
+bool tc_ok(const void* act, const void* w, int M, int N, int K, int G) {
+  const int min_m = tc_min_rows();
+  return min_m > 0 && M >= min_m && N % 128 == 0 && K % 64 == 0 && G >= 32 && K % G == 0 &&
+         lw::group_shift(K, G) >= 0 && aligned(act, 16) && aligned(w, 16);
+}
+
+// out[M,N] = act @ W^T (+bias): tcgen05 GEMM past the crossover, else the
+// stream kernel in row blocks, or the generic kernel.
 template <int BITS>
 cudaError_t matmul_dispatch(const void* act, const void* w, const void* scales, const void* bias, void* out,
                             int M, int N, int K, int G, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if constexpr (BITS == 4 || BITS == 8) {
+    if (tc_ok(act, w, M, N, K, G))
+      return lw_tc_matmul(BITS, act, w, scales, bias, out, M, N, K, G, s) == LW_OK ? cudaSuccess
+                                                                                   : cudaErrorInvalidValue;
+  }
   if (!stream_ok<BITS>(act, w, K, G)) {
     // shapes the register-pipeline kernel cannot take may still suit the ring kernel
     lw::RingPlan rpl;

@@ -471,3 +471,20 @@ def test_quantize_kernels_match_oracle(N, K, G):
         np.testing.assert_array_equal(q.cpu().numpy(), rq, err_msg=f"int{bits} codes {N}x{K} G{G}")
         np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), rs.view(np.uint16),
                                       err_msg=f"int{bits} scales {N}x{K} G{G}")
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M", [33, 64, 300])
+def test_tensor_core_route_with_bias(bits, M):
+    """Past the GEMV crossover the drop-in matmul runs the tcgen05 GEMM (here
+    with QuantLinear's bias in its epilogue, and M = 300 in two row blocks)."""
+    from liteweight_b200.quantlinear import QuantLinear
+    torch.manual_seed(bits + M)
+    lin = torch.nn.Linear(512, 384, bias=True).half()
+    ql = QuantLinear.from_linear(lin, group_size=128, bits=bits).to(DEV)
+    x = torch.randn(M, 512, dtype=torch.float16, device=DEV)
+    y = ql(x)
+    q, s = ql.qweight.cpu().numpy(), ql.scales.cpu().numpy()
+    ref = oq.packed_matmul(x.cpu().numpy(), q, s, 128, bits)
+    ref = (ref.astype(np.float32) + ql.bias.cpu().numpy().astype(np.float32)).astype(np.float16)
+    check_rows(y, ref, f"tcgen05 route bits={bits} M={M}")
