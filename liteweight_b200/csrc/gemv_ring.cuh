@@ -19,7 +19,7 @@
 // each other. A tile is never split between CTAs: no partial sum leaves the
 // SM.
 //
-// Roles (one CTA per SM, 17 warps):
+// Roles (one CTA per SM, 18 warps):
 //   warp 16    one lane copies each unit's scales into the next free unit
 //              buffer and issues each stage's weight copy into the next free
 //              ring slot, writing the stage's unit id into the slot's header.
@@ -31,9 +31,11 @@
 //              them, and feeds mma.sync m16n8k16 with the staged activation
 //              as operand B; it takes its scales for the whole unit from the
 //              unit buffer at the unit's start. At the end of a unit every
-//              warp writes its partial tile to shared memory and warp
-//              (unit % 16) sums the 16 partials in warp order (the same sums
-//              on every run) and applies the epilogue.
+//              warp writes its partial tile into one of four shared-memory
+//              buffers and goes on to the next unit.
+//   warp 17    the reducer: sums each unit's 16 partial tiles in warp order
+//              (the same sums on every run) and applies the epilogue, off the
+//              consumers' path.
 // Lane (g, t) holds tile rows pi(g) and pi(g) + 8, pi(g) = (g >> 1) |
 // ((g & 1) << 2): with the 128-byte swizzle (16-byte piece j of row r at
 // piece j ^ (r & 7)) the 8 lanes of each quarter warp then read 8 distinct
@@ -52,7 +54,10 @@ namespace lw {
 
 constexpr int kRingConsumerWarps = 16;
 constexpr int kRingConsumers = kRingConsumerWarps * 32;
-constexpr int kRingThreads = kRingConsumers + 32;
+constexpr int kRingProducerWarp = kRingConsumerWarps;       // warp 16
+constexpr int kRingReducerWarp = kRingConsumerWarps + 1;    // warp 17
+constexpr int kRingThreads = kRingConsumers + 64;
+constexpr int kRingCombBufs = 4;                            // partial-tile buffers (units in flight to the reducer)
 constexpr int kRingStageRowBytes = 1024;               // bytes of each tile row per stage
 constexpr int kRingBoxes = kRingStageRowBytes / 128;   // 16-row x 128-byte TMA boxes per stage
 constexpr int kRingStageBytes = 16 * kRingStageRowBytes;
@@ -61,7 +66,7 @@ constexpr int kRingMaxUnit = 8;                        // stages of a unit with 
 constexpr int kRingScaleBufs = 4;                      // unit scale buffers
 constexpr int kRingMaxScaleBytes = 4096;               // one buffer: 16 rows x up to 128 groups x 2 bytes
 constexpr int kRingHeadBytes = 1024;                   // barriers + headers
-constexpr int kRingCombBytes = 2 * kRingConsumerWarps * 32 * 16;   // partial tiles, two buffers
+constexpr int kRingCombBytes = kRingCombBufs * kRingConsumerWarps * 32 * 16;   // partial tiles
 // shared memory a launch needs besides its ring and staged activation (the
 // ring starts on a 1024-byte boundary, hence the slack)
 constexpr int kRingFixedBytes = kRingHeadBytes + kRingCombBytes + kRingScaleBufs * kRingMaxScaleBytes + 1024;
@@ -126,8 +131,9 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   const uint32_t base = smem_u32(smem_raw);
   const uint32_t full0 = base, empty0 = base + 8u * kRingMaxStages;
   int* hdr = reinterpret_cast<int*>(smem_raw + 16 * kRingMaxStages);   // [S][2]: unit
-  const uint32_t cfull0 = base + 512, cempty0 = base + 528;           // [partial-tile buffer]
-  const uint32_t sfull0 = base + 544, sempty0 = base + 576;           // [scale buffer]
+  const uint32_t cfull0 = base + 512, cempty0 = base + 544;           // [partial-tile buffer]
+  const uint32_t sfull0 = base + 576, sempty0 = base + 608;           // [scale buffer]
+  int* cunit = reinterpret_cast<int*>(smem_raw + 640);                // [partial-tile buffer]: its unit, -1 = end
   float* comb = reinterpret_cast<float*>(smem_raw + kRingHeadBytes);   // [buffer][warp][lane][4]
   const uint32_t sbuf_off = (uint32_t)(kRingHeadBytes + kRingCombBytes);
   const uint32_t ring_addr =
@@ -141,7 +147,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       mbar_init(full0 + 8u * s, 1);
       mbar_init(empty0 + 8u * s, kRingConsumerWarps);
     }
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < kRingCombBufs; ++h) {
       mbar_init(cfull0 + 8u * h, kRingConsumerWarps);
       mbar_init(cempty0 + 8u * h, 1);
     }
@@ -162,7 +168,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     return false;
   };
 
-  if (warp == kRingConsumerWarps) {
+  if (warp == kRingProducerWarp) {
     // ------------------------------------------------------------ producer
     int* sched = rp.sched;
     const int units = rp.units;
@@ -287,9 +293,57 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
     return;
   }
 
-  // -------------------------------------------------------------- consumers
   const int g = lane >> 2, t = lane & 3;
   const int gr = ring_row(g);
+
+  if (warp == kRingReducerWarp) {
+    // ------------------------------------------------------------ reducer
+    pdl_wait();
+    uint32_t out_flag = 0;
+    if constexpr (kPeerEpi<EPI>) out_flag = exchange_flag(*p.out_step, p.out_tag, p.out_tags);
+    for (int k = 0;; ++k) {
+      const int b = k & (kRingCombBufs - 1);
+      if (!wait(cfull0 + 8u * b, (k / kRingCombBufs) & 1)) break;
+      const int u = cunit[b];
+      if (u < 0) break;
+      const float* cb = comb + (size_t)b * kRingConsumerWarps * 32 * 4;
+      float sum[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int w = 0; w < kRingConsumerWarps; ++w) {
+        const float4 f = *reinterpret_cast<const float4*>(cb + ((size_t)w * 32 + lane) * 4);
+        sum[0][0] += f.x;
+        sum[0][1] += f.y;
+        sum[0][2] += f.z;
+        sum[0][3] += f.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_local(cempty0 + 8u * b);
+      finish_tile<MT, EPI>(p, u, sum, lane, out_flag, gr);
+    }
+    if constexpr (EPI == EPI_PEER_ARGMAX) {
+      // The last CTA to finish (every CTA's atomicMax is then in the local
+      // keys) sends this rank's keys to every rank as flagged words.
+      int last = 0;
+      if (lane == 0) {
+        __threadfence();
+        last = atomicAdd(p.out_arrivals, 1) == (int)gridDim.x - 1;
+      }
+      if (__shfl_sync(0xffffffffu, last, 0)) {
+        __threadfence();
+        const unsigned long long f16 = (unsigned long long)exchange_flag16(out_flag) << 48;
+        for (int m = lane; m < p.M; m += 32) {
+          const unsigned long long word = (__ldcg(p.argmax_keys + m) & 0xFFFFFFFFFFFFull) | f16;
+#pragma unroll
+          for (int d = 0; d < kMaxRanks; ++d)
+            if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + (size_t)p.out_rank * p.M + m, word);
+        }
+        if (lane == 0) *p.out_arrivals = 0;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
   // this lane's 16-byte piece of a stage: box warp / 2, its half warp % 2, rows gr and gr + 8
   const uint32_t piece_off = (uint32_t)((warp >> 1) * 2048 + gr * 128 + (((4 * (warp & 1) + t) ^ gr) << 4));
   // scale group of this lane's piece in stage st
@@ -298,16 +352,29 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   stage_gamma<PRO, kRingConsumers>(p, gam_s);
   pdl_wait();
   pdl_launch_dependents();
-  uint32_t in_flag = 0, out_flag = 0;
+  uint32_t in_flag = 0;
   if constexpr (PRO == PRO_PEER_RESID_NORM) in_flag = exchange_flag(*p.in_step, p.in_tag, p.in_tags);
-  if constexpr (kPeerEpi<EPI>) out_flag = exchange_flag(*p.out_step, p.out_tag, p.out_tags);
   WaitBudget wb;
   stage_activation<BITS, PRO, kRingConsumers, 1>(p, act_s, gam_s, ssq, in_flag, wb);
 
   const __half* arow[MT] = {act_s + (size_t)min(g, p.M - 1) * p.cp + t * 8};
   int slot = 0;
   uint32_t phase = 0;
-  int nunit = 0;   // units done: partial-tile buffer nunit & 1, scale buffer nunit % 4
+  int nunit = 0;   // units done: partial-tile buffer and scale buffer nunit % 4
+  // this warp's partial tile of unit u (-1: the end) into buffer nunit % 4,
+  // once the reducer has read that buffer's previous unit
+  auto hand_off = [&](int u, const float (&acc)[MT][4]) -> bool {
+    const int b = nunit & (kRingCombBufs - 1);
+    const uint32_t use = (uint32_t)(nunit / kRingCombBufs);
+    if (use > 0 && !wait(cempty0 + 8u * b, (use - 1) & 1u)) return false;
+    float* cb = comb + (size_t)b * kRingConsumerWarps * 32 * 4;
+    *reinterpret_cast<float4*>(cb + ((size_t)warp * 32 + lane) * 4) =
+        make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+    if (warp == 0 && lane == 0) cunit[b] = u;
+    __syncwarp();
+    if (lane == 0) mbar_arrive_local(cfull0 + 8u * b);
+    return true;
+  };
   for (;;) {
     if (!wait(full0 + 8u * slot, phase)) break;
     const int u = hdr[2 * slot];
@@ -365,55 +432,14 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       }
     }
     if (!ok) break;
-    // ---- the unit's 16 partial tiles: warp u % 16 sums them in warp order
-    const int par = nunit & 1;
-    const uint32_t use = (uint32_t)(nunit >> 1);
+    // ---- the unit's partial tile goes to the reducer
+    if (!hand_off(u, acc)) break;
     ++nunit;
-    // the buffer's previous contents (two units ago) have been read
-    if (use > 0 && !wait(cempty0 + 8u * par, (use - 1) & 1u)) break;
-    float* cb = comb + (size_t)par * kRingConsumerWarps * 32 * 4;
-    *reinterpret_cast<float4*>(cb + ((size_t)warp * 32 + lane) * 4) =
-        make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-    __syncwarp();
-    if (lane == 0) mbar_arrive_local(cfull0 + 8u * par);
-    if (warp == (u & (kRingConsumerWarps - 1))) {
-      if (!wait(cfull0 + 8u * par, use & 1u)) break;
-      float sum[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-      for (int w = 0; w < kRingConsumerWarps; ++w) {
-        const float4 f = *reinterpret_cast<const float4*>(cb + ((size_t)w * 32 + lane) * 4);
-        sum[0][0] += f.x;
-        sum[0][1] += f.y;
-        sum[0][2] += f.z;
-        sum[0][3] += f.w;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive_local(cempty0 + 8u * par);
-      finish_tile<MT, EPI>(p, u, sum, lane, out_flag, gr);
-    }
   }
-
-  if constexpr (EPI == EPI_PEER_ARGMAX) {
-    // The last CTA to finish (every CTA's atomicMax is then in the local keys)
-    // sends this rank's keys to every rank as flagged words.
-    __shared__ int s_last;
-    named_sync(1, kRingConsumers);
-    if (tid == 0) {
-      __threadfence();
-      s_last = atomicAdd(p.out_arrivals, 1) == (int)gridDim.x - 1;
-    }
-    named_sync(1, kRingConsumers);
-    if (s_last) {
-      __threadfence();
-      const unsigned long long f16 = (unsigned long long)exchange_flag16(out_flag) << 48;
-      for (int m = tid; m < p.M; m += kRingConsumers) {
-        const unsigned long long word = (__ldcg(p.argmax_keys + m) & 0xFFFFFFFFFFFFull) | f16;
-#pragma unroll
-        for (int d = 0; d < kMaxRanks; ++d)
-          if (d < p.out_world) st_relaxed_sys_u64(p.out_dst[d] + (size_t)p.out_rank * p.M + m, word);
-      }
-      if (tid == 0) *p.out_arrivals = 0;
-    }
+  // end of work: an empty hand-off with unit -1 lets the reducer finish
+  if (!abort_s) {
+    float zero[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
+    hand_off(-1, zero);
   }
 }
 
