@@ -999,8 +999,10 @@ def run_decode(args, dist: Dist):
                                     args.lm_head_bits),
             "roofline": roofline, "decode_roofline": decode_roofline, "parity": parity, "gemv": gemv,
             "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": int(launches), "kernels": {k: {kk: v[kk] for kk in ("launches", "us", "GB/s")}
-                                                       for k, v in kstats.items()},
+            "gpu_launches": int(launches),
+            "kernels": {k: {**{kk: v[kk] for kk in ("launches", "us", "GB/s")},
+                            **({"gemv": wl.eng.kernel_choice[k]} if k in wl.eng.kernel_choice else {})}
+                        for k, v in kstats.items()},
             "clocks": clocks}
     if args.layers:
         line["config"]["layers"] = args.layers

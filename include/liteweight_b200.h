@@ -248,6 +248,8 @@ typedef struct {
   int sched_set;                /* 0 or 1: which of the workspace's two work-claim counters the
                                    launch uses (M <= 8 dynamic schedule). Two launches that can
                                    overlap (consecutive with pdl = 1) must use different sets. */
+  int kernel;                   /* 0: the shared-memory ring GEMV when the shape suits it (M <= 8),
+                                   else the register-pipeline GEMV; 1: the register-pipeline GEMV */
 } lw_fused_gemv_args;
 
 int lw_fused_gemv(const lw_fused_gemv_args* args, lw_stream_t stream);

@@ -282,8 +282,8 @@ cudaError_t launch_tma(StreamParams p, const StreamPlan& pl, void* ws, cudaStrea
 // large enough workspace the plan keeps tiles whole.
 template <int BITS, int PRO, int EPI>
 cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl,
-                                bool allow_fold = false, int sched_set = 0) {
-  if (!allow_fold || !fold_scales<BITS>(p.K, p.G)) {
+                                bool allow_fold = false, int sched_set = 0, bool allow_ring = true) {
+  if (allow_ring && (!allow_fold || !fold_scales<BITS>(p.K, p.G))) {
     RingPlan rpl;
     if (ws && plan_ring<BITS, PRO>(p.M, p.N, p.K, p.G, p.w, p.scales, &rpl) && rpl.ws_bytes <= ws_bytes)
       return launch_ring<BITS, PRO, EPI>(p, rpl, ws, sched_set, s, pdl);

@@ -346,8 +346,10 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   // -------------------------------------------------------------- consumers
   // this lane's 16-byte piece of a stage: box warp / 2, its half warp % 2, rows gr and gr + 8
   const uint32_t piece_off = (uint32_t)((warp >> 1) * 2048 + gr * 128 + (((4 * (warp & 1) + t) ^ gr) << 4));
-  // scale group of this lane's piece in stage st
-  auto group_of = [&](int st) -> int { return min(((st * 16 + warp) * KC + t * E) >> p.gshift, ngroups - 1); };
+  // scale group of this lane's piece in stage st (the same for every unit)
+  int goff[kRingMaxUnit];
+#pragma unroll
+  for (int st = 0; st < kRingMaxUnit; ++st) goff[st] = min(((st * 16 + warp) * KC + t * E) >> p.gshift, ngroups - 1);
 
   stage_gamma<PRO, kRingConsumers>(p, gam_s);
   pdl_wait();
@@ -391,8 +393,10 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       const unsigned short* s0 = sb + min(gr, last) * ngroups;
       const unsigned short* s1 = sb + min(gr + 8, last) * ngroups;
 #pragma unroll
-      for (int st = 0; st < kRingMaxUnit; ++st)
-        if (st < rp.spr) sv[st] = (uint32_t)s0[group_of(st)] | ((uint32_t)s1[group_of(st)] << 16);
+      for (int st = 0; st < kRingMaxUnit; ++st) {
+        if (st >= rp.spr) break;
+        sv[st] = (uint32_t)s0[goff[st]] | ((uint32_t)s1[goff[st]] << 16);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive_local(sempty0 + 8u * j);
     }

@@ -75,6 +75,7 @@ class FusedGemvArgs(ctypes.Structure):
         ("out_f32", c_void_p), ("argmax_keys", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("xin", c_void_p), ("xout", c_void_p), ("prefill_seq", c_void_p), ("sched_set", c_int),
+        ("kernel", c_int),
     ]
 
 
@@ -407,7 +408,7 @@ class DecodeEngine:
                  lm_head: torch.Tensor | None, rope_cos: torch.Tensor, rope_sin: torch.Tensor, batch: int,
                  max_seq: int, device=None, tp_rank: int = 0, tp_size: int = 1, tp_group=None, pdl: bool = True,
                  fold_scales: bool = False, exchange: str = "peer", exchange_timeout_s: float = 10.0,
-                 lm_head_quant: tuple | None = None):
+                 lm_head_quant: tuple | None = None, tune_kernels: bool = True):
         assert exchange in ("peer", "nccl")
         self.spec, self.B, self.S = spec, batch, max_seq
         self.fold = int(fold_scales)
@@ -470,6 +471,9 @@ class DecodeEngine:
         self.graph = None
         self.prefill_graphs = {}
         self.host_pos = 0
+        self.kernel_choice = {}
+        if tune_kernels:
+            self.tune_kernels()
 
     def _buffers(self, rows: int):
         """Activations of one launch shape (rows = sequences of a decode step or
@@ -763,6 +767,52 @@ class DecodeEngine:
 
     def kernels_per_step(self) -> int:
         return sum(1 for k, _, _n in self.calls if k in ("gemv", "attn", "sample"))
+
+    def tune_kernels(self, reps: int = 5, margin: float = 0.03) -> dict:
+        """Per projection class of the decode step (qkv, o, gu, down, lm_head),
+        time its launches alone (a CUDA graph replayed `reps` times, CUDA
+        events) with the shared-memory ring GEMV and with the register-pipeline
+        GEMV, and keep the ring unless the other is faster by more than
+        `margin`. Runs on the engine's scratch state (before start())."""
+        classes = []
+        for kind, _a, n in self.calls:
+            if kind == "gemv" and n not in classes:
+                classes.append(n)
+        dev = self.device
+        for name in classes:
+            ms = {}
+            for kern in (0, 1):
+                for kind, a, n in self.calls:
+                    if kind == "gemv" and n == name:
+                        a.kernel = kern
+                        self.stat_args[id(a)].kernel = kern
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    self.enqueue_only(name)
+                torch.cuda.synchronize(dev)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=side):
+                    self.enqueue_only(name)
+                g.replay()
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                ms[kern] = e0.elapsed_time(e1) / reps
+                del g
+            pick = 1 if ms[1] < ms[0] * (1.0 - margin) else 0
+            for kind, a, n in self.calls:
+                if kind == "gemv" and n == name:
+                    a.kernel = pick
+                    self.stat_args[id(a)].kernel = pick
+            self.kernel_choice[name] = {"kernel": "ring" if pick == 0 else "register-pipeline",
+                                        "ring_us": round(ms[0] * 1e3, 2), "pipeline_us": round(ms[1] * 1e3, 2)}
+        self.check()
+        return self.kernel_choice
 
     def enqueue_only(self, name: str):
         """Enqueue just the kernels of one class (qkv, attn, o, gu, down, lm_head)
