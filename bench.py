@@ -530,8 +530,11 @@ class TorchDecodeReference:
     adds :320-335, and attention through torch's scaled_dot_product_attention
     on fp16 tensors, the "sdpa" implementation HF selects by default)."""
 
-    def __init__(self, wl: DecodeWorkload):
-        self.wl, self.torch = wl, wl.torch
+    def __init__(self, wl: DecodeWorkload, split_k: int = 1):
+        # split_k > 1: every fp32 matmul sums K in that many slices (another,
+        # equally valid, accumulation order: the spread it causes is the noise
+        # floor any implementation faces at this depth)
+        self.wl, self.torch, self.split_k = wl, wl.torch, split_k
 
     def _dequant(self, q, s, bits, G):
         torch = self.torch
@@ -547,7 +550,14 @@ class TorchDecodeReference:
 
     def _lin(self, x16, pair, bits, G):
         q, s = pair
-        return (x16.float() @ self._dequant(q, s, bits, G).t()).half()
+        w = self._dequant(q, s, bits, G)
+        if self.split_k == 1:
+            return (x16.float() @ w.t()).half()
+        xs, ws = x16.float().chunk(self.split_k, dim=-1), w.chunk(self.split_k, dim=-1)
+        acc = xs[0] @ ws[0].t()
+        for xa, wa in zip(xs[1:], ws[1:]):
+            acc = acc + xa @ wa.t()
+        return acc.half()
 
     @staticmethod
     def _rmsnorm(x16, w, eps):
@@ -634,8 +644,17 @@ def decode_parity(wl: DecodeWorkload, ids_host, rank: int, steps: int = 32) -> d
     tol = 1e-2 * r.double().pow(2).sum(-1, keepdim=True).sqrt() / (r.shape[-1] ** 0.5)
     err = (got.double() - r[..., :vs].double()).abs()
     ratio = float((err / tol).max())
+    # the same reference with every matmul summed in two K halves: the spread
+    # between two valid fp32 accumulation orders through the whole depth
+    alt = TorchDecodeReference(wl, split_k=2).logits(toks[:, :P + steps], P, steps).transpose(0, 1)
+    floor = float(((alt.double() - r.double()).abs() / tol).max())
+    alt_match = float((alt.argmax(-1).cpu() == ids[:, 1:1 + steps].T).float().mean())
+    del alt
     return {"match_rate": round(match, 4), "tokens_compared": int(ids.numel()),
             "first_mismatch_step": first_mismatch, "logits_err_over_tol": round(ratio, 4),
+            "reference_vs_itself_err_over_tol": round(floor, 4),
+            "reference_vs_itself_note": "the reference with each fp32 matmul summed in two K halves vs as one "
+                                        "sum, same steps: the accumulation-order noise floor at this depth",
             "logits_steps_compared": steps, "logits_columns": f"vocab shard 0 of {wl.tp} ({vs} of {r.shape[-1]})",
             "tolerance": "max-abs err <= 1e-2 * ||ref row||_2 / sqrt(V), per (step, sequence)",
             "reference": "teacher-forced torch on the device: the same packed weights dequantized exactly with fp32 "
