@@ -648,7 +648,6 @@ def decode_parity(wl: DecodeWorkload, ids_host, rank: int, steps: int = 32) -> d
     # between two valid fp32 accumulation orders through the whole depth
     alt = TorchDecodeReference(wl, split_k=2).logits(toks[:, :P + steps], P, steps).transpose(0, 1)
     floor = float(((alt.double() - r.double()).abs() / tol).max())
-    alt_match = float((alt.argmax(-1).cpu() == ids[:, 1:1 + steps].T).float().mean())
     del alt
     return {"match_rate": round(match, 4), "tokens_compared": int(ids.numel()),
             "first_mismatch_step": first_mismatch, "logits_err_over_tol": round(ratio, 4),
