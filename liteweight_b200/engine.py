@@ -1029,12 +1029,15 @@ def build_engine(spec: LlamaSpec, layers: list, embed: torch.Tensor, final_norm:
                  lm_head: torch.Tensor | None, inv_freq: torch.Tensor, batch: int, max_seq: int, device,
                  attention_scaling: float = 1.0, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
                  pdl: bool = True, fold_scales: bool = False, exchange: str = "peer",
-                 lm_head_quant: tuple | None = None) -> DecodeEngine:
-    """Engine from unsharded LayerWeights (liteweight-format tensors, any device)."""
+                 lm_head_quant: tuple | None = None, tune_kernels: bool = True) -> DecodeEngine:
+    """Engine from unsharded LayerWeights (liteweight-format tensors, any device).
+    tune_kernels=False keeps the default GEMV choice (the ring kernel wherever
+    it applies) instead of timing both, so two engines give the same bits."""
     packed = [PackedLayer(lw, spec, tp_rank, tp_size, device) for lw in layers]
     cos, sin = rope_tables(inv_freq, max_seq, attention_scaling, device)
     return DecodeEngine(spec, packed, embed, final_norm, lm_head, cos, sin, batch, max_seq, device, tp_rank,
-                        tp_size, tp_group, pdl, fold_scales, exchange, lm_head_quant=lm_head_quant)
+                        tp_size, tp_group, pdl, fold_scales, exchange, lm_head_quant=lm_head_quant,
+                        tune_kernels=tune_kernels)
 
 
 def synthetic_layers(spec: LlamaSpec, device, seed: int = 0, std: float = 0.02) -> list:

@@ -210,7 +210,7 @@ def _nccl_worker(rank, world, port, out_path, exchange):
     dist.all_reduce(t1)          # communicator up before graph capture
     eng = E.build_engine(_spec(w, 4), _layer_weights(w, to), to(w.embed), to(w.norm), None,
                          torch.from_numpy(w.inv_freq), 2, 64, dev, tp_rank=rank, tp_size=world,
-                         tp_group=dist.group.WORLD, exchange=exchange)
+                         tp_group=dist.group.WORLD, exchange=exchange, tune_kernels=False)
     P, T = 6, 5
     prompt = np.random.default_rng(3).integers(0, w.shape.vocab, (2, P))
     shards = []
