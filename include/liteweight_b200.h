@@ -245,9 +245,7 @@ typedef struct {
   const lw_exchange_out* xout;  /* LW_EPI_PEER_*; read at the call */
   const int* prefill_seq;       /* NULL: decode (row m = sequence m). Else a prompt chunk: the M
                                    rows are positions *pos .. *pos + M - 1 of sequence *prefill_seq */
-  int sched_set;                /* 0 or 1: which of the workspace's two work-claim counters the
-                                   launch uses (M <= 8 dynamic schedule). Two launches that can
-                                   overlap (consecutive with pdl = 1) must use different sets. */
+  int sched_set;                /* reserved (ignored): the ring GEMV's schedule is static */
   int kernel;                   /* 0: the shared-memory ring GEMV when the shape suits it (M <= 8),
                                    else the register-pipeline GEMV; 1: the register-pipeline GEMV */
 } lw_fused_gemv_args;

@@ -63,7 +63,7 @@ inline StreamParams to_stream(const lw_fused_gemv_args* a) {
 template <int BITS, int PRO, int EPI>
 cudaError_t fused_launch(const lw_fused_gemv_args* a, cudaStream_t s) {
   return launch_stream_block<BITS, PRO, EPI>(to_stream(a), a->workspace, a->workspace_bytes, s, a->pdl != 0,
-                                             a->fold_scales != 0, a->sched_set, a->kernel != 1);
+                                             a->fold_scales != 0, a->kernel != 1);
 }
 
 template <int BITS, int PRO, int EPI>

@@ -282,8 +282,7 @@ cudaError_t matmul_dispatch(const void* act, const void* w, const void* scales, 
   if (!stream_ok<BITS>(act, w, K, G)) {
     // shapes the register-pipeline kernel cannot take may still suit the ring kernel
     lw::RingPlan rpl;
-    if (M <= 8 && ws && ring_ok<BITS>(act, w, K, G) && lw::plan_ring<BITS, lw::PRO_PLAIN>(M, N, K, G, w, scales, &rpl) &&
-        rpl.ws_bytes <= ws_bytes) {
+    if (M <= 8 && ring_ok<BITS>(act, w, K, G) && lw::plan_ring<BITS, lw::PRO_PLAIN>(M, N, K, G, w, scales, &rpl)) {
       lw::StreamParams p = {};
       p.M = M;
       p.act = static_cast<const __half*>(act);
@@ -296,7 +295,7 @@ cudaError_t matmul_dispatch(const void* act, const void* w, const void* scales, 
       p.N = N;
       p.K = K;
       p.G = G;
-      return lw::launch_ring<BITS, lw::PRO_PLAIN, lw::EPI_PLAIN>(p, rpl, ws, 0, s, false);
+      return lw::launch_ring<BITS, lw::PRO_PLAIN, lw::EPI_PLAIN>(p, rpl, s, false);
     }
     GemvParams p = {};
     p.act = static_cast<const __half*>(act);

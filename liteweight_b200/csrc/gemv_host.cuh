@@ -20,15 +20,10 @@ constexpr int kBatch = 2;                  // 16-byte chunks per row per registe
 template <int BITS>
 constexpr int kBatchOf = BITS == 16 ? 4 : kBatch;
 // Workspace layout: a fixed region of per-tile counters (kept zero between
-// calls, so any later call of any shape finds its counters zero) whose last
-// kSchedBytes hold the ring kernel's two work-claim counter sets (also kept
-// zero), then the fp32 slots, which are fully rewritten before they are read.
+// calls, so any later call of any shape finds its counters zero), then the
+// fp32 slots, which are fully rewritten before they are read.
 constexpr size_t kCounterBytes = 64 * 1024;
-constexpr size_t kSchedBytes = 256;
-constexpr int kMaxSplitTiles = (int)((kCounterBytes - kSchedBytes) / 4);
-inline int* sched_counters(void* ws, int set) {
-  return reinterpret_cast<int*>(static_cast<char*>(ws) + kCounterBytes - kSchedBytes) + (set & 1) * kRingSchedInts;
-}
+constexpr int kMaxSplitTiles = (int)(kCounterBytes / 4);
 
 inline int device_sm_count() {
   int dev = 0, n = 0;
@@ -188,8 +183,10 @@ struct RingPlan {
 // scales: the unit copy needs 16-byte aligned blocks of whole 16-byte multiples
 // (16 rows x groups x 2 bytes; for the last tile, (N mod 16) rows) that fit a
 // unit buffer; a null `scales` (sizing only) skips the alignment check.
+// fold: the codes variant (fold_scales<BITS>(K, G) must hold), which also
+// stages per-chunk activation sums.
 template <int BITS, int PRO>
-bool plan_ring(int M, int N, int K, int G, const void* w, const void* scales, RingPlan* pl) {
+bool plan_ring(int M, int N, int K, int G, const void* w, const void* scales, RingPlan* pl, bool fold = false) {
   constexpr int KC = 4 * WT<BITS>::E;
   if (!ring_enabled() || M < 1 || M > 8 || N < 16) return false;
   if (BITS < 16) {
@@ -211,19 +208,19 @@ bool plan_ring(int M, int N, int K, int G, const void* w, const void* scales, Ri
   pl->kchunks = 16 * pl->spr;
   const int kpad = pl->kchunks * KC;
   pl->cp = ((size_t)M * (kpad + 32) * 2 + gamma_bytes(PRO, K) <= (size_t)kStageBudget) ? kpad + 32 : kpad;
-  const size_t act = align_up((size_t)M * pl->cp * 2 + gamma_bytes(PRO, K), 16);
+  const size_t act = align_up((size_t)M * pl->cp * 2 + gamma_bytes(PRO, K), 16) + (fold ? ring_asum_bytes(pl->spr) : 0);
   const size_t fixed = (size_t)kRingFixedBytes + act + kRingStaticBytes;
   if (fixed + (size_t)kRingMinStages * kRingStageBytes > kRingSmemMax) return false;
   pl->stages = (int)std::min<size_t>(kRingMaxStages, (kRingSmemMax - fixed) / kRingStageBytes);
   pl->smem = (size_t)kRingFixedBytes + (size_t)pl->stages * kRingStageBytes + act;
   pl->units = (N + 15) / 16;
   pl->grid = std::min(device_sm_count(), pl->units);
-  pl->ws_bytes = kCounterBytes;   // the work-claim counters at its end
+  pl->ws_bytes = 0;               // static schedule, whole tiles: no workspace
   return true;
 }
 
-template <int BITS, int PRO, int EPI>
-cudaError_t launch_ring(StreamParams p, const RingPlan& pl, void* ws, int sched_set, cudaStream_t s, bool pdl) {
+template <int BITS, int PRO, int EPI, bool FOLD = false>
+cudaError_t launch_ring(StreamParams p, const RingPlan& pl, cudaStream_t s, bool pdl) {
   RingParams rp;
   memset(&rp, 0, sizeof(rp));
   const size_t rowbytes = (size_t)p.K * BITS / 8;
@@ -243,8 +240,7 @@ cudaError_t launch_ring(StreamParams p, const RingPlan& pl, void* ws, int sched_
   rp.boxes_last = pl.boxes_last;
   rp.units = pl.units;
   rp.stages = pl.stages;
-  rp.sched = sched_counters(ws, sched_set);
-  auto kern = gemv_ring_kernel<BITS, PRO, EPI>;
+  auto kern = gemv_ring_kernel<BITS, PRO, EPI, FOLD>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
   return lw_launch(kern, dim3(pl.grid), dim3(kRingThreads), pl.smem, s, pdl, rp);
@@ -282,11 +278,16 @@ cudaError_t launch_tma(StreamParams p, const StreamPlan& pl, void* ws, cudaStrea
 // large enough workspace the plan keeps tiles whole.
 template <int BITS, int PRO, int EPI>
 cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl,
-                                bool allow_fold = false, int sched_set = 0, bool allow_ring = true) {
-  if (allow_ring && (!allow_fold || !fold_scales<BITS>(p.K, p.G))) {
+                                bool allow_fold = false, bool allow_ring = true) {
+  if (allow_ring) {
+    const bool fold = allow_fold && fold_scales<BITS>(p.K, p.G);
     RingPlan rpl;
-    if (ws && plan_ring<BITS, PRO>(p.M, p.N, p.K, p.G, p.w, p.scales, &rpl) && rpl.ws_bytes <= ws_bytes)
-      return launch_ring<BITS, PRO, EPI>(p, rpl, ws, sched_set, s, pdl);
+    if (plan_ring<BITS, PRO>(p.M, p.N, p.K, p.G, p.w, p.scales, &rpl, fold)) {
+      if constexpr (BITS < 16) {
+        if (fold) return launch_ring<BITS, PRO, EPI, true>(p, rpl, s, pdl);
+      }
+      return launch_ring<BITS, PRO, EPI>(p, rpl, s, pdl);
+    }
   }
   StreamPlan pl;
   if constexpr (BITS != 16 && EPI != EPI_PEER_ARGMAX) {
@@ -354,10 +355,7 @@ size_t stream_workspace(int M, int N, int K) {
   const int rows = stage_rows<BITS>(K);
   for (int m0 = 0; m0 < M; m0 += rows) {
     const int mb = std::min(rows, M - m0);
-    // the ring kernel (when the group size suits it: not known here) needs
-    // the counter region; the split-tile kernel is its fallback
-    RingPlan rpl;
-    if (plan_ring<BITS, PRO>(mb, N, K, BITS < 16 ? K : 0, nullptr, nullptr, &rpl)) need = std::max(need, rpl.ws_bytes);
+    // (the ring kernel needs none; the split-tile kernel is its fallback)
     StreamPlan pl;
     if (BITS != 16 && EPI != EPI_PEER_ARGMAX && tma_enabled() && plan_tma<BITS, PRO>(mb, N, K, true, &pl)) {
       need = std::max(need, pl.ws_bytes);

@@ -12,12 +12,10 @@
 // row bytes are not whole 128-byte chunks - 128-byte swizzle), `spr` stages
 // per unit; its fp16 scales (16 consecutive rows of the scale matrix, one
 // contiguous block) arrive with one bulk copy into one of four unit buffers.
-// CTA b takes units b and b + grid, then claims further ones from a global
-// counter (in the workspace; the last CTA to finish claiming resets it), with
-// four claims in flight ahead of their use: SMs that get less memory
-// bandwidth take fewer units, and all CTAs finish within about one unit of
-// each other. A tile is never split between CTAs: no partial sum leaves the
-// SM.
+// CTA b takes units b, b + grid, b + 2 grid, ...: no CTA waits on another or
+// on a global counter (claiming units through one atomic counter was measured
+// slower: under a full weight stream each claim's round trip stalls the
+// producer). A tile is never split between CTAs: no partial sum leaves the SM.
 //
 // Roles (one CTA per SM, 18 warps):
 //   warp 16    one lane copies each unit's scales into the next free unit
@@ -29,10 +27,12 @@
 //   warps 0-15 warp w owns chunk w (64 bytes of each row) of every stage: per
 //              stage each lane reads 16 bytes of two rows, unpacks and scales
 //              them, and feeds mma.sync m16n8k16 with the staged activation
-//              as operand B; it takes its scales for the whole unit from the
-//              unit buffer at the unit's start. At the end of a unit every
-//              warp writes its partial tile into one of four shared-memory
-//              buffers and goes on to the next unit.
+//              as operand B, spreading the MMAs over four accumulators (a
+//              dependent mma.sync waits for the previous result); it takes
+//              its scales for the whole unit from the unit buffer at the
+//              unit's start. At the end of a unit every warp writes its
+//              partial tile into one of four shared-memory buffers and goes
+//              on to the next unit.
 //   warp 17    the reducer: sums each unit's 16 partial tiles in warp order
 //              (the same sums on every run) and applies the epilogue, off the
 //              consumers' path.
@@ -76,7 +76,6 @@ constexpr long long kRingWaitNs = 2000000000;          // 2 s: far beyond any co
 // ranks (PRO_PEER_RESID_NORM, up to in_timeout_ns): its bound is this much
 // longer than the latter.
 constexpr long long kRingProducerWaitNs = 60000000000LL;
-constexpr int kRingSchedInts = 4;                      // per schedule set: claim counter, done counter, pad
 
 struct RingParams {
   StreamParams p;          // matmul, prologue, epilogue (p.kchunks = 16 * spr, p.cp staged row stride)
@@ -86,7 +85,6 @@ struct RingParams {
   int units;               // ceil(N / 16)
   int stages;              // ring slots
   int map3d;               // 1: tm_w is the 3-D view {128 bytes, rows, row bytes / 128}, one box per stage
-  int* sched;              // {claims, done}: zero before the first launch, left zero
 };
 
 LW_DEV void tma_load_box(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -111,7 +109,157 @@ LW_DEV void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" :
 // The lane's lower tile row (see the file comment).
 LW_DEV int ring_row(int g) { return (g >> 1) | ((g & 1) << 2); }
 
-template <int BITS, int PRO, int EPI>
+// gemv_piece (exact dequant) for one row pair, its MMAs spread over four
+// accumulators: a dependent mma.sync waits for its predecessor's result, so
+// one accumulator per warp would make each stage a chain of 8 MMAs.
+template <int BITS>
+LW_DEV void ring_piece(float (&acc)[4][4], const uint4& qa, const uint4& qb, uint32_t sa, uint32_t sb,
+                       const __half* arow, int off) {
+  const uint32_t* a32 = reinterpret_cast<const uint32_t*>(&qa);
+  const uint32_t* b32 = reinterpret_cast<const uint32_t*>(&qb);
+  if constexpr (BITS == 4) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      uint32_t A[4], B[4];
+      unpack_int4_word(a32[w], A);
+      unpack_int4_word(b32[w], B);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        A[i] = hmul2_rn(A[i], sa);
+        B[i] = hmul2_rn(B[i], sb);
+      }
+      const uint4 av = *reinterpret_cast<const uint4*>(arow + off + w * 32);
+      mma16816(acc[(2 * w) & 3], A[0], B[0], A[1], B[1], av.x, av.y);
+      mma16816(acc[(2 * w + 1) & 3], A[2], B[2], A[3], B[3], av.z, av.w);
+    }
+  } else if constexpr (BITS == 8) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 av = *reinterpret_cast<const uint4*>(arow + off + j * 32);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t A[2], B[2];
+        dequant_int8_word(a32[2 * j + h], A);
+        dequant_int8_word(b32[2 * j + h], B);
+        A[0] = hmul2_rn(A[0], sa);
+        A[1] = hmul2_rn(A[1], sa);
+        B[0] = hmul2_rn(B[0], sb);
+        B[1] = hmul2_rn(B[1], sb);
+        mma16816(acc[2 * j + h], A[0], B[0], A[1], B[1], h ? av.z : av.x, h ? av.w : av.y);
+      }
+    }
+  } else {
+    const uint4 av = *reinterpret_cast<const uint4*>(arow + off);
+    mma16816(acc[0], qa.x, qb.x, qa.y, qb.y, av.x, av.y);
+    mma16816(acc[1], qa.z, qb.z, qa.w, qb.w, av.z, av.w);
+  }
+}
+
+// ---- codes variant (FOLD): scales applied per chunk in fp32
+// Each code enters the tensor core as an exact fp16 subnormal: (code + 8) *
+// 2^-24 for INT4 (the nibble XOR 8 in the low bits of a half; a nibble four
+// bits up is 16 times that and is summed apart) and (code + 128) * 2^-24 for
+// INT8 (the byte XOR 0x80). For a 64-byte chunk of a row (one scale group) the
+// fp32 sum d of those products gives
+//   sum_k code_k * a_k = 2^24 * d - OFF * sum_k a_k      (OFF = 8 or 128)
+// with sum_k a_k the chunk's activation sum, staged once per launch; the
+// result is scaled by the group's scale in fp32. The weights are not rounded
+// to fp16(code * scale) first, so this is an opt-in (fold_scales), not the
+// numerics of liteweight's dequantize.
+LW_DEV void codes_int4_word(uint32_t q, uint32_t (&o)[4]) {
+  const uint32_t mlo = 0x000F000Fu, mhi = 0x00F000F0u, xlo = 0x00080008u, xhi = 0x00800080u;
+  asm("{\n"
+      " .reg .b32 y;\n"
+      " shr.u32 y, %4, 8;\n"
+      " lop3.b32 %0, %4, %5, %7, 0x6a;\n"
+      " lop3.b32 %1, %4, %6, %8, 0x6a;\n"
+      " lop3.b32 %2, y, %5, %7, 0x6a;\n"
+      " lop3.b32 %3, y, %6, %8, 0x6a;\n"
+      "}\n"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(q), "r"(mlo), "r"(mhi), "r"(xlo), "r"(xhi));
+}
+
+// bytes 0, 1 (o[0]) and 2, 3 (o[1]) as (code + 128) * 2^-24
+LW_DEV void codes_int8_word(uint32_t q, uint32_t (&o)[2]) {
+  const uint32_t x = q ^ 0x80808080u;
+  o[0] = __byte_perm(x, 0u, 0x4140);
+  o[1] = __byte_perm(x, 0u, 0x4342);
+}
+
+// d = a * b (no accumulator input)
+LW_DEV void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+// The lane's 16-byte pieces of rows gr (qa) and gr + 8 (qb) in one chunk:
+// d (INT4: the low nibbles into dlo, the high ones into dhi; two chains of
+// each) starts from zero. Same activation pairing as gemv_piece
+// (perm_int4_pairs for INT4).
+template <int BITS>
+LW_DEV void ring_codes_piece(float (&dlo)[2][4], float (&dhi)[2][4], const uint4& qa, const uint4& qb,
+                             const __half* arow, int off) {
+  const uint32_t* a32 = reinterpret_cast<const uint32_t*>(&qa);
+  const uint32_t* b32 = reinterpret_cast<const uint32_t*>(&qb);
+  if constexpr (BITS == 4) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      uint32_t A[4], B[4];
+      codes_int4_word(a32[w], A);
+      codes_int4_word(b32[w], B);
+      const uint4 av = *reinterpret_cast<const uint4*>(arow + off + w * 32);
+      if (w < 2) {
+        mma16816_z(dlo[w & 1], A[0], B[0], A[2], B[2], av.x, av.z);
+        mma16816_z(dhi[w & 1], A[1], B[1], A[3], B[3], av.y, av.w);
+      } else {
+        mma16816(dlo[w & 1], A[0], B[0], A[2], B[2], av.x, av.z);
+        mma16816(dhi[w & 1], A[1], B[1], A[3], B[3], av.y, av.w);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 av = *reinterpret_cast<const uint4*>(arow + off + j * 32);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t A[2], B[2];
+        codes_int8_word(a32[2 * j + h], A);
+        codes_int8_word(b32[2 * j + h], B);
+        if (j == 0)
+          mma16816_z(dlo[h], A[0], B[0], A[1], B[1], h ? av.z : av.x, h ? av.w : av.y);
+        else
+          mma16816(dlo[h], A[0], B[0], A[1], B[1], h ? av.z : av.x, h ? av.w : av.y);
+      }
+    }
+  }
+}
+
+// acc += scale * (2^24 d - OFF * asum) for the lane's rows (lo, hi: the two
+// fp16 scales in s2) and columns 2t, 2t + 1 (asum: that chunk's activation sums).
+template <int BITS>
+LW_DEV void ring_codes_finish(float (&acc)[4], const float (&dlo)[2][4], const float (&dhi)[2][4], uint32_t s2,
+                              float2 asum) {
+  constexpr float kOff = BITS == 4 ? 8.f : 128.f;
+  const float slo = __half2float(__ushort_as_half((unsigned short)(s2 & 0xFFFFu)));
+  const float shi = __half2float(__ushort_as_half((unsigned short)(s2 >> 16)));
+  const float s24[2] = {slo * 16777216.f, shi * 16777216.f};   // exact: a power of two
+  const float soff[2] = {-kOff * slo, -kOff * shi};            // exact likewise
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = dlo[0][i] + dlo[1][i];
+    const float d = BITS == 4 ? fmaf(dhi[0][i] + dhi[1][i], 0.0625f, lo) : lo;
+    acc[i] = fmaf(d, s24[i >> 1], fmaf(soff[i >> 1], (i & 1) ? asum.y : asum.x, acc[i]));
+  }
+}
+
+// Shared memory of the per-chunk activation sums of the codes variant: [chunk][8 columns] fp32.
+__host__ __device__ constexpr int ring_asum_bytes(int spr) { return 16 * spr * 8 * 4; }
+
+template <int BITS, int PRO, int EPI, bool FOLD = false>
 __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid_constant__ RingParams rp) {
   constexpr int MT = 1;
   constexpr int E = WT<BITS>::E;
@@ -141,6 +289,10 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   uint8_t* ring = smem_raw + (ring_addr - base);
   __half* act_s = reinterpret_cast<__half*>(ring + (size_t)S * kRingStageBytes);
   __half* gam_s = act_s + (size_t)p.M * p.cp;
+  // (codes variant) per-chunk activation sums, after the activation and gamma
+  float* asum_s = reinterpret_cast<float*>(
+      reinterpret_cast<uint8_t*>(act_s) +
+      (((size_t)p.M * p.cp * 2 + (PRO == PRO_PLAIN ? 0 : (size_t)(p.K + 7) / 8 * 16) + 15) & ~(size_t)15));
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -170,7 +322,6 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
 
   if (warp == kRingProducerWarp) {
     // ------------------------------------------------------------ producer
-    int* sched = rp.sched;
     const int units = rp.units;
     const int grid = (int)gridDim.x;
     // the free-slot wait: long bound, gives up at once when a consumer aborted
@@ -187,15 +338,8 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       abort_s = 1;
       return false;
     };
-    // units b, b + grid, then claims (2 grid and up); lane 0 keeps four claim atomics in flight
-    auto issue_claim = [&]() -> int { return lane == 0 ? 2 * grid + atomicAdd(sched, 1) : 0; };
-    auto resolve = [&](int c) -> int {
-      c = __shfl_sync(0xffffffffu, c, 0);
-      return c < units ? c : units;
-    };
-    int u = (int)blockIdx.x;          // the grid never exceeds the unit count
-    int nxt = min(u + grid, units);
-    int qa = issue_claim(), qb = issue_claim(), qc = issue_claim(), qd = issue_claim();
+    // units b, b + grid, b + 2 grid, ...
+    int u = (int)blockIdx.x;
     int slot = 0, nunit = 0;
     uint32_t phase = 0;               // parity of the ring's current lap
     uint32_t issued = 0;              // bit s: slot s has held a copy
@@ -243,14 +387,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
           phase ^= 1u;
         }
       }
-      u = nxt;
-      if (u < units) {
-        nxt = resolve(qa);   // claimed four units ago
-        qa = qb;
-        qb = qc;
-        qc = qd;
-        qd = issue_claim();
-      }
+      u += grid;
     }
     if (live) {
       // end of work: an empty stage with header -1
@@ -264,18 +401,6 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
         issued &= ~(1u << slot);
       } else {
         live = false;
-      }
-    }
-    if (lane == 0) {
-      // The last CTA to finish claiming resets the schedule for the next
-      // launch. The claims still in flight are waited for first (their
-      // results are consumed), so none reaches the counter after the reset.
-      asm volatile("" ::"r"(qa), "r"(qb), "r"(qc), "r"(qd));
-      __threadfence();
-      if (atomicAdd(sched + 1, 1) == grid - 1) {
-        sched[0] = 0;
-        sched[1] = 0;
-        __threadfence();
       }
     }
     // No copy may land after the CTA has exited: wait (bounded) for each
@@ -358,6 +483,20 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
   if constexpr (PRO == PRO_PEER_RESID_NORM) in_flag = exchange_flag(*p.in_step, p.in_tag, p.in_tags);
   WaitBudget wb;
   stage_activation<BITS, PRO, kRingConsumers, 1>(p, act_s, gam_s, ssq, in_flag, wb);
+  if constexpr (FOLD) {
+    // each chunk's activation sum per column (columns past M: zero)
+    for (int c = warp; c < p.kchunks; c += kRingConsumerWarps) {
+      for (int m = 0; m < 8; ++m) {
+        float sum = 0.f;
+        if (m < p.M) {
+          for (int e = lane; e < KC; e += 32) sum += __half2float(act_s[(size_t)m * p.cp + c * KC + e]);
+          sum = warp_sum(sum);
+        }
+        if (lane == 0) asum_s[c * 8 + m] = sum;
+      }
+    }
+    stage_sync<1, kRingConsumers>();
+  }
 
   const __half* arow[MT] = {act_s + (size_t)min(g, p.M - 1) * p.cp + t * 8};
   int slot = 0;
@@ -400,14 +539,22 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       __syncwarp();
       if (lane == 0) mbar_arrive_local(sempty0 + 8u * j);
     }
-    float acc[MT][4] = {{0.f, 0.f, 0.f, 0.f}};
+    float acc[MT][4] = {{0.f, 0.f, 0.f, 0.f}};   // codes variant: the unit's sum
+    float acc4[4][4] = {};                        // exact: four chains, summed at the unit's end
     bool ok = true;
     auto one = [&](int st, uint32_t s2) {
       const uint8_t* sp = ring + (size_t)slot * kRingStageBytes + piece_off;
       const uint4 qa = lds128(sp), qb = lds128(sp + 8 * 128);
       const int off = (st * 16 + warp) * KC;
-      const uint32_t sa = __byte_perm(s2, 0, 0x1010), sb = __byte_perm(s2, 0, 0x3232);
-      gemv_piece<BITS, MT>(acc, qa, qb, sa, sb, arow, off);
+      if constexpr (FOLD) {
+        float dlo[2][4], dhi[2][4];
+        ring_codes_piece<BITS>(dlo, dhi, qa, qb, arow[0], off);
+        const float2 as = *reinterpret_cast<const float2*>(asum_s + (st * 16 + warp) * 8 + 2 * t);
+        ring_codes_finish<BITS>(acc[0], dlo, dhi, s2, as);
+      } else {
+        const uint32_t sa = __byte_perm(s2, 0, 0x1010), sb = __byte_perm(s2, 0, 0x3232);
+        ring_piece<BITS>(acc4, qa, qb, sa, sb, arow[0], off);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive_local(empty0 + 8u * slot);
       if (++slot == S) {
@@ -436,6 +583,10 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       }
     }
     if (!ok) break;
+    if constexpr (!FOLD) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[0][i] = (acc4[0][i] + acc4[1][i]) + (acc4[2][i] + acc4[3][i]);
+    }
     // ---- the unit's partial tile goes to the reducer
     if (!hand_off(u, acc)) break;
     ++nunit;

@@ -499,10 +499,6 @@ class DecodeEngine:
     def _gemv(self, rows: int, **kw) -> FusedGemvArgs:
         a = FusedGemvArgs()
         a.pdl, a.M, a.eps, a.fold_scales = self.pdl, rows, self.spec.eps, self.fold
-        # consecutive GEMVs of a call list may overlap (programmatic dependent
-        # launch): they take turns with the workspace's two work-claim counters
-        a.sched_set = self._sched_next
-        self._sched_next ^= 1
         for k, v in kw.items():
             setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
         return a
@@ -516,7 +512,6 @@ class DecodeEngine:
         tp = self.tp_size > 1
         ex = self.exchange
         seq = self.seq.data_ptr() if prefill else None
-        self._sched_next = 0
         calls = []
         xs = [bufs.x, bufs.x2]
         cur = 0           # index of the buffer holding the residual stream
@@ -618,7 +613,6 @@ class DecodeEngine:
         seq = self.seq.data_ptr()
         tp = self.tp_size > 1
         bufs.sample_xin = None
-        self._sched_next = 0
         calls = [("prefill_embed", bufs, "embed")]
 
         def tc(epi, N, K, w, s_, act, lda, out, ldo, **kw):
@@ -690,14 +684,6 @@ class DecodeEngine:
         self.calls, gemv_args = self._make_calls(self.dec, prefill=False)
         self._attach_workspace(gemv_args)
         self.stat_args = {id(a): self._stat_variant(a) for a in gemv_args}
-        # enqueue_only() runs a class's launches back to back: they take turns
-        # with the work-claim counters there too
-        turn = {}
-        for kind, a, name in self.calls:
-            if kind == "gemv":
-                b = self.stat_args[id(a)]
-                b.sched_set = turn.get(name, 0)
-                turn[name] = b.sched_set ^ 1
         self.x_in = self.x   # layer 0 reads the residual stream from self.x; sample writes it there
         self.sample_xin = self.exchange.in_ptr(2 * len(self.layers)) if self.exchange is not None else None
         self.prefill_calls = {}

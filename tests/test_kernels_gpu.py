@@ -9,6 +9,8 @@ Tolerances:
     rtol 1e-3 for fp16 and INT8, 0.05 / 1e-2 for INT4; tests/test_kernels.py).
 """
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -395,9 +397,8 @@ def test_graph_survives_workspace_growth():
 ])
 def test_ring_edges(bits, M, K, N, G):
     """M <= 8 shapes on the TMA-ring GEMV: ragged row blocks, partial last
-    stages, per-channel scales, long rows; bit-identical on a repeat call (the
-    dynamic unit schedule does not change the sums) and the workspace's
-    counters (work claims included) are zero again afterwards."""
+    stages, per-channel scales, long rows; bit-identical on a repeat call and
+    the workspace's counters are zero again afterwards."""
     from liteweight_b200 import _native as nat
     rng = np.random.default_rng(bits * 31 + M)
     act = rng.standard_normal((M, K)).astype(np.float16)
@@ -411,8 +412,7 @@ def test_ring_edges(bits, M, K, N, G):
     qt = torch.from_numpy(q).to(DEV)
     st = torch.from_numpy(s).to(DEV) if s is not None else None
     need = int(nat.lib().lw_gemm_workspace_size(bits, M, N, K))
-    assert need >= 64 * 1024
-    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    ws = torch.zeros(max(need, 64 * 1024), dtype=torch.uint8, device=DEV)
     nat.lib().lw_take_device_error()   # start from clear device error flags
     stream = torch.cuda.current_stream().cuda_stream
     outs = []
@@ -428,6 +428,58 @@ def test_ring_edges(bits, M, K, N, G):
     torch.cuda.synchronize()
     assert nat.lib().lw_take_device_error() == 0
     check_rows(outs[0], ref, f"ring bits={bits} {M}x{K}x{N} G{G}")
+    assert torch.equal(outs[0], outs[1])
+    assert int(ws[: 64 * 1024].count_nonzero()) == 0
+
+
+@pytest.mark.parametrize("bits,M,K,N,G", [
+    (4, 1, 4096, 4096, 128),     # a decode projection
+    (4, 5, 3072, 3000, 128),     # partial last stage (3-D copy fills zeros), ragged last tile
+    (4, 8, 4096, 2048, 4096),    # per-output-channel scales
+    (4, 2, 14336, 4096, 128),    # a long row
+    (8, 1, 2048, 8192, 2048),    # per-output-channel INT8
+    (8, 3, 4096, 4096, 128),
+])
+def test_ring_codes_variant(bits, M, K, N, G):
+    """The ring GEMV's codes variant (fold_scales: codes as fp16 subnormals,
+    per-chunk fp32 scale): within one fp16 rounding of the exact fp64
+    sum_k code * scale * a, inside the drop-in row tolerance of the oracle's
+    exact-dequant matmul, and bit-identical on a repeat call."""
+    from liteweight_b200 import _native as nat
+    from liteweight_b200 import engine as E
+    rng = np.random.default_rng(bits * 7 + M + K)
+    act = rng.standard_normal((M, K)).astype(np.float16)
+    q, s = quantized(N, K, G, bits, seed=N + K + 1)
+    codes = oq.unpack_int4(q) if bits == 4 else q
+    w64 = codes.astype(np.float64) * np.repeat(s.astype(np.float64), G, axis=1)
+    exact = act.astype(np.float64) @ w64.T
+    a, qt, st = (torch.from_numpy(x).to(DEV) for x in (act, q, s))
+    args = E.FusedGemvArgs()
+    args.bits, args.prologue, args.epilogue = bits, E.PRO_PLAIN, E.EPI_PLAIN
+    args.M, args.N, args.K, args.group_size, args.lda, args.ldo = M, N, K, G, K, N
+    args.act, args.weight, args.scales = a.data_ptr(), qt.data_ptr(), st.data_ptr()
+    args.fold_scales, args.kernel, args.pdl = 1, 0, 0
+    need = int(nat.lib().lw_fused_gemv_workspace_size(ctypes.byref(args)))
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=DEV)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    nat.lib().lw_take_device_error()
+    outs = []
+    for _ in range(2):
+        o = torch.empty(M, N, dtype=torch.float16, device=DEV)
+        args.out = o.data_ptr()
+        nat.check("lw_fused_gemv", nat.lib().lw_fused_gemv(ctypes.byref(args), torch.cuda.current_stream().cuda_stream))
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert nat.lib().lw_take_device_error() == 0
+    got = outs[0].float().cpu().numpy().astype(np.float64)
+    # one fp16 rounding of the exact value (half an ulp), plus the fp32 sums'
+    # rounding, bounded by a small multiple of sum_k |code * scale * a|
+    ulp = np.spacing(np.abs(exact).astype(np.float16)).astype(np.float64)
+    absmag = np.abs(act.astype(np.float64)) @ np.abs(w64).T
+    err = np.abs(got - exact)
+    bound = 0.5 * ulp + 1e-5 * absmag + 1e-7
+    assert np.all(err <= bound), f"codes bits={bits}: worst err/bound {(err / bound).max():.3f}"
+    check_rows(outs[0], oq.packed_matmul(act, q, s, G, bits), f"codes bits={bits} vs exact dequant")
     assert torch.equal(outs[0], outs[1])
     assert int(ws[: 64 * 1024].count_nonzero()) == 0
 
