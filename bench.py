@@ -428,11 +428,23 @@ class DecodeWorkload:
         if self.tp > 1:
             import torch.distributed as tdist
             group = tdist.group.WORLD
+        self.packed, self.max_seq, self.group, self.fold, self.exchange = packed, max_seq, group, fold, exchange
         self.eng = E.DecodeEngine(spec, packed, embed, norm, None, cos, sin, batch, max_seq, device, self.rank,
                                   self.tp, group, fold_scales=fold, exchange=exchange, lm_head_quant=self.lm_quant)
         gp = torch.Generator().manual_seed(7)
         self.prompt = torch.randint(0, spec.vocab, (batch, self.P), generator=gp)
         torch.cuda.synchronize()
+
+    def side_engine(self, batch: int, layers: int | None = None, exchange: str | None = None):
+        """Another engine over the same packed layers (the first `layers` of
+        them), embedding, norm and head: a batch point or the shallow check."""
+        E = self.E
+        exchange = self.exchange if exchange is None else exchange
+        spec = self.spec if layers is None else E.LlamaSpec(**{**self.spec.__dict__, "n_layers": layers})
+        packed = self.packed if layers is None else self.packed[:layers]
+        return E.DecodeEngine(spec, packed, self.embed, self.norm, None, self.cos, self.sin, batch, self.max_seq,
+                              self.dev, self.rank, self.tp, self.group, fold_scales=self.fold,
+                              exchange=exchange, lm_head_quant=self.lm_quant)
 
     def layer_weights(self, li: int):
         """Layer li's unsharded weights, regenerated from its seed (the same
@@ -440,12 +452,13 @@ class DecodeWorkload:
         E = self.E
         return E.synthetic_layers(E.LlamaSpec(**{**self.spec.__dict__, "n_layers": 1}), self.dev, seed=1000 + li)[0]
 
-    def teacher_forced_logits(self, ids, steps: int):
+    def teacher_forced_logits(self, ids, steps: int, eng=None, prompt=None):
         """The engine's logits [steps, B, V/TP] (this rank's vocabulary shard)
         of decode steps 1..steps with the given generated ids forced: step j
         predicts ids[:, j]."""
-        torch, eng = self.torch, self.eng
-        eng.start(self.prompt, forced=ids)
+        torch = self.torch
+        eng = self.eng if eng is None else eng
+        eng.start(self.prompt if prompt is None else prompt, forced=ids)
         eng.prefill()
         eng.capture()
         out = []
@@ -530,11 +543,12 @@ class TorchDecodeReference:
     adds :320-335, and attention through torch's scaled_dot_product_attention
     on fp16 tensors, the "sdpa" implementation HF selects by default)."""
 
-    def __init__(self, wl: DecodeWorkload, split_k: int = 1):
+    def __init__(self, wl: DecodeWorkload, split_k: int = 1, layers: int | None = None):
         # split_k > 1: every fp32 matmul sums K in that many slices (another,
         # equally valid, accumulation order: the spread it causes is the noise
         # floor any implementation faces at this depth)
         self.wl, self.torch, self.split_k = wl, wl.torch, split_k
+        self.layers = wl.spec.n_layers if layers is None else layers   # the first `layers` layers only
 
     def _dequant(self, q, s, bits, G):
         torch = self.torch
@@ -586,7 +600,7 @@ class TorchDecodeReference:
         try:
             x = wl.embed[tokens.to(dev)].half()                               # [B, T, H]
             cos, sin = wl.cos[:T][:, None, :], wl.sin[:T][:, None, :]         # [T, 1, hd]
-            for li in range(sp.n_layers):
+            for li in range(self.layers):
                 L = wl.layer_weights(li)
                 for b in range(B):
                     xb = x[b]
@@ -658,6 +672,86 @@ def decode_parity(wl: DecodeWorkload, ids_host, rank: int, steps: int = 32) -> d
             "tolerance": "max-abs err <= 1e-2 * ||ref row||_2 / sqrt(V), per (step, sequence)",
             "reference": "teacher-forced torch on the device: the same packed weights dequantized exactly with fp32 "
                          "matmuls, the HF fp16 Llama layers with sdpa attention, full depth"}
+
+
+def shallow_parity(wl: DecodeWorkload, dist: "Dist", layers: int = 2, steps: int = 16) -> dict | None:
+    """The decode line's logits check where fp32 summation order cannot
+    dominate: an engine over the first `layers` layers of the same packed
+    model (same embedding and head), greedy tokens from its own run,
+    teacher-forced logits of `steps` steps against TorchDecodeReference over
+    the same layers."""
+    torch = wl.torch
+    eng = wl.side_engine(wl.B, layers=layers)
+    ids = eng.generate(wl.prompt, steps + 1).to(torch.int64)
+    got = wl.teacher_forced_logits(ids, steps, eng=eng)
+    eng.close()
+    del eng
+    if dist.rank != 0:
+        return None
+    toks = torch.cat([wl.prompt.to(torch.int64), ids], dim=1)
+    r = TorchDecodeReference(wl, layers=layers).logits(toks[:, :wl.P + steps], wl.P, steps).transpose(0, 1)
+    tol = 1e-2 * r.double().pow(2).sum(-1, keepdim=True).sqrt() / (r.shape[-1] ** 0.5)
+    vs = got.shape[-1]
+    ratio = float(((got.double() - r[..., :vs].double()).abs() / tol).max())
+    return {"layers": layers, "logits_steps_compared": steps, "logits_err_over_tol": round(ratio, 4)}
+
+
+def batch_sweep(wl: DecodeWorkload, dist: "Dist", batches, warmup: int, steps: int, peak_gbs: float,
+                parity_seqs: int = 4, parity_tokens: int = 16) -> list:
+    """The same model at other batch sizes (an engine per batch over the same
+    packed weights): tokens/s of the whole job (max over ranks), the step's
+    roofline fraction, and the greedy match of the first `parity_seqs`
+    sequences' first `parity_tokens` generated tokens against the
+    teacher-forced TorchDecodeReference."""
+    torch, dev = wl.torch, wl.dev
+    out = []
+    for B in batches:
+        # the peer exchange takes batches one launch stages whole; larger ones
+        # run in row blocks with NCCL all-reduces between the kernels
+        xchg = wl.exchange
+        if wl.tp > 1 and xchg == "peer" and B > wl.E.peer_batch_limit(wl.spec, wl.tp, wl.lm_bits):
+            xchg = "nccl"
+        eng = wl.side_engine(B, exchange=xchg)
+        prompt = torch.randint(0, wl.spec.vocab, (B, wl.P), generator=torch.Generator().manual_seed(100 + B))
+        eng.start(prompt)
+        eng.prefill()
+        eng.capture()
+        for _ in range(warmup):
+            eng.step(1)
+        torch.cuda.synchronize()
+        dist.barrier(dev)
+        torch.cuda.synchronize()
+        ctx0 = eng.host_pos + 1
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            eng.step(1)
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier(dev)
+        eng.check()
+        ms = dist.max(e0.elapsed_time(e1), dev)
+        n = min(parity_tokens, warmup + steps)
+        ids = eng.generated(n + 1).to("cpu", torch.int64)[:parity_seqs]
+        eng.close()
+        del eng
+        step_ms = ms / steps
+        bstep = (wl.spec.weight_bytes_per_token(lm_head_bits=wl.lm_bits) // wl.tp
+                 + B * wl.spec.kv_bytes_per_position() * (ctx0 + steps // 2) // wl.tp)
+        point = {"batch": B, "tokens_per_s": round(B * steps / (ms * 1e-3), 1), "ms_per_step": round(step_ms, 4),
+                 "decode_roofline_frac": round(bstep / (step_ms * 1e-3) / 1e9 / peak_gbs, 4)}
+        if wl.tp > 1:
+            point["all_reduce"] = "in-kernel peer exchange" if xchg == "peer" else "NCCL in the step graph"
+        if dist.rank == 0 and parity_seqs > 0:
+            toks = torch.cat([prompt[:parity_seqs].to(torch.int64), ids], dim=1)
+            lg = TorchDecodeReference(wl).logits(toks[:, :wl.P + n], wl.P - 1, n + 1)
+            ref_ids = lg.argmax(-1).cpu()
+            point["match_rate"] = round(float((ref_ids == ids).float().mean()), 4)
+            point["match_compared"] = f"first {n + 1} tokens of sequences 0..{parity_seqs - 1}"
+            del lg
+        out.append(point)
+        torch.cuda.empty_cache()
+    return out
 
 
 def decode_config(model: str, batch: int, prompt: int, new: int, world: int, fold: bool, exchange: str,
@@ -997,6 +1091,14 @@ def run_decode(args, dist: Dist):
     clocks = clk.summary()
     launches = args.steps * wl.eng.kernels_per_step()
     parity = None if args.no_parity else decode_parity(wl, e["ids"], dist.rank)
+    shallow = None if args.no_parity else shallow_parity(wl, dist)
+    if parity is not None:
+        parity["shallow"] = shallow
+    spec_b = args.batch_sweep if args.batch_sweep is not None else ("8,32,64" if args.model == "8b" and wl.B == 1
+                                                                    else "")
+    sweep_b = [int(b) for b in spec_b.split(",") if b]
+    bsweep = (batch_sweep(wl, dist, sweep_b, args.warmup, min(args.steps, 50), peak.peak_mem_bandwidth_gbs,
+                          parity_seqs=0 if args.no_parity else 4) if sweep_b else None)
     gemv = None
     if dist.world == 1 and not args.no_gemv:
         gw = GemvWorkload(dev, seed=1234)
@@ -1016,7 +1118,7 @@ def run_decode(args, dist: Dist):
             "config": decode_config(args.model, wl.B, wl.P, wl.T, dist.world, args.fold, args.exchange,
                                     args.lm_head_bits),
             "roofline": roofline, "decode_roofline": decode_roofline, "parity": parity, "gemv": gemv,
-            "cpu_baseline": cpu, "e2e": e2e,
+            "batch_sweep": bsweep, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(launches),
             "kernels": {k: {**{kk: v[kk] for kk in ("launches", "us", "GB/s")},
                             **({"gemv": wl.eng.kernel_choice[k]} if k in wl.eng.kernel_choice else {})}
@@ -1069,6 +1171,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the decode line's parity check (profiling runs)")
+    ap.add_argument("--batch-sweep", default=None,
+                    help="comma-separated batch sizes timed beside the line (default 8,32,64 for 8B batch 1; '' none)")
     ap.add_argument("--no-gemv", action="store_true", help="skip the decode line's GEMV figures (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--lm-head-bits", type=int, choices=[16, 8, 4], default=16,

@@ -281,6 +281,15 @@ def down_rows(spec: LlamaSpec, tp_size: int = 1) -> int:
     return max(1, _stage_rows(spec.inter // tp_size, spec.bits, False))
 
 
+def peer_batch_limit(spec: LlamaSpec, tp_size: int, lm_head_bits: int = 16) -> int:
+    """Largest decode batch the in-kernel peer exchange takes: every GEMV of
+    the step must stage the whole batch in one launch (larger batches run in
+    row blocks, with exchange='nccl' under tensor parallelism)."""
+    H, hd = spec.hidden, spec.head_dim
+    return min(32, _stage_rows(H, spec.bits, True), _stage_rows(spec.n_heads // tp_size * hd, spec.bits, False),
+               _stage_rows(spec.inter // tp_size, spec.bits, False), _stage_rows(H, lm_head_bits, True))
+
+
 def prefill_rows(spec: LlamaSpec, tp_size: int = 1, limit: int = 32) -> int:
     """Positions per prompt chunk: the most rows the q|k|v, o, gate|up and
     lm_head launches can stage, at most `limit`. With one rank the down_proj
@@ -416,7 +425,7 @@ class DecodeEngine:
         self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
         assert spec.n_heads % tp_size == 0 and spec.n_kv_heads % tp_size == 0, "heads must split evenly"
         assert spec.inter % (8 * tp_size) == 0 and spec.vocab % tp_size == 0
-        assert batch <= 32, "one launch stages at most 32 activation rows"
+        assert batch >= 1   # batches past what one GEMV launch stages run as row blocks
         self.nq, self.nkv = spec.n_heads // tp_size, spec.n_kv_heads // tp_size
         self.inter = spec.inter // tp_size
         self.vshard = spec.vocab // tp_size
@@ -537,42 +546,69 @@ class DecodeEngine:
                 return dict(epilogue=EPI_PEER_F32, xout=ex.out_ptr(e))
             return dict(epilogue=EPI_F32, out_f32=bufs.psum)
 
+        # bytes per row of every per-row pointer a decode GEMV takes (row m = sequence m)
+        row_bytes = dict(psum=4 * H, q_out=2 * self.nq * hd, k_cache=2 * self.nkv * self.S * hd,
+                         v_cache=2 * self.nkv * self.S * hd, argmax_keys=8, out_f32=4 * H)
+
+        def gemv_blocks(name, K, bits, kw):
+            """One decode GEMV as row blocks of at most what one launch can
+            stage (every block re-reads the weights); a single call when the
+            rows fit. The peer exchange addresses whole [M][K] blocks, so it
+            takes only batches that fit."""
+            fit = min(32, max(1, _stage_rows(K, bits, kw.get("prologue", PRO_NORM) != PRO_PLAIN)))
+            if prefill or rows <= fit:
+                a = self._gemv(rows, bits=bits, K=K, **kw)
+                calls.append(("gemv", a, name))
+                gemv_args.append(a)
+                return
+            if ex is not None:
+                raise ValueError(f"batch {rows} exceeds the {fit} rows one {name} launch stages; the peer "
+                                 "exchange takes whole batches: use exchange='nccl'")
+            ld = dict(act=kw.get("lda", 0), x_out=kw.get("lda", 0), out=kw.get("ldo", 0), residual=kw.get("ldo", 0))
+            for r0 in range(0, rows, fit):
+                d = dict(kw)
+                for k, v in kw.items():
+                    per = row_bytes.get(k, 2 * ld[k] if k in ld else None)
+                    if per is None or v is None:
+                        continue
+                    d[k] = (v.data_ptr() if isinstance(v, torch.Tensor) else v) + r0 * per
+                a = self._gemv(min(fit, rows - r0), bits=bits, K=K, **d)
+                calls.append(("gemv", a, name))
+                gemv_args.append(a)
+
         if prefill:
             calls.append(("prefill_embed", bufs, "embed"))
         for li, L in enumerate(self.layers):
             pro = norm_pro()
-            a = self._gemv(rows, bits=sp.bits, epilogue=EPI_ROPE_KV, N=(self.nq + 2 * self.nkv) * hd, K=H,
-                           group_size=sp.group_size, weight=L.qkv_w, scales=L.qkv_s, gamma=L.in_norm,
-                           head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv, max_seq=self.S,
-                           rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, q_out=bufs.q,
-                           k_cache=self.k_cache[li], v_cache=self.v_cache[li], prefill_seq=seq, **pro)
-            calls.append(("gemv", a, "qkv"))
-            gemv_args.append(a)
+            gemv_blocks("qkv", H, sp.bits, dict(
+                epilogue=EPI_ROPE_KV, N=(self.nq + 2 * self.nkv) * hd, group_size=sp.group_size, weight=L.qkv_w,
+                scales=L.qkv_s, gamma=L.in_norm, head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv,
+                max_seq=self.S, rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, q_out=bufs.q,
+                k_cache=self.k_cache[li], v_cache=self.v_cache[li], prefill_seq=seq, **pro))
             at = AttentionArgs(q=bufs.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
                                v_cache=self.v_cache[li].data_ptr(), out=bufs.attn.data_ptr(), pos=self.pos.data_ptr(),
                                batch=rows, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
                                pdl=self.pdl, prefill_seq=seq)
             calls.append(("attn", at, "attn"))
-            a = self._gemv(rows, bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.nq * hd, group_size=sp.group_size,
-                           weight=L.o_w, scales=L.o_s, act=bufs.attn, lda=self.nq * hd, ldo=H,
-                           **partial_epi(2 * li))
-            calls.append(("gemv", a, "o"))
-            gemv_args.append(a)
+            gemv_blocks("o", self.nq * hd, sp.bits, dict(
+                prologue=PRO_PLAIN, N=H, group_size=sp.group_size, weight=L.o_w, scales=L.o_s, act=bufs.attn,
+                lda=self.nq * hd, ldo=H, **partial_epi(2 * li)))
             if tp:
                 if ex is None:
                     calls.append(("allreduce", bufs.psum, "allreduce"))
                 pending = 2 * li
             pro = norm_pro()
-            a = self._gemv(rows, bits=sp.bits, epilogue=EPI_SWIGLU, N=2 * self.inter, K=H, group_size=sp.group_size,
-                           weight=L.gu_w, scales=L.gu_s, gamma=L.post_norm, out=bufs.act, ldo=self.inter, **pro)
-            calls.append(("gemv", a, "gu"))
-            gemv_args.append(a)
-            blk = rows if tp else min(rows, down_rows(sp, 1))
+            gemv_blocks("gu", H, sp.bits, dict(
+                epilogue=EPI_SWIGLU, N=2 * self.inter, group_size=sp.group_size, weight=L.gu_w, scales=L.gu_s,
+                gamma=L.post_norm, out=bufs.act, ldo=self.inter, **pro))
+            blk = rows if (tp and ex is not None) else min(rows, down_rows(sp, self.tp_size), 32)
             for r0 in range(0, rows, blk):   # row blocks when the chunk exceeds what the down_proj can stage
                 nr = min(blk, rows - r0)
                 epi = partial_epi(2 * li + 1)
                 if not tp:
                     epi.update(out=xs[cur].data_ptr() + 2 * r0 * H, residual=xs[cur].data_ptr() + 2 * r0 * H)
+                elif ex is None:
+                    epi.update(out_f32=bufs.psum.data_ptr() + 4 * r0 * H)
                 a = self._gemv(nr, bits=sp.bits, prologue=PRO_PLAIN, N=H, K=self.inter, group_size=sp.group_size,
                                weight=L.d_w, scales=L.d_s, act=bufs.act.data_ptr() + 2 * r0 * self.inter,
                                lda=self.inter, ldo=H, **epi)
@@ -590,11 +626,10 @@ class DecodeEngine:
         head = dict(epilogue=EPI_ARGMAX, argmax_keys=bufs.keys)
         if ex is not None:
             head.update(epilogue=EPI_PEER_ARGMAX, xout=ex.out_ptr(2 * len(self.layers)))
-        a = self._gemv(rows, bits=self.lm_bits, N=self.vshard, K=H, group_size=self.lm_group, weight=self.lm_head,
-                       scales=self.lm_scales, gamma=self.final_norm, out=bufs.logits, ldo=self.vshard,
-                       argmax_offset=self.tp_rank * self.vshard, **head, **pro)
-        calls.append(("gemv", a, "lm_head"))
-        gemv_args.append(a)
+        gemv_blocks("lm_head", H, self.lm_bits, dict(
+            N=self.vshard, group_size=self.lm_group, weight=self.lm_head, scales=self.lm_scales,
+            gamma=self.final_norm, out=bufs.logits, ldo=self.vshard, argmax_offset=self.tp_rank * self.vshard,
+            **head, **pro))
         if tp and ex is None:
             calls.append(("allreduce_max", bufs.keys, "allreduce"))
         calls.append(("prefill_sample" if prefill else "sample", bufs, "sample"))

@@ -122,11 +122,12 @@ def random_model(hidden, inter, layers, heads, kv, hd, vocab, bits, seed):
 
 @pytest.mark.parametrize("fold", [False, True])
 @pytest.mark.parametrize("bits,batch,hd,heads,kv", [(4, 1, 64, 8, 2), (8, 3, 64, 8, 2), (4, 4, 128, 8, 1),
-                                                    (8, 1, 128, 4, 4)])
+                                                    (8, 1, 128, 4, 4), (4, 40, 64, 8, 2)])
 def test_random_model_vs_oracle(bits, batch, hd, heads, kv, fold):
     """Free-running greedy decode; the oracle replays the engine's own tokens
     (teacher forcing), so every step's logits are compared on equal inputs.
-    Vocab 1000 (not a multiple of 16) exercises the ragged lm_head tile."""
+    Vocab 1000 (not a multiple of 16) exercises the ragged lm_head tile;
+    batch 40 runs every GEMV of the step as row blocks (32 + 8 sequences)."""
     w = random_model(512, 1536, 3, heads, kv, hd, 1000, bits, seed=bits * 10 + batch)
     P, T = 5, 7
     prompt = np.random.default_rng(batch).integers(0, 1000, (batch, P))
