@@ -294,21 +294,29 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       reinterpret_cast<uint8_t*>(act_s) +
       (((size_t)p.M * p.cp * 2 + (PRO == PRO_PLAIN ? 0 : (size_t)(p.K + 7) / 8 * 16) + 15) & ~(size_t)15));
 
-  if (tid == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(full0 + 8u * s, 1);
-      mbar_init(empty0 + 8u * s, kRingConsumerWarps);
+  // the weight map's descriptor is fetched while the barriers are set up
+  if (tid == kRingProducerWarp * 32)
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&rp.tm_w)) : "memory");
+  // barriers: one per lane of warp 0 (lane s < 16: ring slot s; 16 + h: partial-tile
+  // buffer h; 20 + j: scale buffer j), each lane fencing its own inits
+  static_assert(kRingMaxStages <= 16 && kRingCombBufs <= 4 && kRingScaleBufs <= 4, "one barrier pair per lane");
+  if (warp == 0) {
+    bool did = false;
+    if (lane < S) {
+      mbar_init(full0 + 8u * lane, 1);
+      mbar_init(empty0 + 8u * lane, kRingConsumerWarps);
+      did = true;
+    } else if (lane >= 16 && lane < 16 + kRingCombBufs) {
+      mbar_init(cfull0 + 8u * (lane - 16), kRingConsumerWarps);
+      mbar_init(cempty0 + 8u * (lane - 16), 1);
+      did = true;
+    } else if (lane >= 20 && lane < 20 + kRingScaleBufs) {
+      mbar_init(sfull0 + 8u * (lane - 20), 1);
+      mbar_init(sempty0 + 8u * (lane - 20), kRingConsumerWarps);
+      did = true;
     }
-    for (int h = 0; h < kRingCombBufs; ++h) {
-      mbar_init(cfull0 + 8u * h, kRingConsumerWarps);
-      mbar_init(cempty0 + 8u * h, 1);
-    }
-    for (int j = 0; j < kRingScaleBufs; ++j) {
-      mbar_init(sfull0 + 8u * j, 1);
-      mbar_init(sempty0 + 8u * j, kRingConsumerWarps);
-    }
-    abort_s = 0;
-    fence_mbar_init();
+    if (lane == 31) abort_s = 0;
+    if (did) fence_mbar_init();
   }
   __syncthreads();
 
