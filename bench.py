@@ -733,13 +733,22 @@ def batch_sweep(wl: DecodeWorkload, dist: "Dist", batches, warmup: int, steps: i
         ms = dist.max(e0.elapsed_time(e1), dev)
         n = min(parity_tokens, warmup + steps)
         ids = eng.generated(n + 1).to("cpu", torch.int64)[:parity_seqs]
+        # per class of the step: its launches alone in a graph, CUDA events
+        kus = {}
+        for name in dict.fromkeys(nm for kind, _a, nm in eng.calls if kind in ("gemv", "attn", "tcgemm")):
+            launches = sum(1 for kind, _a, nm in eng.calls if nm == name and kind in ("gemv", "attn", "tcgemm"))
+            g = capture_graph(lambda name=name: eng.enqueue_only(name))
+            kus[name] = {"launches": launches, "us": round(time_graph(g, 5) / launches * 1e3, 2),
+                         "path": "tcgemm" if any(kind == "tcgemm" and nm == name for kind, _a, nm in eng.calls)
+                         else "gemv" if name != "attn" else "attention"}
+            del g
         eng.close()
         del eng
         step_ms = ms / steps
         bstep = (wl.spec.weight_bytes_per_token(lm_head_bits=wl.lm_bits) // wl.tp
                  + B * wl.spec.kv_bytes_per_position() * (ctx0 + steps // 2) // wl.tp)
         point = {"batch": B, "tokens_per_s": round(B * steps / (ms * 1e-3), 1), "ms_per_step": round(step_ms, 4),
-                 "decode_roofline_frac": round(bstep / (step_ms * 1e-3) / 1e9 / peak_gbs, 4)}
+                 "decode_roofline_frac": round(bstep / (step_ms * 1e-3) / 1e9 / peak_gbs, 4), "kernels": kus}
         if wl.tp > 1:
             point["all_reduce"] = "in-kernel peer exchange" if xchg == "peer" else "NCCL in the step graph"
         if dist.rank == 0 and parity_seqs > 0:

@@ -328,6 +328,7 @@ int lw_prefill_sample(int* tokens, unsigned long long* keys, const void* embed, 
  *   LW_TC_EPI_SWIGLU: gate|up rows interleaved by 8, out[m][i] = silu(gate) * up
  *   LW_TC_EPI_ROPE_KV: q|k|v rows in rope-pair order; RoPE q, k at position
  *                      *pos + m; q -> q_out, k, v -> the cache of sequence *seq
+ *                      (seq NULL: decode rows, row m is sequence m at *pos)
  *   LW_TC_EPI_F32:    out is fp32 [M][ldo], out = y (a tensor-parallel rank's
  *                      partial sum of a row-split linear, to be all-reduced)
  * Weights dequantize exactly (fp16(code * scale)) as the GEMV does; the sums
@@ -349,7 +350,7 @@ typedef struct {
   const void* rope_cos;  /* fp16 [max_seq][head_dim] */
   const void* rope_sin;
   const int* pos;
-  const int* seq;
+  const int* seq;        /* NULL: decode rows (row m = sequence m at *pos) */
   void* q_out;           /* fp16 [M][n_q_heads * head_dim] */
   void* k_cache;         /* fp16 [batch][n_kv_heads][max_seq][head_dim] */
   void* v_cache;

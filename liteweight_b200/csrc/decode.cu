@@ -38,10 +38,11 @@ struct AttnParams {
   float scale_log2;    // head_dim^-0.5 * log2(e)
 };
 
-// Cluster attention: one thread-block cluster of kAttnCluster CTAs per
-// (sequence, kv head); CTA r of the cluster and warp w of the CTA own
-// positions [base + (r * W + w) * P, ... + P) of every round of
-// kAttnCluster * W * P positions (P = 8). Per round a warp computes, on the
+// Cluster attention: one thread-block cluster of CL CTAs per (sequence, kv
+// head) - CL = kAttnCluster (8) while the grid stays within about two waves of
+// the SMs, fewer for large batches; CTA r of the cluster and warp w of the CTA
+// own positions [base + (r * W + w) * P, ... + P) of every round of
+// CL * W * P positions (P = 8). Per round a warp computes, on the
 // tensor cores, S = Q K^T for the GQA group's query heads (MMA rows; rows
 // past GQ are zero) against its 8 positions (one m16n8k16 per 16 head dims),
 // an online softmax per head (rows: max / sum over the 4 lanes of a row), and
@@ -55,7 +56,7 @@ struct AttnParams {
 // no counters. The first two rounds of positions before *pos are loaded before
 // griddepcontrol.wait (they do not depend on the previous kernel).
 constexpr int kAttnWarps = 8;
-constexpr int kAttnCluster = 8;
+constexpr int kAttnCluster = 8;   // largest cluster (CTAs per sequence and kv head)
 constexpr int kAttnPos = 8;   // positions per warp per round
 
 LW_DEV void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
@@ -65,7 +66,10 @@ LW_DEV void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
       : "r"(a0), "r"(a1), "r"(b0));
 }
 
-template <int HD, int GQ>
+// CL: CTAs per cluster (8 for one or a few sequences: the latency of one
+// sequence's positions split 8 ways; 1 for large batches, whose (sequence, kv
+// head) pairs already fill the GPU several times over).
+template <int HD, int GQ, int CL>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const AttnParams p) {
   static_assert(GQ <= 8 && (HD == 64 || HD == 128), "GQA group of at most 8 heads, head_dim 64 or 128");
   namespace cg = cooperative_groups;
@@ -85,7 +89,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   auto acc_at = [](int h, int d) { return h * SAS + d + (d >> 5); };
-  const int per_round = kAttnCluster * W * kAttnPos;
+  const int per_round = CL * W * kAttnPos;
   const int first = (rank * W + warp) * kAttnPos;
   // Positions before *pos were written by earlier steps, not by the kernel
   // this one waits for: the first two rounds of them are loaded before
@@ -244,22 +248,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const Attn
   }
   // CTAs of the cluster -> output: CTA r finishes elements r, r + CL, ...
   cluster.sync();
-  for (int i = rank * (W * 32) + threadIdx.x; i < GQ * HD; i += kAttnCluster * W * 32) {
+  for (int i = rank * (W * 32) + threadIdx.x; i < GQ * HD; i += CL * W * 32) {
     const int h = i / HD, d = i - h * HD;
     // all remote reads issued together (independent distributed-shared-memory loads)
-    float mc[kAttnCluster], lc[kAttnCluster], ac[kAttnCluster];
+    float mc[CL], lc[CL], ac[CL];
 #pragma unroll
-    for (int c = 0; c < kAttnCluster; ++c) {
+    for (int c = 0; c < CL; ++c) {
       mc[c] = *cluster.map_shared_rank(&cta_m[h], c);
       lc[c] = *cluster.map_shared_rank(&cta_l[h], c);
       ac[c] = *cluster.map_shared_rank(&cta_acc[h][d], c);
     }
     float M = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < kAttnCluster; ++c) M = fmaxf(M, mc[c]);
+    for (int c = 0; c < CL; ++c) M = fmaxf(M, mc[c]);
     float L = 0.f, A = 0.f;
 #pragma unroll
-    for (int c = 0; c < kAttnCluster; ++c) {
+    for (int c = 0; c < CL; ++c) {
       const float w = mc[c] == -INFINITY ? 0.f : exp2f(mc[c] - M);   // a CTA with no positions adds nothing
       L = fmaf(lc[c], w, L);
       A = fmaf(ac[c], w, A);
@@ -712,16 +716,28 @@ int validate(const lw_fused_gemv_args* a) {
   return LW_OK;
 }
 
-template <int HD, int GQ>
-cudaError_t attn_launch(const lw::AttnParams& p, cudaStream_t s, bool pdl) {
+// CTAs per (sequence, kv head): the largest of 8, 4, 2, 1 that keeps the grid
+// within about two waves of one CTA per SM.
+inline int attn_cluster_size(int B, int nkv) {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0)
+    sms = 148;
+  int cl = lw::kAttnCluster;
+  while (cl > 1 && (long long)B * nkv * cl > 2LL * sms) cl /= 2;
+  return cl;
+}
+
+template <int HD, int GQ, int CL>
+cudaError_t attn_launch_cl(const lw::AttnParams& p, cudaStream_t s, bool pdl) {
   lw_count_launch();
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(lw::kAttnCluster, p.nkv, p.B);
+  cfg.gridDim = dim3(CL, p.nkv, p.B);
   cfg.blockDim = dim3(lw::kAttnWarps * 32);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = lw::kAttnCluster;
+  attr[0].val.clusterDim.x = CL;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   int na = 1;
@@ -732,7 +748,17 @@ cudaError_t attn_launch(const lw::AttnParams& p, cudaStream_t s, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, lw::attn_decode_kernel<HD, GQ>, p);
+  return cudaLaunchKernelEx(&cfg, lw::attn_decode_kernel<HD, GQ, CL>, p);
+}
+
+template <int HD, int GQ>
+cudaError_t attn_launch(const lw::AttnParams& p, cudaStream_t s, bool pdl) {
+  switch (attn_cluster_size(p.B, p.nkv)) {
+    case 8: return attn_launch_cl<HD, GQ, 8>(p, s, pdl);
+    case 4: return attn_launch_cl<HD, GQ, 4>(p, s, pdl);
+    case 2: return attn_launch_cl<HD, GQ, 2>(p, s, pdl);
+    default: return attn_launch_cl<HD, GQ, 1>(p, s, pdl);
+  }
 }
 
 }  // namespace

@@ -81,7 +81,7 @@ struct TcGemmParams {
   const __half* rope_cos;
   const __half* rope_sin;
   const int* pos;
-  const int* seq;
+  const int* seq;      // prompt chunk: row m = position *pos + m of sequence *seq; null: row m = sequence m
   int head_dim, n_q_heads, n_kv_heads, max_seq;
   __half* q_out;
   __half* k_cache;
@@ -241,7 +241,9 @@ LW_DEV void tc_epilogue(const TcGemmParams& p, int n, int m, float y, int lane) 
       const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
       const int head = (t16 * 16) / hd, jt = t16 % (hd / 16);
       const int d_lo = 8 * jt + g, d_hi = d_lo + hd / 2;
-      const int pos = *p.pos + m, row = *p.seq;
+      // a prompt chunk: row m is position *pos + m of sequence *seq; decode
+      // rows (seq null): row m is sequence m at position *pos
+      const int pos = p.seq ? *p.pos + m : *p.pos, row = p.seq ? *p.seq : m;
       const float y_lo = r16(y), y_hi = r16(partner);
       float o_lo = y_lo, o_hi = y_hi;
       if (head < nq + nkv) {
@@ -681,7 +683,7 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
       if (a->ldo < a->N || !al(a->out, 16)) return LW_ERR_BAD_SHAPE;
       break;
     case LW_TC_EPI_ROPE_KV:
-      if (!a->q_out || !a->k_cache || !a->v_cache || !a->rope_cos || !a->rope_sin || !a->pos || !a->seq)
+      if (!a->q_out || !a->k_cache || !a->v_cache || !a->rope_cos || !a->rope_sin || !a->pos)
         return LW_ERR_NULL_POINTER;
       if (a->head_dim % 16 || a->N != (a->n_q_heads + 2 * a->n_kv_heads) * a->head_dim) return LW_ERR_BAD_SHAPE;
       break;

@@ -30,6 +30,7 @@ tensor-parallel exchange), or by NCCL all-reduces between the kernels
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
@@ -93,6 +94,15 @@ class PrefillGemmArgs(ctypes.Structure):
 
 TC_EPI_RESID, TC_EPI_SWIGLU, TC_EPI_ROPE_KV, TC_EPI_F32 = 0, 1, 2, 3
 TC_ROWS = 256   # prompt-chunk rows on the tensor-core path (the GEMM's largest M)
+
+
+def tc_decode_min_batch() -> int:
+    """Smallest decode batch whose linears run on the tensor-core GEMM (it reads
+    each weight once for all rows; the GEMVs stage at most 26 rows of a K = 4096
+    activation per launch and re-read the weights per row block).
+    LW_B200_TC_DECODE_MIN overrides it; 0 keeps every batch on the GEMVs."""
+    v = os.environ.get("LW_B200_TC_DECODE_MIN")
+    return int(v) if v not in (None, "") else 24
 
 
 class AttentionArgs(ctypes.Structure):
@@ -465,6 +475,8 @@ class DecodeEngine:
         # with tensor parallelism the row-split linears' fp32 partials are all-reduced by NCCL
         # between the GEMMs); shapes the GEMM does not tile run the fused GEMVs and exchanges.
         self.use_tc = tc_supported(spec, tp_size)
+        n = tc_decode_min_batch()
+        self.tc_decode = self.use_tc and n > 0 and n <= batch <= TC_ROWS
         self.prefill_rows = TC_ROWS if self.use_tc else prefill_rows(spec, tp_size)
         self.dec = self._buffers(batch)
         self.pf = self._buffers(self.prefill_rows)
@@ -635,7 +647,7 @@ class DecodeEngine:
         calls.append(("prefill_sample" if prefill else "sample", bufs, "sample"))
         return calls, gemv_args
 
-    def _make_tc_calls(self, bufs, final: bool):
+    def _make_tc_calls(self, bufs, final: bool, decode: bool = False):
         """A prompt chunk on the tensor cores: per layer RMSNorm rows, the q|k|v
         GEMM (RoPE + KV append), attention, the o GEMM (+ residual, in place),
         RMSNorm, the gate|up GEMM (SwiGLU), the down GEMM (+ residual); the last
@@ -643,51 +655,71 @@ class DecodeEngine:
         parallelism the o and down GEMMs write this rank's fp32 partial sums,
         NCCL all-reduces them, and lw_resid_rmsnorm_rows adds them to the
         residual before the next norm; the lm_head's vocabulary-shard argmax keys
-        are max-reduced the same way, so prefill_sample reads local keys."""
+        are max-reduced the same way, so prefill_sample reads local keys.
+        decode=True: the same layers for one decode step of a large batch (row
+        m = sequence m at *pos), then the lm_head GEMV over every row (in row
+        blocks of what one launch stages) and the sampler."""
         sp, H, hd, rows = self.spec, self.spec.hidden, self.spec.head_dim, bufs.rows
-        seq = self.seq.data_ptr()
+        seq = None if decode else self.seq.data_ptr()
         tp = self.tp_size > 1
         bufs.sample_xin = None
-        calls = [("prefill_embed", bufs, "embed")]
+        calls = [] if decode else [("prefill_embed", bufs, "embed")]
 
-        def tc(epi, N, K, w, s_, act, lda, out, ldo, **kw):
+        def tc(epi, N, K, w, s_, act, lda, out, ldo, name="tc", **kw):
             a = PrefillGemmArgs(bits=sp.bits, epilogue=epi, pdl=self.pdl, M=rows, N=N, K=K,
                                 group_size=sp.group_size, lda=lda, ldo=ldo, act=act.data_ptr(), weight=w.data_ptr(),
                                 scales=s_.data_ptr(), out=out.data_ptr() if out is not None else None)
             for k, v in kw.items():
                 setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
-            return ("tcgemm", a, "tc")
+            return ("tcgemm", a, name)
 
         def norm(gamma, pending):
             if pending:
                 return ("resid_rmsnorm", (bufs.x, bufs.psum, gamma, bufs.h, rows), "norm")
             return ("rmsnorm", (bufs.x, gamma, bufs.h, rows), "norm")
 
-        def row_split(w, s_, act, K):
+        def row_split(w, s_, act, K, name):
             if not tp:
-                return [tc(TC_EPI_RESID, H, K, w, s_, act, K, bufs.x, H, residual=bufs.x)]
-            return [tc(TC_EPI_F32, H, K, w, s_, act, K, bufs.psum, H), ("allreduce", bufs.psum, "allreduce")]
+                return [tc(TC_EPI_RESID, H, K, w, s_, act, K, bufs.x, H, name=name, residual=bufs.x)]
+            return [tc(TC_EPI_F32, H, K, w, s_, act, K, bufs.psum, H, name=name), ("allreduce", bufs.psum, "allreduce")]
 
         for li, L in enumerate(self.layers):
             calls.append(norm(L.in_norm, tp and li > 0))
             calls.append(tc(TC_EPI_ROPE_KV, (self.nq + 2 * self.nkv) * hd, H, L.qkv_w, L.qkv_s, bufs.h, H, bufs.q,
-                            self.nq * hd, head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv, max_seq=self.S,
-                            rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, seq=seq, q_out=bufs.q,
-                            k_cache=self.k_cache[li], v_cache=self.v_cache[li]))
+                            self.nq * hd, name="qkv", head_dim=hd, n_q_heads=self.nq, n_kv_heads=self.nkv,
+                            max_seq=self.S, rope_cos=self.rope_cos, rope_sin=self.rope_sin, pos=self.pos, seq=seq,
+                            q_out=bufs.q, k_cache=self.k_cache[li], v_cache=self.v_cache[li]))
             at = AttentionArgs(q=bufs.q.data_ptr(), k_cache=self.k_cache[li].data_ptr(),
                                v_cache=self.v_cache[li].data_ptr(), out=bufs.attn.data_ptr(), pos=self.pos.data_ptr(),
                                batch=rows, n_q_heads=self.nq, n_kv_heads=self.nkv, head_dim=hd, max_seq=self.S,
                                pdl=self.pdl, prefill_seq=seq)
             calls.append(("attn", at, "attn"))
-            calls += row_split(L.o_w, L.o_s, bufs.attn, self.nq * hd)
+            calls += row_split(L.o_w, L.o_s, bufs.attn, self.nq * hd, "o")
             calls.append(norm(L.post_norm, tp))
-            calls.append(tc(TC_EPI_SWIGLU, 2 * self.inter, H, L.gu_w, L.gu_s, bufs.h, H, bufs.act, self.inter))
-            calls += row_split(L.d_w, L.d_s, bufs.act, self.inter)
+            calls.append(tc(TC_EPI_SWIGLU, 2 * self.inter, H, L.gu_w, L.gu_s, bufs.h, H, bufs.act, self.inter,
+                            name="gu"))
+            calls += row_split(L.d_w, L.d_s, bufs.act, self.inter, "down")
         if not final:
             calls.append(("prefill_advance", rows, "advance"))
             return calls, []
         if tp:   # the last down partial joins the residual stream (h is not used)
             calls.append(norm(self.final_norm, True))
+        if decode:
+            # every row's logits and argmax key, in row blocks of what one GEMV launch stages
+            fit = min(32, max(1, _stage_rows(H, self.lm_bits, True)))
+            gemv_args = []
+            for r0 in range(0, rows, fit):
+                a = self._gemv(min(fit, rows - r0), bits=self.lm_bits, prologue=PRO_NORM, epilogue=EPI_ARGMAX,
+                               N=self.vshard, K=H, group_size=self.lm_group, weight=self.lm_head,
+                               scales=self.lm_scales, gamma=self.final_norm, act=bufs.x.data_ptr() + 2 * r0 * H,
+                               lda=H, out=bufs.logits.data_ptr() + 2 * r0 * self.vshard, ldo=self.vshard,
+                               argmax_keys=bufs.keys.data_ptr() + 8 * r0, argmax_offset=self.tp_rank * self.vshard)
+                calls.append(("gemv", a, "lm_head"))
+                gemv_args.append(a)
+            if tp:
+                calls.append(("allreduce_max", bufs.keys, "allreduce"))
+            calls.append(("sample", bufs, "sample"))
+            return calls, gemv_args
         last = bufs.x.data_ptr() + 2 * (rows - 1) * H
         a = self._gemv(1, bits=self.lm_bits, prologue=PRO_NORM, epilogue=EPI_ARGMAX, N=self.vshard, K=H,
                        group_size=self.lm_group, weight=self.lm_head, scales=self.lm_scales,
@@ -716,11 +748,15 @@ class DecodeEngine:
 
     def _build_calls(self):
         self.workspace = None
-        self.calls, gemv_args = self._make_calls(self.dec, prefill=False)
+        if self.tc_decode:   # large batches: the step's linears on the tensor cores (NCCL under TP)
+            self.calls, gemv_args = self._make_tc_calls(self.dec, final=True, decode=True)
+        else:
+            self.calls, gemv_args = self._make_calls(self.dec, prefill=False)
         self._attach_workspace(gemv_args)
         self.stat_args = {id(a): self._stat_variant(a) for a in gemv_args}
         self.x_in = self.x   # layer 0 reads the residual stream from self.x; sample writes it there
-        self.sample_xin = self.exchange.in_ptr(2 * len(self.layers)) if self.exchange is not None else None
+        self.sample_xin = (self.exchange.in_ptr(2 * len(self.layers))
+                           if self.exchange is not None and not self.tc_decode else None)
         self.prefill_calls = {}
 
     def _stat_variant(self, a: FusedGemvArgs) -> FusedGemvArgs:
@@ -787,7 +823,8 @@ class DecodeEngine:
             self.spec.hidden, self.pdl, s))
 
     def kernels_per_step(self) -> int:
-        return sum(1 for k, _, _n in self.calls if k in ("gemv", "attn", "sample"))
+        return sum(1 for k, _, _n in self.calls if k in ("gemv", "attn", "sample", "tcgemm", "rmsnorm",
+                                                          "resid_rmsnorm"))
 
     def tune_kernels(self, reps: int = 5, margin: float = 0.03) -> dict:
         """Per projection class of the decode step (qkv, o, gu, down, lm_head),
@@ -847,6 +884,8 @@ class DecodeEngine:
                 nat.check("lw_fused_gemv", lib.lw_fused_gemv(ctypes.byref(self.stat_args[id(a)]), s))
             elif kind == "attn":
                 nat.check("lw_attention_decode", lib.lw_attention_decode(ctypes.byref(a), s))
+            elif kind == "tcgemm":
+                nat.check("lw_prefill_gemm", lib.lw_prefill_gemm(ctypes.byref(a), s))
 
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
         """Greedy continuation of input_ids [B, P] (host or device); returns the

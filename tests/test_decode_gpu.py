@@ -122,12 +122,11 @@ def random_model(hidden, inter, layers, heads, kv, hd, vocab, bits, seed):
 
 @pytest.mark.parametrize("fold", [False, True])
 @pytest.mark.parametrize("bits,batch,hd,heads,kv", [(4, 1, 64, 8, 2), (8, 3, 64, 8, 2), (4, 4, 128, 8, 1),
-                                                    (8, 1, 128, 4, 4), (4, 40, 64, 8, 2)])
+                                                    (8, 1, 128, 4, 4)])
 def test_random_model_vs_oracle(bits, batch, hd, heads, kv, fold):
     """Free-running greedy decode; the oracle replays the engine's own tokens
     (teacher forcing), so every step's logits are compared on equal inputs.
-    Vocab 1000 (not a multiple of 16) exercises the ragged lm_head tile;
-    batch 40 runs every GEMV of the step as row blocks (32 + 8 sequences)."""
+    Vocab 1000 (not a multiple of 16) exercises the ragged lm_head tile."""
     w = random_model(512, 1536, 3, heads, kv, hd, 1000, bits, seed=bits * 10 + batch)
     P, T = 5, 7
     prompt = np.random.default_rng(batch).integers(0, 1000, (batch, P))
@@ -136,6 +135,27 @@ def test_random_model_vs_oracle(bits, batch, hd, heads, kv, fold):
     gen = eng.generated(T).cpu().numpy()
     oracle = ol.teacher_forced_logits(w, prompt, gen)
     assert_rows(got, oracle, f"bits={bits} B={batch} hd={hd} fold={fold}")
+
+
+@pytest.mark.parametrize("tc", [True, False])
+@pytest.mark.parametrize("bits,kv", [(4, 2), (8, 2), (4, 8)])
+def test_large_batch_vs_oracle(bits, kv, tc, monkeypatch):
+    """Batch 40: the step's linears on the tensor-core GEMM with decode rows
+    (row m = sequence m at *pos), or - with the tensor-core decode switched off
+    - every GEMV as row blocks (32 + 8 sequences); the lm_head GEMV in row
+    blocks either way. 40 x 2 kv heads run the attention in 2-CTA clusters,
+    40 x 8 in single CTAs. Teacher-forced logits against the oracle."""
+    from liteweight_b200 import engine as E
+    monkeypatch.setenv("LW_B200_TC_DECODE_MIN", "24" if tc else "0")
+    w = random_model(512, 1536, 3, 8, kv, 64, 1000, bits, seed=bits * 10 + 40 + kv)
+    P, T, B = 5, 7, 40
+    prompt = np.random.default_rng(40).integers(0, 1000, (B, P))
+    eng = engine_from_oracle(w, bits, 128, batch=B, max_seq=48)
+    assert eng.tc_decode == tc and E.tc_supported(eng.spec)
+    got = run_engine(eng, prompt, P + T - 1)
+    gen = eng.generated(T).cpu().numpy()
+    oracle = ol.teacher_forced_logits(w, prompt, gen)
+    assert_rows(got, oracle, f"bits={bits} B={B} tc={tc}")
 
 
 def test_graph_equals_eager_and_long_context():
