@@ -68,7 +68,9 @@ def env_int(name: str, default: int) -> int:
 # ----------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running.
+    Entering waits (up to 3 s) for the first sample, so a short timed region
+    still has samples from its start; leaving waits one interval more."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -83,15 +85,24 @@ class ClockSampler:
         try:
             import tempfile
             self.out = tempfile.NamedTemporaryFile("w", suffix=".csv", delete=False)
+            import shutil
+            line_buffered = ["stdbuf", "-oL"] if shutil.which("stdbuf") else []   # a line per sample, as taken
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+                line_buffered + ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < 3.0 and self.proc.poll() is None:
+                if os.path.getsize(self.out.name) > 0:
+                    break
+                time.sleep(0.01)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.06)   # one more sample after the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
