@@ -295,7 +295,9 @@ cudaError_t matmul_dispatch(const void* act, const void* w, const void* scales, 
       p.N = N;
       p.K = K;
       p.G = G;
-      return lw::launch_ring<BITS, lw::PRO_PLAIN, lw::EPI_PLAIN>(p, rpl, s, false);
+      // programmatic dependent launch with every global read after the wait:
+      // the launch and barrier setup overlap whatever kernel came before
+      return lw::launch_ring<BITS, lw::PRO_PLAIN, lw::EPI_PLAIN>(p, rpl, s, true, true);
     }
     GemvParams p = {};
     p.act = static_cast<const __half*>(act);
@@ -325,7 +327,9 @@ cudaError_t matmul_dispatch(const void* act, const void* w, const void* scales, 
     p.N = N;
     p.K = K;
     p.G = G;
-    cudaError_t e = lw::launch_stream_block<BITS, lw::PRO_PLAIN, lw::EPI_PLAIN>(p, ws, ws_bytes, s, false);
+    // the ring kernel (M <= 8) launches with PDL, reading everything after the wait
+    cudaError_t e = lw::launch_stream_block<BITS, lw::PRO_PLAIN, lw::EPI_PLAIN>(p, ws, ws_bytes, s, false, false,
+                                                                                true, true);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

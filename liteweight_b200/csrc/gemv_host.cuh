@@ -220,7 +220,7 @@ bool plan_ring(int M, int N, int K, int G, const void* w, const void* scales, Ri
 }
 
 template <int BITS, int PRO, int EPI, bool FOLD = false>
-cudaError_t launch_ring(StreamParams p, const RingPlan& pl, cudaStream_t s, bool pdl) {
+cudaError_t launch_ring(StreamParams p, const RingPlan& pl, cudaStream_t s, bool pdl, bool weights_after_wait = false) {
   RingParams rp;
   memset(&rp, 0, sizeof(rp));
   const size_t rowbytes = (size_t)p.K * BITS / 8;
@@ -240,6 +240,7 @@ cudaError_t launch_ring(StreamParams p, const RingPlan& pl, cudaStream_t s, bool
   rp.boxes_last = pl.boxes_last;
   rp.units = pl.units;
   rp.stages = pl.stages;
+  rp.weights_after_wait = weights_after_wait;
   auto kern = gemv_ring_kernel<BITS, PRO, EPI, FOLD>;
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
@@ -278,15 +279,16 @@ cudaError_t launch_tma(StreamParams p, const StreamPlan& pl, void* ws, cudaStrea
 // large enough workspace the plan keeps tiles whole.
 template <int BITS, int PRO, int EPI>
 cudaError_t launch_stream_block(StreamParams p, void* ws, size_t ws_bytes, cudaStream_t s, bool pdl,
-                                bool allow_fold = false, bool allow_ring = true) {
+                                bool allow_fold = false, bool allow_ring = true, bool ring_safe_pdl = false) {
   if (allow_ring) {
     const bool fold = allow_fold && fold_scales<BITS>(p.K, p.G);
     RingPlan rpl;
     if (plan_ring<BITS, PRO>(p.M, p.N, p.K, p.G, p.w, p.scales, &rpl, fold)) {
       if constexpr (BITS < 16) {
-        if (fold) return launch_ring<BITS, PRO, EPI, true>(p, rpl, s, pdl);
+        if (fold) return launch_ring<BITS, PRO, EPI, true>(p, rpl, s, pdl || ring_safe_pdl, ring_safe_pdl);
       }
-      return launch_ring<BITS, PRO, EPI>(p, rpl, s, pdl);
+      // ring_safe_pdl: programmatic dependent launch with every global read after the wait
+      return launch_ring<BITS, PRO, EPI>(p, rpl, s, pdl || ring_safe_pdl, ring_safe_pdl);
     }
   }
   StreamPlan pl;

@@ -23,7 +23,9 @@
 //              ring slot, writing the stage's unit id into the slot's header.
 //              It starts before griddepcontrol.wait: weights do not depend on
 //              the previous kernel, so up to `stages` x 16 KB per SM stream in
-//              while that kernel finishes.
+//              while that kernel finishes (unless weights_after_wait: the
+//              drop-in ops, whose weights a previous kernel may have written,
+//              only overlap the launch and the barrier setup).
 //   warps 0-15 warp w owns chunk w (64 bytes of each row) of every stage: per
 //              stage each lane reads 16 bytes of two rows, unpacks and scales
 //              them, and feeds mma.sync m16n8k16 with the staged activation
@@ -85,6 +87,8 @@ struct RingParams {
   int units;               // ceil(N / 16)
   int stages;              // ring slots
   int map3d;               // 1: tm_w is the 3-D view {128 bytes, rows, row bytes / 128}, one box per stage
+  int weights_after_wait;  // 1: weights and scales are read after griddepcontrol.wait too (they may be
+                           // the previous kernel's output: the drop-in ops launched with PDL)
 };
 
 LW_DEV void tma_load_box(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -346,6 +350,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) gemv_ring_kernel(const __grid
       abort_s = 1;
       return false;
     };
+    if (rp.weights_after_wait) pdl_wait();
     // units b, b + grid, b + 2 grid, ...
     int u = (int)blockIdx.x;
     int slot = 0, nunit = 0;
