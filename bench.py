@@ -313,19 +313,24 @@ class GemvWorkload:
             d["shapes"][f"{K}x{N}"] = {"us": round(ms * 1e3, 3), "GB/s": round(b / (ms * 1e-3) / 1e9, 1)}
         return fam
 
-    def extra_stats(self, peak_gbs: float) -> dict:
+    def extra_stats(self, peak_gbs: float, peak_tflops: float | None = None) -> dict:
         """The single W8A16 QuantLinear with per-output-channel scales (K=2048,
-        N=8192; M = 1 and 16) and the 8B gate|up shape (INT4, K=4096, N=28672, M=1)."""
+        N=8192; M = 1 and 16) and the 8B gate|up shape (INT4, K=4096, N=28672;
+        M = 1, and M = 256 - the tcgen05 route of the drop-in op - in TFLOP/s
+        against the measured bf16 burst peak)."""
         out = {}
         for i in range(self.n_step, len(self.items)):
             bits, K, N, G = self.items[i]
             name = (f"config1_w8a16_perchannel_K{K}_N{N}" if (bits, K, N, G) == CONFIG1
                     else f"w4a16_gate_up_8b_K{K}_N{N}_G{G}")
-            for M in ((1, 16) if (bits, K, N, G) == CONFIG1 else (1,)):
+            for M in ((1, 16) if (bits, K, N, G) == CONFIG1 else (1, 256)):
                 ms = self.time_item(i, M)
                 gbs = gemv_bytes(M, K, N, bits, G) / (ms * 1e-3) / 1e9
-                out.setdefault(name, {})[f"M{M}"] = {"us": round(ms * 1e3, 3), "GB/s": round(gbs, 1),
-                                                     "frac": round(gbs / peak_gbs, 4)}
+                point = {"us": round(ms * 1e3, 3), "GB/s": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)}
+                if M > 32 and peak_tflops:
+                    tf = 2 * M * N * K / (ms * 1e-3) / 1e12
+                    point.update({"TFLOP/s": round(tf, 1), "tensor_frac": round(tf / peak_tflops, 4)})
+                out.setdefault(name, {})[f"M{M}"] = point
         return out
 
     def e2e(self, steps: int) -> dict:
@@ -373,14 +378,14 @@ class GemvWorkload:
                 out[f"w{bits}_M{M}"] = round(tot_b / (ms * 1e-3) / 1e9, 1)
         return out
 
-    def summary(self, peak_gbs: float, sweep: bool = True) -> dict:
+    def summary(self, peak_gbs: float, sweep: bool = True, peak_tflops: float | None = None) -> dict:
         """The GEMV half of the headline metric, for the default line."""
         fam = self.kernel_stats()
         m1 = {}
         for k, v in fam.items():
             gbs = v["bytes"] / (v["ms"] * 1e-3) / 1e9
             m1[k] = {"GB/s": round(gbs, 1), "frac": round(gbs / peak_gbs, 4), "shapes": v["shapes"]}
-        out = {"M1_llama_3_2_1b_shapes_G128": m1, **self.extra_stats(peak_gbs),
+        out = {"M1_llama_3_2_1b_shapes_G128": m1, **self.extra_stats(peak_gbs, peak_tflops),
                "timing": "graph of back-to-back launches over rotating weight copies > 2x L2, CUDA events",
                "peak_gbs": peak_gbs}
         if sweep:
@@ -1124,7 +1129,7 @@ def run_decode(args, dist: Dist):
     gemv = None
     if dist.world == 1 and not args.no_gemv:
         gw = GemvWorkload(dev, seed=1234)
-        gemv = gw.summary(peak.peak_mem_bandwidth_gbs, sweep=not args.no_sweep)
+        gemv = gw.summary(peak.peak_mem_bandwidth_gbs, sweep=not args.no_sweep, peak_tflops=peak.peak_bf16_tflops)
         del gw
     if dist.rank != 0:
         wl.eng.close()
