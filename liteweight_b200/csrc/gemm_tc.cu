@@ -719,11 +719,24 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
   p.k_cache = static_cast<__half*>(a->k_cache);
   p.v_cache = static_cast<__half*>(a->v_cache);
 
-  // K slices per tile: while the tiles alone leave at least half the SMs idle
-  // and every slice keeps >= 8 blocks of 64
+  // K slices per tile. The cluster combine of the partial tiles grows with the
+  // rows: up to 64 rows, slices (up to 4) while the tiles alone leave at least
+  // half the SMs idle and every slice keeps >= 8 blocks of 64; past 64 rows, two
+  // slices for long rows (>= 128 blocks) only. Measured (INT4, 8B shapes, us):
+  // at 32 / 64 rows q|k|v 17.6 / 21.1 in 2 slices vs 29.7 / 31.0 whole; at 256
+  // rows q|k|v (48 tiles, 64 blocks) 30.0 whole vs 43.5 in 2 slices, o (32
+  // tiles) 29.6 vs 42.1 / 57.1 in 2 / 4, down (224 blocks) 76.2 vs 66.7 in 2.
   const int tiles = p.N / lw::kTcTileN;
   int splits = 1;
-  while (splits < lw::kTcMaxSplits && tiles * splits * 2 <= sm_count() && p.kblocks >= splits * 2 * 8) splits *= 2;
+  if (p.Mpad <= 64) {
+    while (splits < lw::kTcMaxSplits && tiles * splits * 2 <= sm_count() && p.kblocks >= splits * 2 * 8) splits *= 2;
+  } else if (p.kblocks >= 128 && tiles * 2 <= sm_count()) {
+    splits = 2;
+  }
+  if (const char* e = getenv("LW_B200_TC_SPLITS")) {   // a fixed split (1, 2 or 4), for measurements
+    const int v = atoi(e);
+    if ((v == 1 || v == 2 || v == 4) && p.kblocks >= v * 8) splits = v;
+  }
   p.splits = splits;
   p.kb_per = (p.kblocks + splits - 1) / splits;
 

@@ -63,8 +63,9 @@ def _close(got, ref):
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("M,N,K,G", [(1, 128, 64, 64), (5, 256, 256, 128), (16, 128, 512, 32), (37, 384, 192, 64),
                                      (128, 256, 1024, 128), (256, 128, 256, 256),
-                                     # K sliced over a cluster (2 or 4 CTAs per tile), ragged slices
-                                     (64, 512, 4096, 128), (200, 128, 2048, 64), (33, 256, 1088, 64)])
+                                     (64, 512, 4096, 128), (200, 128, 2048, 64), (33, 256, 1088, 64),
+                                     # long K (>= 128 blocks of 64): sliced over a 2-CTA cluster
+                                     (64, 128, 8192, 128)])
 @pytest.mark.parametrize("residual", [False, True])
 def test_gemm_residual(bits, M, N, K, G, residual):
     q, s, deq = _weights(bits, N, K, G, seed=M + N + K)
@@ -77,6 +78,24 @@ def test_gemm_residual(bits, M, N, K, G, residual):
     _run(bits=bits, epilogue=0, M=M, N=N, K=K, group_size=G, lda=K, ldo=N, act=act, weight=q, scales=s, out=out,
          residual=out if residual else None)
     _close(out, ref)
+
+
+@pytest.mark.parametrize("splits", [2, 4])
+@pytest.mark.parametrize("M,N,K,G", [(64, 512, 4096, 128), (200, 128, 2048, 64), (33, 256, 1088, 64)])
+def test_gemm_k_slices(M, N, K, G, splits, monkeypatch):
+    """K sliced over a cluster of 2 or 4 CTAs per tile (forced: the default
+    slices only rows of >= 128 blocks of 64), ragged slices, partial tiles
+    summed over distributed shared memory."""
+    monkeypatch.setenv("LW_B200_TC_SPLITS", str(splits))
+    for bits in (4, 8):
+        q, s, deq = _weights(bits, N, K, G, seed=M + N + K + splits)
+        gen = torch.Generator(device=DEV).manual_seed(M + splits)
+        act = torch.randn(M, K, generator=gen, device=DEV).half()
+        out = torch.randn(M, N, generator=gen, device=DEV).half()
+        ref = (out.float() + (act.float() @ deq.float().T).half().float()).half()
+        _run(bits=bits, epilogue=0, M=M, N=N, K=K, group_size=G, lda=K, ldo=N, act=act, weight=q, scales=s,
+             out=out, residual=out)
+        _close(out, ref)
 
 
 @pytest.mark.parametrize("bits", [4, 8])
