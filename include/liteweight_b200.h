@@ -37,7 +37,7 @@ typedef enum {
   LW_ERR_BAD_SHAPE = 2,      /* M, N or K <= 0, or K / N inconsistent with the format */
   LW_ERR_BAD_GROUP = 3,      /* group_size <= 0 or K % group_size != 0 */
   LW_ERR_ALIGNMENT = 4,      /* a pointer is not aligned to its element size */
-  LW_ERR_UNSUPPORTED = 5,    /* valid input this build does not handle */
+  LW_ERR_UNSUPPORTED = 5,    /* valid input the library does not handle */
   LW_ERR_LAUNCH = 6,         /* the CUDA launch failed (cudaGetLastError) */
   LW_ERR_WORKSPACE = 7,      /* workspace missing or too small */
   LW_ERR_TIMEOUT = 8         /* a bounded device-side wait gave up */
