@@ -331,11 +331,17 @@ int lw_prefill_sample(int* tokens, unsigned long long* keys, const void* embed, 
  *                      (seq NULL: decode rows, row m is sequence m at *pos)
  *   LW_TC_EPI_F32:    out is fp32 [M][ldo], out = y (a tensor-parallel rank's
  *                      partial sum of a row-split linear, to be all-reduced)
+ *   LW_TC_EPI_ARGMAX: out = fp16 logits; argmax_keys[m] = atomic max of
+ *                      (order key of the fp16 logit) << 32 | ~(n + argmax_offset)
+ *                      over the N rows (the keys lw_fused_gemv's argmax writes;
+ *                      zero before, as the sampler leaves them). The only
+ *                      epilogue that also takes fp16 weights (bits 16, scales NULL:
+ *                      the lm_head of a large decode batch)
  * Weights dequantize exactly (fp16(code * scale)) as the GEMV does; the sums
  * differ from it only in order. K a multiple of 64, INT4 or INT8, group size a
  * power of two >= 32 dividing K. No counterpart in the reference (its prompt
  * runs through one HF forward over QuantLinear's dequantize + matmul). */
-enum { LW_TC_EPI_RESID = 0, LW_TC_EPI_SWIGLU = 1, LW_TC_EPI_ROPE_KV = 2, LW_TC_EPI_F32 = 3 };
+enum { LW_TC_EPI_RESID = 0, LW_TC_EPI_SWIGLU = 1, LW_TC_EPI_ROPE_KV = 2, LW_TC_EPI_F32 = 3, LW_TC_EPI_ARGMAX = 4 };
 
 typedef struct {
   int bits, epilogue, pdl;
@@ -354,6 +360,8 @@ typedef struct {
   void* q_out;           /* fp16 [M][n_q_heads * head_dim] */
   void* k_cache;         /* fp16 [batch][n_kv_heads][max_seq][head_dim] */
   void* v_cache;
+  unsigned long long* argmax_keys;   /* LW_TC_EPI_ARGMAX: [M] */
+  int argmax_offset;                 /* LW_TC_EPI_ARGMAX: global index of weight row 0 */
 } lw_prefill_gemm_args;
 
 int lw_prefill_gemm(const lw_prefill_gemm_args* args, lw_stream_t stream);

@@ -86,6 +86,9 @@ struct TcGemmParams {
   __half* q_out;
   __half* k_cache;
   __half* v_cache;
+  // argmax (LW_TC_EPI_ARGMAX)
+  unsigned long long* keys;   // [M]: max over the rows n of (order key of fp16 y) << 32 | ~(n + argmax_offset)
+  int argmax_offset;
 };
 
 // ---- tcgen05 / mbarrier helpers (PTX ISA 8.7, sm_100a)
@@ -226,6 +229,21 @@ LW_DEV void tc_epilogue(const TcGemmParams& p, int n, int m, float y, int lane) 
     if (p.bias) y = r16(y + __half2float(p.bias[n]));
     if (p.residual) y = r16(__half2float(p.residual[(size_t)m * p.ldo + n]) + y);
     p.out[(size_t)m * p.ldo + n] = __float2half_rn(y);
+  } else if constexpr (EPI == LW_TC_EPI_ARGMAX) {
+    // logits and the first index of their maximum (the GEMV argmax's keys):
+    // the warp's 32 rows reduce to one key per row m, then one atomic
+    unsigned long long key = 0ull;
+    if (m < p.M && n < p.N) {
+      const __half h = __float2half_rn(y);
+      p.out[(size_t)m * p.ldo + n] = h;
+      key = ((unsigned long long)f16_order_key(h) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)(n + p.argmax_offset));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+      key = other > key ? other : key;
+    }
+    if (lane == 0 && key) atomicMax(p.keys + m, key);
   } else {
     // rows g and g + 8 of every 16-row tile are partners (gate/up, or the
     // rotate_half pair): the lower lane of each pair finishes both
@@ -328,7 +346,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       tma_prefetch_map(&p.tm_x);
     }
     const int first = min(S, nkb);
-    const int wx = BITS == 4 ? kTcKBlock / 2 : kTcKBlock;   // weight bytes per row per block
+    const int wx = kTcKBlock * BITS / 8;   // weight bytes per row per block
     for (int i = 0; i < first; ++i) {
       const uint32_t st = base + i * p.stage_bytes, bar = smem_u32(&bar_raw[i]);
       if (leader) {
@@ -398,12 +416,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const int dg = tid >> 7, ar = tid & 127;
     const int ngroups = p.K / p.G;
     const unsigned short* ssrc =
-        reinterpret_cast<const unsigned short*>(p.scales) + (size_t)min(n0 + ar, p.N - 1) * ngroups;
+        BITS < 16 ? reinterpret_cast<const unsigned short*>(p.scales) + (size_t)min(n0 + ar, p.N - 1) * ngroups
+                  : nullptr;
     auto scales_of = [&](int kb, unsigned short& s0, unsigned short& s1) {
-      s0 = __ldg(ssrc + min((kb * kTcKBlock) >> p.gshift, ngroups - 1));
-      s1 = __ldg(ssrc + min((kb * kTcKBlock + 32) >> p.gshift, ngroups - 1));
+      if constexpr (BITS < 16) {
+        s0 = __ldg(ssrc + min((kb * kTcKBlock) >> p.gshift, ngroups - 1));
+        s1 = __ldg(ssrc + min((kb * kTcKBlock + 32) >> p.gshift, ngroups - 1));
+      }
     };
-    const uint32_t raw_off = p.b_bytes + (uint32_t)ar * (BITS == 4 ? 32u : 64u);
+    const uint32_t raw_off = p.b_bytes + (uint32_t)ar * (uint32_t)(kTcKBlock * BITS / 8);
     // this warp's 32 lanes of tensor memory (a warp reaches lanes 32 (warp % 4) ..)
     const uint32_t a_taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)p.acc_cols;
     int i = dg, s = dg;   // block index within this CTA's K slice, its ring slot (S >= kTcDeqGroups)
@@ -417,7 +438,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       tc_fence_after();   // the MMAs that read this slot's A columns before have completed
       uint8_t* st = base_ptr + (size_t)s * p.stage_bytes;
       uint4 o[8];
-      if constexpr (BITS == 4) {
+      if constexpr (BITS == 16) {
+        // fp16 weights as they are: row ar's eight 16-byte chunks, stored
+        // 128-byte swizzled (chunk j of row r at j ^ (r % 8)) so that the 32
+        // rows of a warp spread over the banks
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = lds128(st + raw_off + (uint32_t)((j ^ (ar & 7)) << 4));
+      } else if constexpr (BITS == 4) {
         const uint4 q0 = lds128(st + raw_off), q1 = lds128(st + raw_off + 16);
         const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
@@ -665,11 +692,14 @@ int lw_tc_matmul(int bits, const void* act, const void* w, const void* scales, c
 extern "C" {
 namespace {
 int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t stream) {
-  if (!a || !a->act || !a->weight || !a->scales || !a->out) return LW_ERR_NULL_POINTER;
-  if (a->bits != 4 && a->bits != 8) return LW_ERR_UNSUPPORTED;
+  if (!a || !a->act || !a->weight || !a->out) return LW_ERR_NULL_POINTER;
+  if (a->bits != 4 && a->bits != 8 && a->bits != 16) return LW_ERR_UNSUPPORTED;
+  if (a->bits != 16 && !a->scales) return LW_ERR_NULL_POINTER;
+  if (a->bits == 16 && a->epilogue != LW_TC_EPI_ARGMAX) return LW_ERR_UNSUPPORTED;   // fp16 weights: the lm_head
   if (a->M <= 0 || a->M > lw::kTcMaxM || a->N <= 0 || a->N % lw::kTcTileN || a->K <= 0 || a->K % lw::kTcKBlock)
     return LW_ERR_BAD_SHAPE;
-  if (a->group_size < 32 || a->K % a->group_size || lw::group_shift(a->K, a->group_size) < 0) return LW_ERR_BAD_GROUP;
+  const int group = a->bits == 16 ? a->K : a->group_size;
+  if (group < 32 || a->K % group || lw::group_shift(a->K, group) < 0) return LW_ERR_BAD_GROUP;
   if (a->lda < a->K || a->lda % 8 || a->ldo % 8) return LW_ERR_BAD_SHAPE;
   if (!al(a->act, 16) || !al(a->weight, 16) || !al(a->out, 2)) return LW_ERR_ALIGNMENT;
   switch (a->epilogue) {
@@ -687,6 +717,10 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
         return LW_ERR_NULL_POINTER;
       if (a->head_dim % 16 || a->N != (a->n_q_heads + 2 * a->n_kv_heads) * a->head_dim) return LW_ERR_BAD_SHAPE;
       break;
+    case LW_TC_EPI_ARGMAX:
+      if (!a->argmax_keys) return LW_ERR_NULL_POINTER;
+      if (a->ldo < a->N || !al(a->argmax_keys, 8)) return LW_ERR_BAD_SHAPE;
+      break;
     default:
       return LW_ERR_UNSUPPORTED;
   }
@@ -700,8 +734,8 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
   p.Mpad = (a->M + 15) / 16 * 16;
   p.N = a->N;
   p.K = a->K;
-  p.G = a->group_size;
-  p.gshift = lw::group_shift(a->K, a->group_size);
+  p.G = group;
+  p.gshift = lw::group_shift(a->K, group);
   p.kblocks = a->K / lw::kTcKBlock;
   p.idesc = tc_idesc(p.Mpad);
   int acc = 32;
@@ -718,6 +752,8 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
   p.q_out = static_cast<__half*>(a->q_out);
   p.k_cache = static_cast<__half*>(a->k_cache);
   p.v_cache = static_cast<__half*>(a->v_cache);
+  p.keys = static_cast<unsigned long long*>(a->argmax_keys);
+  p.argmax_offset = a->argmax_offset;
 
   // K slices per tile. The cluster combine of the partial tiles grows with the
   // rows: up to 64 rows, slices (up to 4) while the tiles alone leave at least
@@ -740,7 +776,7 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
   p.splits = splits;
   p.kb_per = (p.kblocks + splits - 1) / splits;
 
-  const uint32_t wx = a->bits == 4 ? lw::kTcKBlock / 2 : lw::kTcKBlock;   // weight bytes per row per block
+  const uint32_t wx = (uint32_t)(lw::kTcKBlock * a->bits / 8);   // weight bytes per row per block
   p.w_bytes = wx * lw::kTcTileN;
   p.b_bytes = (uint32_t)p.Mpad * 128;
   p.stage_bytes = p.b_bytes + p.w_bytes;
@@ -754,8 +790,10 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
   const size_t smem = 1024 + (size_t)p.stages * p.stage_bytes;
 
   const size_t rowbytes = (size_t)a->K * a->bits / 8;
+  // fp16 rows (128 bytes per block) land 128-byte swizzled: the reading
+  // threads (one row each) then spread over the banks
   if (!encode_2d(&p.tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a->weight, rowbytes, (uint64_t)a->N, rowbytes, wx,
-                 lw::kTcTileN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+                 lw::kTcTileN, a->bits == 16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !encode_2d(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->act, (uint64_t)a->K, (uint64_t)a->M,
                  (uint64_t)a->lda * 2, lw::kTcKBlock, (uint32_t)p.Mpad, CU_TENSOR_MAP_SWIZZLE_128B))
     return LW_ERR_LAUNCH;
@@ -773,6 +811,9 @@ int prefill_gemm(const lw_prefill_gemm_args* a, const void* bias, lw_stream_t st
   LW_TC(8, LW_TC_EPI_ROPE_KV)
   LW_TC(4, LW_TC_EPI_F32)
   LW_TC(8, LW_TC_EPI_F32)
+  LW_TC(16, LW_TC_EPI_ARGMAX)
+  LW_TC(4, LW_TC_EPI_ARGMAX)
+  LW_TC(8, LW_TC_EPI_ARGMAX)
 #undef LW_TC
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? LW_OK : LW_ERR_LAUNCH;

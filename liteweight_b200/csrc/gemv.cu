@@ -410,7 +410,7 @@ const char* lw_status_string(int status) {
   }
 }
 
-int lw_abi_version(void) { return 112; }
+int lw_abi_version(void) { return 113; }
 
 int lw_take_device_error(void) {
   const int mine = lw_tu_take_error();

@@ -89,10 +89,11 @@ class PrefillGemmArgs(ctypes.Structure):
         ("head_dim", c_int), ("n_q_heads", c_int), ("n_kv_heads", c_int), ("max_seq", c_int),
         ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("pos", c_void_p), ("seq", c_void_p),
         ("q_out", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
+        ("argmax_keys", c_void_p), ("argmax_offset", c_int),
     ]
 
 
-TC_EPI_RESID, TC_EPI_SWIGLU, TC_EPI_ROPE_KV, TC_EPI_F32 = 0, 1, 2, 3
+TC_EPI_RESID, TC_EPI_SWIGLU, TC_EPI_ROPE_KV, TC_EPI_F32, TC_EPI_ARGMAX = 0, 1, 2, 3, 4
 TC_ROWS = 256   # prompt-chunk rows on the tensor-core path (the GEMM's largest M)
 
 
@@ -665,10 +666,12 @@ class DecodeEngine:
         bufs.sample_xin = None
         calls = [] if decode else [("prefill_embed", bufs, "embed")]
 
-        def tc(epi, N, K, w, s_, act, lda, out, ldo, name="tc", **kw):
-            a = PrefillGemmArgs(bits=sp.bits, epilogue=epi, pdl=self.pdl, M=rows, N=N, K=K,
-                                group_size=sp.group_size, lda=lda, ldo=ldo, act=act.data_ptr(), weight=w.data_ptr(),
-                                scales=s_.data_ptr(), out=out.data_ptr() if out is not None else None)
+        def tc(epi, N, K, w, s_, act, lda, out, ldo, name="tc", bits=None, group_size=None, **kw):
+            a = PrefillGemmArgs(bits=sp.bits if bits is None else bits, epilogue=epi, pdl=self.pdl, M=rows, N=N,
+                                K=K, group_size=sp.group_size if group_size is None else group_size, lda=lda,
+                                ldo=ldo, act=act.data_ptr(), weight=w.data_ptr(),
+                                scales=s_.data_ptr() if s_ is not None else None,
+                                out=out.data_ptr() if out is not None else None)
             for k, v in kw.items():
                 setattr(a, k, v.data_ptr() if isinstance(v, torch.Tensor) else v)
             return ("tcgemm", a, name)
@@ -704,6 +707,19 @@ class DecodeEngine:
             return calls, []
         if tp:   # the last down partial joins the residual stream (h is not used)
             calls.append(norm(self.final_norm, True))
+        if decode and self.vshard % 128 == 0 and (self.lm_bits == 16 or self.lm_group >= 32):
+            # every row's logits and argmax key on the tensor cores: the head's
+            # weights are read once for the whole batch
+            if not tp:
+                calls.append(norm(self.final_norm, False))
+            calls.append(tc(TC_EPI_ARGMAX, self.vshard, H, self.lm_head, self.lm_scales, bufs.h, H, bufs.logits,
+                            self.vshard, name="lm_head", bits=self.lm_bits,
+                            group_size=H if self.lm_bits == 16 else self.lm_group, argmax_keys=bufs.keys,
+                            argmax_offset=self.tp_rank * self.vshard))
+            if tp:
+                calls.append(("allreduce_max", bufs.keys, "allreduce"))
+            calls.append(("sample", bufs, "sample"))
+            return calls, []
         if decode:
             # every row's logits and argmax key, in row blocks of what one GEMV launch stages
             fit = min(32, max(1, _stage_rows(H, self.lm_bits, True)))

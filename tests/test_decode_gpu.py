@@ -138,18 +138,20 @@ def test_random_model_vs_oracle(bits, batch, hd, heads, kv, fold):
 
 
 @pytest.mark.parametrize("tc", [True, False])
-@pytest.mark.parametrize("bits,kv", [(4, 2), (8, 2), (4, 8)])
-def test_large_batch_vs_oracle(bits, kv, tc, monkeypatch):
+@pytest.mark.parametrize("bits,kv,vocab", [(4, 2, 1000), (8, 2, 1000), (4, 8, 1000), (4, 2, 1024)])
+def test_large_batch_vs_oracle(bits, kv, vocab, tc, monkeypatch):
     """Batch 40: the step's linears on the tensor-core GEMM with decode rows
     (row m = sequence m at *pos), or - with the tensor-core decode switched off
-    - every GEMV as row blocks (32 + 8 sequences); the lm_head GEMV in row
-    blocks either way. 40 x 2 kv heads run the attention in 2-CTA clusters,
-    40 x 8 in single CTAs. Teacher-forced logits against the oracle."""
+    - every GEMV as row blocks (32 + 8 sequences). The lm_head runs on the
+    tensor cores (argmax epilogue) when the vocabulary is whole 128-row tiles
+    (1024), else as GEMV row blocks (1000). 40 x 2 kv heads run the attention
+    in 2-CTA clusters, 40 x 8 in single CTAs. Teacher-forced logits against
+    the oracle."""
     from liteweight_b200 import engine as E
     monkeypatch.setenv("LW_B200_TC_DECODE_MIN", "24" if tc else "0")
-    w = random_model(512, 1536, 3, 8, kv, 64, 1000, bits, seed=bits * 10 + 40 + kv)
+    w = random_model(512, 1536, 3, 8, kv, 64, vocab, bits, seed=bits * 10 + 40 + kv)
     P, T, B = 5, 7, 40
-    prompt = np.random.default_rng(40).integers(0, 1000, (B, P))
+    prompt = np.random.default_rng(40).integers(0, vocab, (B, P))
     eng = engine_from_oracle(w, bits, 128, batch=B, max_seq=48)
     assert eng.tc_decode == tc and E.tc_supported(eng.spec)
     got = run_engine(eng, prompt, P + T - 1)

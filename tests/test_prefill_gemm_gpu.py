@@ -98,6 +98,31 @@ def test_gemm_k_slices(M, N, K, G, splits, monkeypatch):
         _close(out, ref)
 
 
+@pytest.mark.parametrize("bits", [16, 4])
+@pytest.mark.parametrize("M", [1, 40, 64])
+def test_gemm_argmax(bits, M):
+    """LW_TC_EPI_ARGMAX (the lm_head of a large decode batch): fp16 logits
+    within the row tolerance of an fp32 reference, and per row the key of the
+    first maximum of those logits - the key lw_fused_gemv's argmax writes
+    ((order key of the fp16 value) << 32 | ~(index + offset))."""
+    N, K, G, offset = 1024, 512, 128, 3000
+    gen = torch.Generator(device=DEV).manual_seed(M + bits)
+    act = torch.randn(M, K, generator=gen, device=DEV).half()
+    if bits == 16:
+        w = (torch.randn(N, K, generator=gen, device=DEV) * 0.05).half()
+        q, s, deq = w, None, w
+    else:
+        q, s, deq = _weights(bits, N, K, G, seed=M)
+    out = torch.zeros(M, N, device=DEV).half()
+    keys = torch.zeros(M, dtype=torch.int64, device=DEV)
+    _run(bits=bits, epilogue=4, M=M, N=N, K=K, group_size=G, lda=K, ldo=N, act=act, weight=q, scales=s, out=out,
+         argmax_keys=keys, argmax_offset=offset)
+    _close(out, (act.float() @ deq.float().T).half())
+    idx = out.float().argmax(dim=1)          # the first maximum of the kernel's own fp16 logits
+    got = (0xFFFFFFFF - (keys & 0xFFFFFFFF)) - offset
+    assert torch.equal(got.cpu(), idx.cpu())
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("M", [3, 64, 200])
 @pytest.mark.parametrize("K", [512, 2048])
