@@ -197,7 +197,7 @@ def _gpu_model(world):
     return _GPU_MODEL_8 if world > 4 else _GPU_MODEL
 
 
-def _nccl_worker(rank, world, port, out_path, exchange):
+def _nccl_worker(rank, world, port, out_path, exchange, batch=2):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -209,10 +209,10 @@ def _nccl_worker(rank, world, port, out_path, exchange):
     t1 = torch.zeros(1, device=dev)
     dist.all_reduce(t1)          # communicator up before graph capture
     eng = E.build_engine(_spec(w, 4), _layer_weights(w, to), to(w.embed), to(w.norm), None,
-                         torch.from_numpy(w.inv_freq), 2, 64, dev, tp_rank=rank, tp_size=world,
+                         torch.from_numpy(w.inv_freq), batch, 64, dev, tp_rank=rank, tp_size=world,
                          tp_group=dist.group.WORLD, exchange=exchange, tune_kernels=False)
     P, T = 6, 5
-    prompt = np.random.default_rng(3).integers(0, w.shape.vocab, (2, P))
+    prompt = np.random.default_rng(3).integers(0, w.shape.vocab, (batch, P))
     shards = []
     for rep in range(2):         # a second generation reuses the graph; the step count keeps growing
         eng.start(torch.from_numpy(prompt))
@@ -236,7 +236,7 @@ def _nccl_worker(rank, world, port, out_path, exchange):
     chunked = eng.generate(torch.from_numpy(prompt), T).numpy()
     if rank == 0:
         np.savez(out_path, logits=np.stack(shards), tokens=gen, prompt=prompt, chunked=chunked,
-                 same=all(bool(torch.equal(g, gens[0])) for g in gens))
+                 same=all(bool(torch.equal(g, gens[0])) for g in gens), tc_decode=eng.tc_decode)
     eng.close()                  # collective; releases the graph (NCCL calls in the "nccl" mode)
     del eng
     gc.collect()
@@ -244,12 +244,12 @@ def _nccl_worker(rank, world, port, out_path, exchange):
     dist.destroy_process_group()
 
 
-def _run_tp(exchange, world):
+def _run_tp(exchange, world, batch=2):
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
         out = os.path.join(d, "tp.npz")
-        mp.start_processes(_nccl_worker, args=(world, port, out, exchange), nprocs=world, start_method="spawn",
-                           join=True)
+        mp.start_processes(_nccl_worker, args=(world, port, out, exchange, batch), nprocs=world,
+                           start_method="spawn", join=True)
         return dict(np.load(out))
 
 
@@ -277,3 +277,22 @@ def test_tp_decode_matches_oracle(world):
         o = ref.reshape(-1, ref.shape[-1]).astype(np.float64)
         tol = oq.row_tolerance(o)
         assert np.all(np.abs(g - o) <= tol), float((np.abs(g - o) / tol).max())
+
+
+@pytest.mark.gpu
+def test_tp_large_batch_on_tensor_cores():
+    """Batch 24 at two ranks: the decode step's linears and the lm_head on the
+    tcgen05 GEMM (decode rows, argmax epilogue), the o/down partials and the
+    argmax keys all-reduced by NCCL in the step graph; every rank picks the same
+    tokens and the logits are within the row tolerance of the unsharded oracle."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    r = _run_tp("peer", 2, batch=24)
+    assert bool(r["tc_decode"]) and bool(r["same"])
+    assert (r["chunked"] == r["tokens"]).mean() >= 0.8
+    w = random_model(**_gpu_model(2))
+    ref = ol.teacher_forced_logits(w, r["prompt"], r["tokens"])
+    g = r["logits"].reshape(-1, ref.shape[-1]).astype(np.float64)
+    o = ref.reshape(-1, ref.shape[-1]).astype(np.float64)
+    tol = oq.row_tolerance(o)
+    assert np.all(np.abs(g - o) <= tol), float((np.abs(g - o) / tol).max())
