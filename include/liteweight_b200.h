@@ -207,6 +207,10 @@ typedef struct {
   const int* step;
   int* error;           /* device: set to LW_ERR_TIMEOUT when a wait gives up (may be NULL) */
   long long timeout_ns; /* wait limit */
+  int* slice_flags;     /* NULL: every CTA of the consuming GEMV sums every rank's partials for the
+                           whole K. Else (>= 1024 local ints, zero before first use): CTA b sums
+                           slice b of K, writes it to x_out and sets slice_flags[b] to the exchange's
+                           flag; every CTA then reads the whole new residual from x_out. Same bits. */
 } lw_exchange_in;
 
 typedef struct {

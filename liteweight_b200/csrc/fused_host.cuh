@@ -46,6 +46,7 @@ inline StreamParams to_stream(const lw_fused_gemv_args* a) {
     p.in_step = a->xin->step;
     p.in_error = a->xin->error;
     p.in_timeout_ns = a->xin->timeout_ns;
+    p.in_slice_flags = a->xin->slice_flags;
   }
   if ((a->epilogue == LW_EPI_PEER_F32 || a->epilogue == LW_EPI_PEER_ARGMAX) && a->xout) {
     p.out_world = a->xout->world;

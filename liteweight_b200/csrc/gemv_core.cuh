@@ -116,6 +116,7 @@ struct StreamParams {
   const int* in_step;                  // decode steps completed
   int* in_error;
   long long in_timeout_ns;
+  int* in_slice_flags;                 // non-null: the CTAs reduce slices of K (see stage_activation)
   // tensor-parallel exchange, producer (EPI_PEER_*)
   int out_world, out_rank, out_tag, out_tags;
   const int* out_step;
@@ -401,9 +402,73 @@ LW_DEV void stage_activation(const StreamParams& p, __half* act_s, const __half*
       sq = fmaf(f, f, sq);
     }
   };
+  // Cooperative exchange (in_slice_flags): CTA b sums slice b of K (groups of
+  // 8 elements) over the ranks - one (group, rank) word block per thread, then
+  // the same rank-order sums as below - writes the new residual slice to x_out
+  // and flags it; every CTA then reads the whole new residual back from x_out.
+  // The same values, in the same order, as each CTA summing everything itself.
+  bool coop = false;
+  if constexpr (PRO == PRO_PEER_RESID_NORM) {
+    const int G8 = (p.K + 7) / 8;
+    const int per = (G8 + (int)gridDim.x - 1) / (int)gridDim.x;
+    // (the scratch, M x per x world x 32 bytes, must fit the staged activation, M x cp x 2)
+    coop = p.in_slice_flags != nullptr && gridDim.x <= kSliceFlagsMax && per * p.in_world * 16 <= p.cp;
+    if (coop) {
+      const int ga = (int)blockIdx.x * per, ng = max(0, min(G8, ga + per) - ga);
+      const int W = p.in_world;
+      const size_t rstride = (size_t)p.M * p.K;
+      float* part = reinterpret_cast<float*>(act_s);   // scratch until the staging below: [M][ng][W][8]
+      for (int t = tid; t < p.M * ng * W; t += NT) {
+        const int m = t / (ng * W), rem = t - m * ng * W, gi = rem / W, r = rem - gi * W;
+        float ps[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+        add_flagged8<1>(p.in_src + r * rstride + (size_t)m * p.K + (size_t)(ga + gi) * 8, rstride, 1, in_flag, ps,
+                        wb, p.in_timeout_ns, p.in_error);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part[(size_t)t * 8 + e] = ps[e];
+      }
+      stage_sync<BAR, NT>();
+      for (int t = tid; t < p.M * ng; t += NT) {
+        const int m = t / ng, gi = t - m * ng, k = (ga + gi) * 8;
+        float ps[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+        for (int r = 0; r < W; ++r)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ps[e] += part[((size_t)t * W + r) * 8 + e];
+        uint4 v = ldg_nc(p.act + (size_t)m * p.lda + k);
+        __half* hv = reinterpret_cast<__half*>(&v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(__half2float(hv[e]) + r16(ps[e]));
+        *reinterpret_cast<uint4*>(p.x_out + (size_t)m * p.lda + k) = v;
+      }
+      stage_sync<BAR, NT>();
+      if (tid == 0) {
+        __threadfence();   // the slice is visible before its flag
+        st_volatile_u32(reinterpret_cast<unsigned int*>(p.in_slice_flags) + blockIdx.x, in_flag);
+      }
+      for (int c = tid; c < (int)gridDim.x; c += NT) {
+        while (ld_volatile_u32(reinterpret_cast<const unsigned int*>(p.in_slice_flags) + c) != in_flag)
+          if (!wb.keep_waiting(p.in_timeout_ns, p.in_error)) break;
+      }
+      __threadfence();
+      stage_sync<BAR, NT>();
+    }
+  }
   for (int m = 0; m < p.M; ++m) {
     float sq = 0.f;
-    if constexpr (PRO == PRO_PEER_RESID_NORM) {
+    if (coop) {
+      for (int i = tid; i < groups8; i += NT) {
+        const int k = i * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (k < p.K) {
+          v = __ldcg(reinterpret_cast<const uint4*>(p.x_out + (size_t)m * p.lda + k));
+          square_sum(v, sq);
+        }
+        store(m, k, v);
+      }
+    } else if constexpr (PRO == PRO_PEER_RESID_NORM) {
       for (int i = tid; i < groups8; i += NT) {
         const int k = i * 8;
         uint4 v = make_uint4(0, 0, 0, 0);

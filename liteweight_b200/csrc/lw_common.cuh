@@ -87,6 +87,18 @@ LW_DEV unsigned long long ld_volatile_u64(const void* p) {
   return v;
 }
 
+// 4-byte flag words shared by the CTAs of one GPU.
+LW_DEV unsigned int ld_volatile_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+LW_DEV void st_volatile_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Slice flags of a cooperatively reduced exchange: one per CTA of the consumer.
+constexpr int kSliceFlagsMax = 1024;
+
 LW_DEV unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

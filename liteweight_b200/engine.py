@@ -53,7 +53,10 @@ class ExchangeOut(ctypes.Structure):
 class ExchangeIn(ctypes.Structure):
     """Mirror of lw_exchange_in (include/liteweight_b200.h)."""
     _fields_ = [("world", c_int), ("tag", c_int), ("tags_per_step", c_int), ("src", c_void_p), ("step", c_void_p),
-                ("error", c_void_p), ("timeout_ns", ctypes.c_longlong)]
+                ("error", c_void_p), ("timeout_ns", ctypes.c_longlong), ("slice_flags", c_void_p)]
+
+
+SLICE_FLAGS = 1024   # per slot set: one flag per CTA of a cooperatively reducing GEMV (kSliceFlagsMax)
 
 
 def exchange_flag(step: int, tag: int, tags_per_step: int) -> int:
@@ -376,6 +379,13 @@ class PeerExchange:
         self.step = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.error = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.arrivals = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # LW_B200_EXCHANGE_SPLIT=1: the consuming GEMV reduces the partials
+        # cooperatively (each CTA one slice of K, a flag per CTA, one flag array
+        # per slot set) instead of every CTA reading every rank's partials for
+        # the whole K. Same bits; measured slower at two ranks (569.5 vs 721.4
+        # tokens/s: each CTA then waits for the grid's last one), so off by default.
+        self.split = os.environ.get("LW_B200_EXCHANGE_SPLIT") == "1"
+        self.slice_flags = torch.zeros(2 * SLICE_FLAGS, dtype=torch.int32, device=self.device)
         self.outs, self.ins = [], []
         for e in range(self.tags):
             out = ExchangeOut(world=world, rank=rank, step=self.step.data_ptr(), tag=e, tags_per_step=self.tags,
@@ -383,9 +393,12 @@ class PeerExchange:
             for d in range(world):
                 out.dst[d] = self.peers[d] + self._recv_offset(e)   # the kernel adds rank * rows
             self.outs.append(out)
+            flags = (self.slice_flags.data_ptr() + 4 * SLICE_FLAGS * (e % 2)
+                     if self.split and e < n_partial else None)
             self.ins.append(ExchangeIn(world=world, tag=e, tags_per_step=self.tags,
                                        src=self.base + self._recv_offset(e), step=self.step.data_ptr(),
-                                       error=self.error.data_ptr(), timeout_ns=int(timeout_s * 1e9)))
+                                       error=self.error.data_ptr(), timeout_ns=int(timeout_s * 1e9),
+                                       slice_flags=flags))
         self.closed = False
 
     def _recv_offset(self, e: int) -> int:

@@ -14,7 +14,7 @@ def test_struct_layout_matches_library():
     lwbuild.build()
     E.check_abi()
     assert ctypes.sizeof(E.FusedGemvArgs) == 256 and ctypes.sizeof(E.AttentionArgs) == 72
-    assert ctypes.sizeof(E.ExchangeOut) == 96 and ctypes.sizeof(E.ExchangeIn) == 48
+    assert ctypes.sizeof(E.ExchangeOut) == 96 and ctypes.sizeof(E.ExchangeIn) == 56
 
 
 @pytest.mark.parametrize("hd", [64, 128])
