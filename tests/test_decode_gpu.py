@@ -257,6 +257,31 @@ def test_chunked_prefill(bits, batch, P, down_block, path, monkeypatch):
     assert (oracle.argmax(-1) == got.T).mean() >= 0.9
 
 
+@pytest.mark.parametrize("path,R,chunks,bits", [("gemv", 4, 5, 4), ("tc", 4, 5, 8), ("tc", 64, 2, 4),
+                                                ("tc", 128, 2, 8)])
+def test_prefill_final_logits_vs_oracle(path, R, chunks, bits):
+    """The logits the prompt pass computes at the prompt's last position (the
+    ones that pick the first new token) against the oracle's, within the row
+    tolerance, for chunks of 4 rows and for 64- and 128-row chunks on the
+    tcgen05 GEMM (the prompt pass of generate() and of the bench)."""
+    w = random_model(512, 1024, 2, 8, 2, 64, 1000, bits, seed=31 + R + bits)
+    P = R * chunks   # whole chunks: the last one is the engine's own chunk buffers
+    prompt = np.random.default_rng(R).integers(0, 1000, (1, P))
+    eng = engine_from_oracle(w, bits, 128, batch=1, max_seq=P + 8)
+    eng.use_tc = path == "tc"
+    eng.prefill_rows = R
+    eng.pf = eng._buffers(R)
+    eng.start(torch.from_numpy(prompt))
+    eng.prefill()
+    torch.cuda.synchronize()
+    eng.check()
+    got = eng.pf.logits[R - 1].float().cpu().numpy()[None]
+    first = eng.tokens[P].item()
+    ref = ol.teacher_forced_logits(w, prompt, np.array([[first]]))[0]
+    assert_rows(got, ref, f"prefill {path} rows {R} int{bits}")
+    assert first == int(ref[0].argmax()) or ref[0][first] >= ref[0].max() - oq.row_tolerance(ref)[0, 0]
+
+
 @pytest.mark.parametrize("head_bits,bits", [(4, 4), (8, 4), (8, 8)])
 def test_quantized_lm_head_vs_oracle(head_bits, bits):
     """The lm_head quantized like swap_linears does when it is not skipped:
